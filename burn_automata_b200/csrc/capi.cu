@@ -1,0 +1,1160 @@
+// capi.cu -- the extern "C" boundary (include/npa_b200.h).
+//
+// Validation mirrors the reference's checks and their order:
+//   HashGridConfig::validate       crates/burn_automata_kernels/src/config.rs:65-84
+//   check_shapes                   crates/burn_automata_kernels/src/reference/shape.rs:3-25
+//   euler_step shape checks        crates/burn_automata_kernels/src/reference/step.rs:16-27
+//   NpaModel::validate / weights   crates/burn_automata/src/model.rs:77-107, :757-766
+//   step_cpu grid/model dim check  crates/burn_automata/src/model.rs:778-784
+// Everything is checked before the first CUDA call, so a bad argument is
+// reported the same way with or without a GPU.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "npa_internal.h"
+
+namespace npa {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+npa_status fail(npa_status st, const std::string& msg) {
+  set_error(msg);
+  return st;
+}
+
+npa_status cuda_fail(cudaError_t err, const char* what) {
+  set_error(std::string(what) + ": " + cudaGetErrorString(err));
+  if (err == cudaErrorMemoryAllocation) return NPA_ERR_OUT_OF_MEMORY;
+  if (err == cudaErrorNoDevice || err == cudaErrorInsufficientDriver) return NPA_ERR_NO_DEVICE;
+  return NPA_ERR_CUDA;
+}
+
+npa_status after_launch(const char* kernel, int launches) {
+  g_launches.fetch_add(static_cast<uint64_t>(launches), std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, kernel);
+  return NPA_OK;
+}
+
+static float powi_f32(float x, int n) {
+  float result = 1.0f;
+  bool have = false;
+  float square = x;
+  while (n) {
+    if (n & 1) {
+      result = have ? result * square : square;
+      have = true;
+    }
+    n >>= 1;
+    if (n) square = square * square;
+  }
+  return have ? result : 1.0f;
+}
+
+npa_status validate_grid(const npa_grid_config* cfg) {
+  if (!cfg) return fail(NPA_ERR_INVALID_ARGUMENT, "grid config is null");
+  if (!(cfg->dim == 2 || cfg->dim == 3))
+    return fail(NPA_ERR_INVALID_DIM, "expected spatial dim 2 or 3, got " + std::to_string(cfg->dim));
+  if (!std::isfinite(cfg->eps) || cfg->eps <= 0.0f)
+    return fail(NPA_ERR_INVALID_EPS, "eps must be finite and positive");
+  if (!(cfg->mode == NPA_MODE_GRID || cfg->mode == NPA_MODE_PARTICLE))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "unknown hashgrid mode");
+  if (!(cfg->boundary == NPA_BOUNDARY_PERIODIC || cfg->boundary == NPA_BOUNDARY_CLAMPED))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "unknown boundary");
+  for (int axis = 0; axis < cfg->dim; ++axis) {
+    const int64_t s = cfg->grid_size[axis];
+    if (s <= 0) return fail(NPA_ERR_INVALID_GRID_SIZE, "grid sizes must be non-zero for active dimensions");
+    if (cfg->mode == NPA_MODE_PARTICLE && (s & (s - 1)) != 0)
+      return fail(NPA_ERR_PARTICLE_MODE_REQUIRES_POW2,
+                  "particle hashgrid mode requires power-of-two grid size at axis " +
+                      std::to_string(axis) + ", got " + std::to_string(s));
+  }
+  int64_t cells = 1;
+  for (int axis = 0; axis < cfg->dim; ++axis) {
+    if (cfg->grid_size[axis] > (int64_t(1) << 30))
+      return fail(NPA_ERR_UNSUPPORTED, "grid size above 2^30 on one axis");
+    cells *= cfg->grid_size[axis];
+    if (cells > (int64_t(1) << 31)) return fail(NPA_ERR_UNSUPPORTED, "cell count above 2^31");
+  }
+  return NPA_OK;
+}
+
+GridParams make_grid_params(const npa_grid_config& cfg) {
+  GridParams g{};
+  g.dim = cfg.dim;
+  g.boundary = cfg.boundary;
+  g.mode = cfg.mode;
+  uint64_t cells = 1;
+  for (int a = 0; a < 3; ++a) {
+    g.grid_size[a] = a < cfg.dim ? static_cast<int>(cfg.grid_size[a]) : 1;
+    if (a < cfg.dim) cells *= static_cast<uint64_t>(cfg.grid_size[a]);
+  }
+  g.cells = static_cast<uint32_t>(cells);
+  g.eps = cfg.eps;
+  g.eps2 = cfg.eps * cfg.eps;
+  for (int a = 0; a < 3; ++a) {
+    // `grid_size as f32 * eps` (hashgrid.rs:170) == `eps * size as f32` (:80).
+    g.extent[a] = static_cast<float>(a < cfg.dim ? cfg.grid_size[a] : 1) * cfg.eps;
+    g.half[a] = g.extent[a] * 0.5f;
+  }
+  const float pi = 3.14159274101257324219f;  // std::f32::consts::PI
+  if (cfg.dim == 2) {
+    g.poly6_norm = 4.0f / (pi * powi_f32(cfg.eps, 8));
+    g.spiky_norm = 10.0f / (pi * powi_f32(cfg.eps, 5));
+  } else {
+    g.poly6_norm = 315.0f / (64.0f * pi * powi_f32(cfg.eps, 9));
+    g.spiky_norm = 15.0f / (pi * powi_f32(cfg.eps, 6));
+  }
+  return g;
+}
+
+}  // namespace npa
+
+using namespace npa;
+
+// ---------------------------------------------------------------------------
+// small host helpers
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr uint64_t kMaxParticles = (uint64_t(1) << 31);
+
+npa_status check_counts(int64_t batch, int64_t n) {
+  if (batch < 0 || n < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "batch and particle count must be >= 0");
+  if (batch > 0 && uint64_t(n) > kMaxParticles / uint64_t(batch))
+    return fail(NPA_ERR_UNSUPPORTED, "batch * particle_count above 2^31");
+  return NPA_OK;
+}
+
+npa_status check_bins(const npa_grid_config* cfg, int64_t batch) {
+  int64_t cells = 1;
+  for (int a = 0; a < cfg->dim; ++a) cells *= cfg->grid_size[a];
+  if (batch > 0 && uint64_t(cells) > (uint64_t(0xFFFFFFFEu) / uint64_t(batch)))
+    return fail(NPA_ERR_UNSUPPORTED, "batch * cell_count + 1 does not fit in uint32");
+  return NPA_OK;
+}
+
+// check_shapes (shape.rs:3-25).
+npa_status check_shapes(int64_t positions_len, int64_t states_len, int64_t batch, int64_t n,
+                        int64_t c) {
+  const int64_t expected = batch * n;
+  if (positions_len != expected)
+    return fail(NPA_ERR_POSITION_SHAPE, "positions length " + std::to_string(positions_len) +
+                                            " does not match batch_size * particle_count " +
+                                            std::to_string(expected));
+  if (states_len != expected * c)
+    return fail(NPA_ERR_STATE_SHAPE, "state length " + std::to_string(states_len) +
+                                         " does not match batch_size * particle_count * state_dims " +
+                                         std::to_string(expected * c));
+  return NPA_OK;
+}
+
+npa_status output_shape(int64_t actual, int64_t expected) {
+  if (actual != expected)
+    return fail(NPA_ERR_OUTPUT_SHAPE, "output buffer length " + std::to_string(actual) +
+                                          " does not match expected " + std::to_string(expected));
+  return NPA_OK;
+}
+
+npa_status ensure_device(int device) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(NPA_ERR_NO_DEVICE, std::string("no CUDA device: ") +
+                                       (e != cudaSuccess ? cudaGetErrorString(e) : "count is 0"));
+  }
+  if (device < 0 || device >= count) return fail(NPA_ERR_INVALID_ARGUMENT, "device ordinal out of range");
+  NPA_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  return NPA_OK;
+}
+
+npa_status current_device(int* device) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(NPA_ERR_NO_DEVICE, "no CUDA device");
+  }
+  NPA_CUDA(cudaGetDevice(device), "cudaGetDevice");
+  return NPA_OK;
+}
+
+// Optional test hook: total bytes the host-buffer entry points may allocate
+// per call (0 = unlimited).  Exercises the out-of-memory path without
+// exhausting a device.
+std::atomic<uint64_t> g_alloc_cap{0};
+
+// Device scratch of one host-buffer call, freed on scope exit.
+struct Scratch {
+  std::vector<void*> ptrs;
+  uint64_t bytes = 0;
+  cudaStream_t stream = nullptr;
+  ~Scratch() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : ptrs) cudaFree(p);
+    if (stream) cudaStreamDestroy(stream);
+  }
+  npa_status init() {
+    NPA_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    return NPA_OK;
+  }
+  template <class T>
+  npa_status alloc(T** out, size_t count) {
+    *out = nullptr;
+    const size_t b = std::max<size_t>(count * sizeof(T), 256);
+    const uint64_t cap = g_alloc_cap.load();
+    if (cap && bytes + b > cap) return fail(NPA_ERR_OUT_OF_MEMORY, "allocation cap reached");
+    void* p = nullptr;
+    NPA_CUDA(cudaMalloc(&p, b), "cudaMalloc");
+    ptrs.push_back(p);
+    bytes += b;
+    *out = static_cast<T*>(p);
+    return NPA_OK;
+  }
+  template <class T>
+  npa_status upload(T** out, const void* host, size_t count) {
+    NPA_TRY(alloc(out, count));
+    if (count)
+      NPA_CUDA(cudaMemcpyAsync(*out, host, count * sizeof(T), cudaMemcpyHostToDevice, stream),
+               "cudaMemcpyAsync H2D");
+    return NPA_OK;
+  }
+  npa_status download(void* host, const void* dev, size_t bytes_) {
+    if (bytes_ && host)
+      NPA_CUDA(cudaMemcpyAsync(host, dev, bytes_, cudaMemcpyDeviceToHost, stream),
+               "cudaMemcpyAsync D2H");
+    return NPA_OK;
+  }
+  npa_status finish() {
+    NPA_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+    return NPA_OK;
+  }
+};
+
+// Layout of the workspace behind the device perception / step entry points.
+struct PerceiveWorkspace {
+  HashgridBuffers hg;
+  float* volume;
+  void* sort_scratch;
+  size_t sort_scratch_bytes;
+};
+
+size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n) {
+  const size_t total = size_t(batch) * n;
+  Carve c(nullptr, 0);
+  c.take<uint32_t>(size_t(batch) * g.cells + 1);
+  c.take<uint32_t>(total);
+  c.take<uint32_t>(total);
+  c.take<float4>(total);
+  c.take<int4>(total);
+  c.take<float>(total);
+  const size_t sort = hashgrid_scratch_bytes(g, batch, n);
+  c.take<char>(sort);
+  return c.used + 256;
+}
+
+bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, size_t bytes,
+                    PerceiveWorkspace* out) {
+  const size_t total = size_t(batch) * n;
+  Carve c(ws, bytes);
+  out->hg.bin_offsets = c.take<uint32_t>(size_t(batch) * g.cells + 1);
+  out->hg.permutation = c.take<uint32_t>(total);
+  out->hg.inverse = c.take<uint32_t>(total);
+  out->hg.spos = c.take<float4>(total);
+  out->hg.scoord = c.take<int4>(total);
+  out->volume = c.take<float>(total);
+  out->sort_scratch_bytes = hashgrid_scratch_bytes(g, batch, n);
+  out->sort_scratch = c.take<char>(out->sort_scratch_bytes);
+  return c.fits();
+}
+
+SortedGrid sorted_view(const PerceiveWorkspace& w, uint32_t n, uint32_t batch) {
+  SortedGrid s;
+  s.bin_offsets = w.hg.bin_offsets;
+  s.permutation = w.hg.permutation;
+  s.spos = w.hg.spos;
+  s.scoord = w.hg.scoord;
+  s.n = n;
+  s.total = n * batch;
+  return s;
+}
+
+npa_status validate_decode(const npa_gaussian_decode_config* cfg, int64_t c) {
+  if (!cfg) return fail(NPA_ERR_INVALID_ARGUMENT, "decode config is null");
+  if (cfg->mode < 0 || cfg->mode > 3) return fail(NPA_ERR_INVALID_ARGUMENT, "unknown decode mode");
+  if (cfg->sh_degree < 0 || cfg->sh_degree > 8) return fail(NPA_ERR_INVALID_ARGUMENT, "sh_degree out of range");
+  const int64_t k = cfg->mode == NPA_DECODE_SH0_ORIENTED ? int64_t(cfg->sh_degree + 1) * (cfg->sh_degree + 1) : 1;
+  // validate_decode_layout (gaussian.rs:102-125), an assert! in the reference.
+  if ((cfg->mode <= NPA_DECODE_SH0_FIXED_SCALE && c < 3) ||
+      (cfg->mode == NPA_DECODE_SH0_LEARNED_SCALE && c < 5) ||
+      (cfg->mode == NPA_DECODE_SH0_ORIENTED && c < k * 3 + 8))
+    return fail(NPA_ERR_STATE_SHAPE, "state_dims too small for the decode mode's tail channels");
+  // f32::clamp asserts min <= max (NaN bounds fail the assert too).
+  if (!(cfg->min_scale <= cfg->max_scale) || !(cfg->min_opacity <= cfg->max_opacity))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "decode clamp bounds are inverted or NaN");
+  return NPA_OK;
+}
+
+int64_t record_floats(const npa_gaussian_decode_config* cfg) {
+  const int64_t k = cfg->mode == NPA_DECODE_SH0_ORIENTED ? int64_t(cfg->sh_degree + 1) * (cfg->sh_degree + 1) : 1;
+  return 12 + 3 * k;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct npa_model {
+  DeviceModel dm{};
+  npa_model_config cfg{};
+  std::mutex mu;
+};
+
+namespace {
+
+int64_t model_perception_dims(const npa_model_config& c) {
+  return int64_t(c.state_dims) * 2 + (c.state_grad ? int64_t(c.state_dims) * c.spatial_dims : 0) +
+         (c.density_grad ? c.spatial_dims : 0) + (c.position_features ? c.spatial_dims : 0) +
+         c.auxiliary_input_dims;
+}
+
+npa_perception_options model_options(const npa_model_config& c) {
+  npa_perception_options o{};
+  o.state_grad = c.state_grad;
+  o.density_grad = c.density_grad;
+  o.scale_equivariance = c.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE;
+  o.particle_density_equivariance = c.equivariance == NPA_EQUIV_PARTICLE_DENSITY ||
+                                    c.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE;
+  o.log_norm_grad = c.log_norm_grad;
+  o.log_norm_density_grad = c.log_norm_density_grad;
+  o.hybrid_state_gradient = 1;  // step_cpu always sets it (model.rs:800)
+  o.position_features = c.position_features;
+  o.eps0 = c.eps0;
+  return o;
+}
+
+// step_cpu's checks (model.rs:778-784) plus the 3D gate channel requirement.
+npa_status check_step(const npa_model* m, const npa_grid_config* grid) {
+  NPA_TRY(validate_grid(grid));
+  if (grid->dim != m->cfg.spatial_dims)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "grid dim does not match model spatial dims");
+  if (grid->dim == 3 && m->cfg.position_features && m->cfg.state_dims > 3 &&
+      m->cfg.state_dims <= 7)
+    return fail(NPA_ERR_INVALID_ARGUMENT,
+                "3D position gates read state channel 7; state_dims must exceed 7");
+  return NPA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t npa_abi_version(void) { return NPA_ABI_VERSION; }
+
+const char* npa_status_string(npa_status status) {
+  switch (status) {
+    case NPA_OK: return "ok";
+    case NPA_ERR_INVALID_DIM: return "invalid dim";
+    case NPA_ERR_INVALID_EPS: return "invalid eps";
+    case NPA_ERR_INVALID_GRID_SIZE: return "invalid grid size";
+    case NPA_ERR_PARTICLE_MODE_REQUIRES_POW2: return "particle mode requires power-of-two grid size";
+    case NPA_ERR_POSITION_SHAPE: return "position shape";
+    case NPA_ERR_STATE_SHAPE: return "state shape";
+    case NPA_ERR_OUTPUT_SHAPE: return "output shape";
+    case NPA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case NPA_ERR_INVALID_MODEL: return "invalid model";
+    case NPA_ERR_CUDA: return "cuda error";
+    case NPA_ERR_DEVICE_STATUS: return "device status error";
+    case NPA_ERR_TIMEOUT: return "device wait timed out";
+    case NPA_ERR_OUT_OF_MEMORY: return "out of memory";
+    case NPA_ERR_UNSUPPORTED: return "unsupported";
+    case NPA_ERR_NO_DEVICE: return "no device";
+    default: return "unknown status";
+  }
+}
+
+const char* npa_last_error_message(void) { return g_last_error.c_str(); }
+
+uint64_t npa_kernel_launch_count(void) { return g_launches.load(); }
+
+// Test hook for the out-of-memory path of the host-buffer entry points.
+void npa_debug_set_allocation_cap(uint64_t bytes) { g_alloc_cap.store(bytes); }
+
+npa_status npa_grid_validate(const npa_grid_config* cfg) { return validate_grid(cfg); }
+
+npa_status npa_grid_cell_count(const npa_grid_config* cfg, int64_t* cell_count) {
+  NPA_TRY(validate_grid(cfg));
+  if (!cell_count) return fail(NPA_ERR_INVALID_ARGUMENT, "null output");
+  int64_t c = 1;
+  for (int a = 0; a < cfg->dim; ++a) c *= cfg->grid_size[a];
+  *cell_count = c;
+  return NPA_OK;
+}
+
+npa_status npa_feature_dims(const npa_grid_config* cfg, const npa_perception_options* o,
+                            int64_t state_dims, int64_t* feature_dims) {
+  NPA_TRY(validate_grid(cfg));
+  if (!o || !feature_dims || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "bad argument");
+  *feature_dims = state_dims * 2 + (o->state_grad ? state_dims * cfg->dim : 0) +
+                  (o->density_grad ? cfg->dim : 0) + (o->position_features ? cfg->dim : 0);
+  return NPA_OK;
+}
+
+npa_status npa_gaussian_record_floats(const npa_gaussian_decode_config* cfg, int64_t* floats) {
+  if (!cfg || !floats) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  if (cfg->mode < 0 || cfg->mode > 3 || cfg->sh_degree < 0 || cfg->sh_degree > 8)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "bad decode config");
+  *floats = record_floats(cfg);
+  return NPA_OK;
+}
+
+// ---- host-buffer operators ----
+
+npa_status npa_build_hashgrid(const npa_grid_config* cfg, const float* positions,
+                              int64_t positions_len, int64_t batch, int64_t n,
+                              uint32_t* bin_offsets, int64_t bin_offsets_len,
+                              uint32_t* permutation, uint32_t* inverse_permutation,
+                              int64_t permutation_len) {
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_counts(batch, n));
+  if (positions_len != batch * n)
+    return fail(NPA_ERR_POSITION_SHAPE, "positions length does not match batch_size * particle_count");
+  NPA_TRY(check_bins(cfg, batch));
+  const GridParams g = make_grid_params(*cfg);
+  NPA_TRY(output_shape(bin_offsets_len, batch * int64_t(g.cells) + 1));
+  NPA_TRY(output_shape(permutation_len, batch * n));
+  if ((batch * n > 0 && (!positions || !permutation || !inverse_permutation)) || !bin_offsets)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch s;
+  NPA_TRY(s.init());
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  float4* dpos;
+  NPA_TRY(s.upload(&dpos, positions, total));
+  HashgridBuffers hb;
+  NPA_TRY(s.alloc(&hb.bin_offsets, size_t(B) * g.cells + 1));
+  NPA_TRY(s.alloc(&hb.permutation, total));
+  NPA_TRY(s.alloc(&hb.inverse, total));
+  NPA_TRY(s.alloc(&hb.spos, total));
+  NPA_TRY(s.alloc(&hb.scoord, total));
+  const size_t sb = hashgrid_scratch_bytes(g, B, N);
+  char* scratch;
+  NPA_TRY(s.alloc(&scratch, sb));
+  NPA_TRY(launch_hashgrid(g, dpos, B, N, hb, scratch, sb, s.stream));
+  NPA_TRY(s.download(bin_offsets, hb.bin_offsets, (size_t(B) * g.cells + 1) * 4));
+  NPA_TRY(s.download(permutation, hb.permutation, size_t(total) * 4));
+  NPA_TRY(s.download(inverse_permutation, hb.inverse, size_t(total) * 4));
+  return s.finish();
+}
+
+npa_status npa_perceive_with_options(const npa_grid_config* cfg, const npa_perception_options* o,
+                                     const float* positions, int64_t positions_len,
+                                     const float* states, int64_t states_len, int64_t batch,
+                                     int64_t n, int64_t state_dims, float* features,
+                                     int64_t features_len, float* density, float* blurred_state,
+                                     float* state_gradient, float* density_gradient) {
+  if (!o) return fail(NPA_ERR_INVALID_ARGUMENT, "options are null");
+  NPA_TRY(check_counts(batch, n));
+  if (state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "state_dims must be >= 0");
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, state_dims));
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_bins(cfg, batch));
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  const PerceptionParams p = make_perception_params(g, *o, N, int(state_dims));
+  NPA_TRY(output_shape(features_len, int64_t(total) * p.feature_dims));
+  if (total > 0 && (!positions || (state_dims > 0 && !states) || (p.feature_dims > 0 && !features)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch s;
+  NPA_TRY(s.init());
+  float4* dpos;
+  float* dst;
+  NPA_TRY(s.upload(&dpos, positions, total));
+  NPA_TRY(s.upload(&dst, states, size_t(total) * state_dims));
+  const size_t wsb = perceive_workspace_bytes(g, B, N);
+  char* ws;
+  NPA_TRY(s.alloc(&ws, wsb));
+  float *dfeat, *ddens = nullptr, *dblur = nullptr, *dsg = nullptr, *ddg = nullptr;
+  NPA_TRY(s.alloc(&dfeat, size_t(total) * p.feature_dims));
+  if (density) NPA_TRY(s.alloc(&ddens, total));
+  if (blurred_state) NPA_TRY(s.alloc(&dblur, size_t(total) * state_dims));
+  if (state_gradient && p.state_grad) NPA_TRY(s.alloc(&dsg, size_t(total) * state_dims * g.dim));
+  if (density_gradient && p.density_grad) NPA_TRY(s.alloc(&ddg, size_t(total) * g.dim));
+  NPA_TRY(npa_dev_perceive_with_options(cfg, o, reinterpret_cast<float*>(dpos), dst, batch, n,
+                                        state_dims, dfeat, ddens, dblur, dsg, ddg, ws, wsb,
+                                        s.stream));
+  NPA_TRY(s.download(features, dfeat, size_t(total) * p.feature_dims * 4));
+  NPA_TRY(s.download(density, ddens, size_t(total) * 4 * (ddens != nullptr)));
+  NPA_TRY(s.download(blurred_state, dblur, size_t(total) * state_dims * 4 * (dblur != nullptr)));
+  NPA_TRY(s.download(state_gradient, dsg, size_t(total) * state_dims * g.dim * 4 * (dsg != nullptr)));
+  NPA_TRY(s.download(density_gradient, ddg, size_t(total) * g.dim * 4 * (ddg != nullptr)));
+  return s.finish();
+}
+
+npa_status npa_euler_step(const npa_grid_config* cfg, const float* positions,
+                          int64_t positions_len, const float* states, int64_t states_len,
+                          const float* dx, int64_t dx_len, const float* ds, int64_t ds_len,
+                          int64_t batch, int64_t n, int64_t state_dims, float dt,
+                          const float* update_mask, float* next_positions, float* next_states) {
+  NPA_TRY(check_counts(batch, n));
+  if (state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "state_dims must be >= 0");
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, state_dims));
+  NPA_TRY(output_shape(dx_len, positions_len));
+  NPA_TRY(output_shape(ds_len, states_len));
+  NPA_TRY(validate_grid(cfg));
+  const uint32_t total = uint32_t(batch * n);
+  if (total > 0 && (!positions || !dx || !next_positions ||
+                    (state_dims > 0 && (!states || !ds || !next_states))))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  const GridParams g = make_grid_params(*cfg);
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch s;
+  NPA_TRY(s.init());
+  float4 *dpos, *ddx, *dnp;
+  float *dst, *dds, *dns, *dmask = nullptr;
+  NPA_TRY(s.upload(&dpos, positions, total));
+  NPA_TRY(s.upload(&dst, states, size_t(total) * state_dims));
+  NPA_TRY(s.upload(&ddx, dx, total));
+  NPA_TRY(s.upload(&dds, ds, size_t(total) * state_dims));
+  if (update_mask) NPA_TRY(s.upload(&dmask, update_mask, total));
+  NPA_TRY(s.alloc(&dnp, total));
+  NPA_TRY(s.alloc(&dns, size_t(total) * state_dims));
+  NPA_TRY(launch_euler(g, dpos, dst, ddx, dds, total, int(state_dims), dt, dmask, dnp, dns,
+                       s.stream));
+  NPA_TRY(s.download(next_positions, dnp, size_t(total) * 16));
+  NPA_TRY(s.download(next_states, dns, size_t(total) * state_dims * 4));
+  return s.finish();
+}
+
+npa_status npa_decode_gaussians_3d(const npa_gaussian_decode_config* cfg, const float* positions,
+                                   int64_t positions_len, const float* states,
+                                   int64_t states_len, int64_t state_dims, float* out,
+                                   int64_t out_len) {
+  if (positions_len < 0 || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "negative length");
+  // assert_eq!(positions.len() * state_dims, states.len()) (gaussian.rs:59)
+  if (positions_len * state_dims != states_len)
+    return fail(NPA_ERR_STATE_SHAPE, "states length does not match positions * state_dims");
+  NPA_TRY(validate_decode(cfg, state_dims));
+  if (positions_len > int64_t(kMaxParticles)) return fail(NPA_ERR_UNSUPPORTED, "too many particles");
+  NPA_TRY(output_shape(out_len, positions_len * record_floats(cfg)));
+  const uint32_t count = uint32_t(positions_len);
+  if (count > 0 && (!positions || !states || !out)) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch s;
+  NPA_TRY(s.init());
+  float4* dpos;
+  float *dst, *dout;
+  NPA_TRY(s.upload(&dpos, positions, count));
+  NPA_TRY(s.upload(&dst, states, size_t(count) * state_dims));
+  NPA_TRY(s.alloc(&dout, size_t(out_len)));
+  NPA_TRY(launch_decode(*cfg, dpos, dst, count, int(state_dims), dout, s.stream));
+  NPA_TRY(s.download(out, dout, size_t(out_len) * 4));
+  return s.finish();
+}
+
+// ---- model ----
+
+npa_status npa_model_create(const npa_model_config* cfg, const float* w1, int64_t w1_len,
+                            const float* b1, int64_t b1_len, const float* w2, int64_t w2_len,
+                            const float* b2, int64_t b2_len, int32_t device, npa_model** out) {
+  if (!cfg || !out) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  // NpaModel::validate (model.rs:757-766) then NpaWeights::validate (:77-107).
+  if (!(cfg->spatial_dims == 2 || cfg->spatial_dims == 3))
+    return fail(NPA_ERR_INVALID_MODEL, "spatial_dims must be 2 or 3");
+  if (cfg->state_dims < 0 || cfg->hidden_dims <= 0 || cfg->auxiliary_input_dims < 0)
+    return fail(NPA_ERR_INVALID_MODEL, "state_dims, hidden_dims and auxiliary_input_dims must be non-negative");
+  if (!(cfg->equivariance >= 0 && cfg->equivariance <= 2))
+    return fail(NPA_ERR_INVALID_MODEL, "unknown equivariance mode");
+  const int64_t F = model_perception_dims(*cfg);
+  const int64_t H = cfg->hidden_dims;
+  const int64_t O = int64_t(cfg->spatial_dims) + cfg->state_dims;
+  if (w1_len != H * F) return fail(NPA_ERR_INVALID_MODEL, "w1 len " + std::to_string(w1_len) + " != " + std::to_string(H * F));
+  if (b1_len != H) return fail(NPA_ERR_INVALID_MODEL, "b1 len " + std::to_string(b1_len) + " != " + std::to_string(H));
+  if (w2_len != O * H) return fail(NPA_ERR_INVALID_MODEL, "w2 len " + std::to_string(w2_len) + " != " + std::to_string(O * H));
+  if (b2_len != O) return fail(NPA_ERR_INVALID_MODEL, "b2 len " + std::to_string(b2_len) + " != " + std::to_string(O));
+  if (!w1 || !b1 || !w2 || !b2) return fail(NPA_ERR_INVALID_ARGUMENT, "null weights");
+  if (cfg->auxiliary_input_dims != 0)
+    return fail(NPA_ERR_UNSUPPORTED, "auxiliary input dims are not part of the rollout step");
+  if (H > 256 || O > 64)
+    return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range (hidden <= 256, update dims <= 64)");
+  NPA_TRY(ensure_device(device));
+  const int64_t Hp = (H + 127) / 128 * 128;
+  std::vector<float> w1t(size_t(F) * Hp, 0.0f);
+  for (int64_t h = 0; h < H; ++h)
+    for (int64_t f = 0; f < F; ++f) w1t[size_t(f) * Hp + h] = w1[h * F + f];
+  npa_model* m = new npa_model();
+  m->cfg = *cfg;
+  DeviceModel& d = m->dm;
+  d.spatial_dims = cfg->spatial_dims;
+  d.state_dims = cfg->state_dims;
+  d.hidden_dims = int(H);
+  d.feature_dims = int(F);
+  d.update_dims = int(O);
+  d.eps0 = cfg->eps0;
+  d.alpha = cfg->alpha;
+  d.equivariance = cfg->equivariance;
+  d.density_grad = cfg->density_grad;
+  d.state_grad = cfg->state_grad;
+  d.log_norm_grad = cfg->log_norm_grad;
+  d.log_norm_density_grad = cfg->log_norm_density_grad;
+  d.position_features = cfg->position_features;
+  d.device = device;
+  auto up = [&](float** dst, const float* src, size_t count) -> npa_status {
+    NPA_CUDA(cudaMalloc(dst, std::max<size_t>(count, 4) * sizeof(float)), "cudaMalloc weights");
+    NPA_CUDA(cudaMemcpy(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice), "cudaMemcpy weights");
+    return NPA_OK;
+  };
+  npa_status st = up(&d.w1t, w1t.data(), w1t.size());
+  if (st == NPA_OK) st = up(&d.b1, b1, size_t(H));
+  if (st == NPA_OK) st = up(&d.w2, w2, size_t(O * H));
+  if (st == NPA_OK) st = up(&d.b2, b2, size_t(O));
+  if (st != NPA_OK) {
+    npa_model_destroy(m);
+    return st;
+  }
+  *out = m;
+  return NPA_OK;
+}
+
+void npa_model_destroy(npa_model* m) {
+  if (!m) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->dm.device);
+  cudaFree(m->dm.w1t);
+  cudaFree(m->dm.b1);
+  cudaFree(m->dm.w2);
+  cudaFree(m->dm.b2);
+  cudaSetDevice(prev);
+  delete m;
+}
+
+npa_status npa_model_forward_update_from_features(npa_model* m, const float* features,
+                                                  int64_t features_len, float* update,
+                                                  int64_t update_len) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  const int64_t F = m->dm.feature_dims, O = m->dm.update_dims;
+  if (features_len < 0 || features_len % F != 0)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "feature len " + std::to_string(features_len) +
+                                              " is not divisible by perception dims " + std::to_string(F));
+  const int64_t rows = features_len / F;
+  if (rows > int64_t(kMaxParticles)) return fail(NPA_ERR_UNSUPPORTED, "too many rows");
+  NPA_TRY(output_shape(update_len, rows * O));
+  if (rows > 0 && (!features || !update)) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_device(m->dm.device));
+  Scratch s;
+  NPA_TRY(s.init());
+  float *df, *du;
+  NPA_TRY(s.upload(&df, features, size_t(features_len)));
+  NPA_TRY(s.alloc(&du, size_t(update_len)));
+  NPA_TRY(launch_forward_update(m->dm, df, uint32_t(rows), du, s.stream));
+  NPA_TRY(s.download(update, du, size_t(update_len) * 4));
+  return s.finish();
+}
+
+npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float* positions,
+                          int64_t positions_len, const float* states, int64_t states_len,
+                          int64_t batch, int64_t n, float dt, const float* update_mask,
+                          float* next_positions, float* next_states, float* dx, float* ds,
+                          float* features, float* density) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_step(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, m->dm.state_dims));
+  NPA_TRY(check_bins(grid, batch));
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  const int C = m->dm.state_dims;
+  if (total > 0 && (!positions || (C > 0 && (!states || !next_states)) || !next_positions))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_device(m->dm.device));
+  const GridParams g = make_grid_params(*grid);
+  Scratch s;
+  NPA_TRY(s.init());
+  float4* dpos;
+  float *dst, *dmask = nullptr;
+  NPA_TRY(s.upload(&dpos, positions, total));
+  NPA_TRY(s.upload(&dst, states, size_t(total) * C));
+  if (update_mask) NPA_TRY(s.upload(&dmask, update_mask, total));
+  float4 *dnp, *ddx = nullptr;
+  float *dns, *dds = nullptr, *dfeat = nullptr, *ddens = nullptr;
+  NPA_TRY(s.alloc(&dnp, total));
+  NPA_TRY(s.alloc(&dns, size_t(total) * C));
+  if (dx) NPA_TRY(s.alloc(&ddx, total));
+  if (ds) NPA_TRY(s.alloc(&dds, size_t(total) * C));
+  if (features) NPA_TRY(s.alloc(&dfeat, size_t(total) * m->dm.feature_dims));
+  if (density) NPA_TRY(s.alloc(&ddens, total));
+  size_t wsb = 0;
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
+  char* ws;
+  NPA_TRY(s.alloc(&ws, wsb));
+  NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(dpos), dst, batch, n, dt, dmask,
+                             reinterpret_cast<float*>(dnp), dns, reinterpret_cast<float*>(ddx),
+                             dds, dfeat, ddens, ws, wsb, s.stream));
+  NPA_TRY(s.download(next_positions, dnp, size_t(total) * 16));
+  NPA_TRY(s.download(next_states, dns, size_t(total) * C * 4));
+  if (dx) NPA_TRY(s.download(dx, ddx, size_t(total) * 16));
+  if (ds) NPA_TRY(s.download(ds, dds, size_t(total) * C * 4));
+  if (features) NPA_TRY(s.download(features, dfeat, size_t(total) * m->dm.feature_dims * 4));
+  if (density) NPA_TRY(s.download(density, ddens, size_t(total) * 4));
+  return s.finish();
+}
+
+// ---- device operators ----
+
+npa_status npa_dev_hashgrid_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,
+                                           size_t* bytes) {
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(cfg, batch));
+  if (!bytes) return fail(NPA_ERR_INVALID_ARGUMENT, "null output");
+  const GridParams g = make_grid_params(*cfg);
+  *bytes = hashgrid_scratch_bytes(g, uint32_t(batch), uint32_t(n)) +
+           sorted_view_bytes(uint32_t(batch), uint32_t(n)) + 256;
+  return NPA_OK;
+}
+
+npa_status npa_dev_build_hashgrid(const npa_grid_config* cfg, const float* d_positions,
+                                  int64_t batch, int64_t n, uint32_t* d_bin_offsets,
+                                  uint32_t* d_permutation, uint32_t* d_inverse_permutation,
+                                  void* d_workspace, size_t workspace_bytes, void* stream) {
+  size_t need = 0;
+  NPA_TRY(npa_dev_hashgrid_workspace_size(cfg, batch, n, &need));
+  if (workspace_bytes < need) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  if (!d_bin_offsets || (batch * n > 0 && (!d_positions || !d_permutation || !d_inverse_permutation || !d_workspace)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  Carve c(d_workspace, workspace_bytes);
+  HashgridBuffers hb;
+  hb.bin_offsets = d_bin_offsets;
+  hb.permutation = d_permutation;
+  hb.inverse = d_inverse_permutation;
+  hb.spos = c.take<float4>(total);
+  hb.scoord = c.take<int4>(total);
+  const size_t sb = hashgrid_scratch_bytes(g, B, N);
+  char* scratch = c.take<char>(sb);
+  if (!c.fits()) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  return launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, hb, scratch, sb,
+                         static_cast<cudaStream_t>(stream));
+}
+
+npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,
+                                           int64_t state_dims, size_t* bytes) {
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(cfg, batch));
+  if (!bytes || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "bad argument");
+  const GridParams g = make_grid_params(*cfg);
+  *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n));
+  return NPA_OK;
+}
+
+npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
+                                         const npa_perception_options* o,
+                                         const float* d_positions, const float* d_states,
+                                         int64_t batch, int64_t n, int64_t state_dims,
+                                         float* d_features, float* d_density,
+                                         float* d_blurred_state, float* d_state_gradient,
+                                         float* d_density_gradient, void* d_workspace,
+                                         size_t workspace_bytes, void* stream) {
+  if (!o) return fail(NPA_ERR_INVALID_ARGUMENT, "options are null");
+  size_t need = 0;
+  NPA_TRY(npa_dev_perceive_workspace_size(cfg, batch, n, state_dims, &need));
+  if (workspace_bytes < need) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  const PerceptionParams p = make_perception_params(g, *o, N, int(state_dims));
+  if (total > 0 && (!d_positions || (state_dims > 0 && !d_states) || (p.feature_dims > 0 && !d_features) || !d_workspace))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  PerceiveWorkspace w;
+  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
+                          w.sort_scratch, w.sort_scratch_bytes, st));
+  const SortedGrid sv = sorted_view(w, N, B);
+  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, st));
+  return launch_perception(g, p, sv, B, d_states, int(state_dims), w.volume, d_features,
+                           d_blurred_state, p.state_grad ? d_state_gradient : nullptr,
+                           p.density_grad ? d_density_gradient : nullptr, st);
+}
+
+npa_status npa_dev_model_forward_update(npa_model* m, const float* d_features, int64_t rows,
+                                        float* d_update, void* stream) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  if (rows < 0 || rows > int64_t(kMaxParticles)) return fail(NPA_ERR_INVALID_ARGUMENT, "bad row count");
+  if (rows > 0 && (!d_features || !d_update)) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  return launch_forward_update(m->dm, d_features, uint32_t(rows), d_update,
+                               static_cast<cudaStream_t>(stream));
+}
+
+npa_status npa_dev_euler_step(const npa_grid_config* cfg, const float* d_positions,
+                              const float* d_states, const float* d_dx, const float* d_ds,
+                              int64_t batch, int64_t n, int64_t state_dims, float dt,
+                              const float* d_update_mask, float* d_next_positions,
+                              float* d_next_states, void* stream) {
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_counts(batch, n));
+  if (state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "state_dims must be >= 0");
+  const GridParams g = make_grid_params(*cfg);
+  return launch_euler(g, reinterpret_cast<const float4*>(d_positions), d_states,
+                      reinterpret_cast<const float4*>(d_dx), d_ds, uint32_t(batch * n),
+                      int(state_dims), dt, d_update_mask, reinterpret_cast<float4*>(d_next_positions),
+                      d_next_states, static_cast<cudaStream_t>(stream));
+}
+
+npa_status npa_dev_decode_gaussians_3d(const npa_gaussian_decode_config* cfg,
+                                       const float* d_positions, const float* d_states,
+                                       int64_t count, int64_t state_dims, float* d_out,
+                                       void* stream) {
+  if (count < 0 || count > int64_t(kMaxParticles)) return fail(NPA_ERR_INVALID_ARGUMENT, "bad count");
+  NPA_TRY(validate_decode(cfg, state_dims));
+  return launch_decode(*cfg, reinterpret_cast<const float4*>(d_positions), d_states,
+                       uint32_t(count), int(state_dims), d_out, static_cast<cudaStream_t>(stream));
+}
+
+npa_status npa_dev_step_workspace_size(npa_model* m, const npa_grid_config* grid, int64_t batch,
+                                       int64_t n, size_t* bytes) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_step(m, grid));
+  return npa_dev_perceive_workspace_size(grid, batch, n, m->dm.state_dims, bytes);
+}
+
+npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const float* d_positions,
+                              const float* d_states, int64_t batch, int64_t n, float dt,
+                              const float* d_update_mask, float* d_next_positions,
+                              float* d_next_states, float* d_dx, float* d_ds, float* d_features,
+                              float* d_density, void* d_workspace, size_t workspace_bytes,
+                              void* stream) {
+  size_t need = 0;
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &need));
+  if (workspace_bytes < need) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  const GridParams g = make_grid_params(*grid);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  if (total > 0 && (!d_positions || !d_next_positions || !d_workspace ||
+                    (m->dm.state_dims > 0 && (!d_states || !d_next_states))))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (!fused_step_supported(m->dm))
+    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the fused kernel's range (state_dims <= 32)");
+  PerceiveWorkspace w;
+  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  const PerceptionParams p = make_perception_params(g, model_options(m->cfg), N, m->dm.state_dims);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
+                          w.sort_scratch, w.sort_scratch_bytes, st));
+  const SortedGrid sv = sorted_view(w, N, B);
+  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, st));
+  StepOutputs out;
+  out.next_positions = reinterpret_cast<float4*>(d_next_positions);
+  out.next_states = d_next_states;
+  out.dx = reinterpret_cast<float4*>(d_dx);
+  out.ds = d_ds;
+  out.features = d_features;
+  return launch_fused_step(m->dm, g, p, sv, B, reinterpret_cast<const float4*>(d_positions),
+                           d_states, w.volume, dt, d_update_mask, out, st);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// executor
+// ---------------------------------------------------------------------------
+// One rollout step is three phases, each captured into its own CUDA graph per
+// ping-pong parity: (0) hashgrid, (1) density, (2) fused perception + MLP +
+// Euler.  Replaying the phases as separate graphs lets a caller bracket the
+// dominant kernel with CUDA events on the launching stream.
+constexpr int kPhases = 3;
+
+struct npa_executor {
+  npa_model* model = nullptr;
+  npa_grid_config grid{};
+  GridParams g{};
+  PerceptionParams p{};
+  int64_t batch = 0, n = 0;
+  float* pos[2] = {nullptr, nullptr};
+  float* st[2] = {nullptr, nullptr};
+  int cur = 0;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  PerceiveWorkspace w{};
+  cudaGraphExec_t graph[2][kPhases] = {};
+  float graph_dt = 0.0f;
+  cudaStream_t graph_stream = nullptr;
+  int64_t launches[kPhases] = {0, 0, 0};
+};
+
+namespace {
+
+npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cudaStream_t s) {
+  const uint32_t B = uint32_t(e->batch), N = uint32_t(e->n);
+  const SortedGrid sv = sorted_view(e->w, N, B);
+  switch (phase) {
+    case 0:
+      return launch_hashgrid(e->g, reinterpret_cast<const float4*>(e->pos[from]), B, N, e->w.hg,
+                             e->w.sort_scratch, e->w.sort_scratch_bytes, s);
+    case 1:
+      return launch_density(e->g, sv, B, e->w.volume, nullptr, s);
+    default: {
+      StepOutputs out;
+      out.next_positions = reinterpret_cast<float4*>(e->pos[1 - from]);
+      out.next_states = e->st[1 - from];
+      out.dx = nullptr;
+      out.ds = nullptr;
+      out.features = nullptr;
+      return launch_fused_step(e->model->dm, e->g, e->p, sv, B,
+                               reinterpret_cast<const float4*>(e->pos[from]), e->st[from],
+                               e->w.volume, dt, nullptr, out, s);
+    }
+  }
+}
+
+void exec_drop_graphs(npa_executor* e) {
+  for (auto& row : e->graph)
+    for (auto& g : row) {
+      if (g) cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+}
+
+npa_status exec_capture(npa_executor* e, float dt, cudaStream_t stream) {
+  exec_drop_graphs(e);
+  for (int from = 0; from < 2; ++from) {
+    for (int phase = 0; phase < kPhases; ++phase) {
+      cudaGraph_t graph = nullptr;
+      NPA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal),
+               "cudaStreamBeginCapture");
+      const uint64_t before = npa_kernel_launch_count();
+      npa_status st = exec_enqueue_phase(e, from, phase, dt, stream);
+      cudaError_t ce = cudaStreamEndCapture(stream, &graph);
+      if (st != NPA_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return st;
+      }
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+      e->launches[phase] = int64_t(npa_kernel_launch_count() - before);
+      ce = cudaGraphInstantiate(&e->graph[from][phase], graph, 0);
+      cudaGraphDestroy(graph);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    }
+  }
+  e->graph_dt = dt;
+  e->graph_stream = stream;
+  return NPA_OK;
+}
+
+npa_status exec_run_phase(npa_executor* e, int phase, float dt, int32_t use_graph,
+                          cudaStream_t s) {
+  if (use_graph) {
+    NPA_CUDA(cudaGraphLaunch(e->graph[e->cur][phase], s), "cudaGraphLaunch");
+    g_launches.fetch_add(uint64_t(e->launches[phase]), std::memory_order_relaxed);
+    return NPA_OK;
+  }
+  return exec_enqueue_phase(e, e->cur, phase, dt, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_t batch,
+                               int64_t n, npa_executor** out) {
+  if (!m || !out) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  NPA_TRY(check_step(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(grid, batch));
+  if (!fused_step_supported(m->dm))
+    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the fused kernel's range (state_dims <= 32)");
+  NPA_TRY(ensure_device(m->dm.device));
+  npa_executor* e = new npa_executor();
+  e->model = m;
+  e->grid = *grid;
+  e->g = make_grid_params(*grid);
+  e->p = make_perception_params(e->g, model_options(m->cfg), uint32_t(n), m->dm.state_dims);
+  e->batch = batch;
+  e->n = n;
+  const size_t total = size_t(batch) * n;
+  const size_t C = size_t(m->dm.state_dims);
+  e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n));
+  npa_status st = NPA_OK;
+  auto alloc = [&](void** p, size_t b) -> npa_status {
+    NPA_CUDA(cudaMalloc(p, std::max<size_t>(b, 256)), "cudaMalloc executor");
+    return NPA_OK;
+  };
+  for (int i = 0; i < 2 && st == NPA_OK; ++i) {
+    st = alloc(reinterpret_cast<void**>(&e->pos[i]), total * 16);
+    if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->st[i]), total * C * 4);
+  }
+  if (st == NPA_OK) st = alloc(&e->ws, e->ws_bytes);
+  if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w))
+    st = fail(NPA_ERR_INVALID_ARGUMENT, "executor workspace layout");
+  if (st != NPA_OK) {
+    npa_executor_destroy(e);
+    return st;
+  }
+  *out = e;
+  return NPA_OK;
+}
+
+void npa_executor_destroy(npa_executor* e) {
+  if (!e) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(e->model->dm.device);
+  exec_drop_graphs(e);
+  for (int i = 0; i < 2; ++i) {
+    cudaFree(e->pos[i]);
+    cudaFree(e->st[i]);
+  }
+  cudaFree(e->ws);
+  cudaSetDevice(prev);
+  delete e;
+}
+
+npa_status npa_executor_upload_state(npa_executor* e, const float* positions, const float* states) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  NPA_TRY(ensure_device(e->model->dm.device));
+  const size_t total = size_t(e->batch) * e->n;
+  const size_t C = size_t(e->model->dm.state_dims);
+  if (total && (!positions || (C && !states))) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_CUDA(cudaMemcpy(e->pos[e->cur], positions, total * 16, cudaMemcpyHostToDevice), "upload positions");
+  if (C) NPA_CUDA(cudaMemcpy(e->st[e->cur], states, total * C * 4, cudaMemcpyHostToDevice), "upload states");
+  return NPA_OK;
+}
+
+npa_status npa_executor_set_state_device(npa_executor* e, const float* d_positions,
+                                         const float* d_states, void* stream) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  NPA_TRY(ensure_device(e->model->dm.device));
+  const size_t total = size_t(e->batch) * e->n;
+  const size_t C = size_t(e->model->dm.state_dims);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  NPA_CUDA(cudaMemcpyAsync(e->pos[e->cur], d_positions, total * 16, cudaMemcpyDeviceToDevice, s), "copy positions");
+  if (C) NPA_CUDA(cudaMemcpyAsync(e->st[e->cur], d_states, total * C * 4, cudaMemcpyDeviceToDevice, s), "copy states");
+  return NPA_OK;
+}
+
+static npa_status exec_prepare(npa_executor* e, int64_t steps, float dt, int32_t use_graph,
+                               cudaStream_t s) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
+  NPA_TRY(ensure_device(e->model->dm.device));
+  if (use_graph && s == nullptr) return fail(NPA_ERR_INVALID_ARGUMENT, "graph replay needs a non-default stream");
+  if (use_graph && (!e->graph[0][0] || e->graph_dt != dt || e->graph_stream != s))
+    NPA_TRY(exec_capture(e, dt, s));
+  return NPA_OK;
+}
+
+npa_status npa_executor_step_many(npa_executor* e, int64_t steps, float dt, int32_t use_graph,
+                                  void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  NPA_TRY(exec_prepare(e, steps, dt, use_graph, s));
+  for (int64_t k = 0; k < steps; ++k) {
+    for (int phase = 0; phase < kPhases; ++phase) NPA_TRY(exec_run_phase(e, phase, dt, use_graph, s));
+    e->cur = 1 - e->cur;
+  }
+  return NPA_OK;
+}
+
+npa_status npa_executor_step_many_profiled(npa_executor* e, int64_t steps, float dt,
+                                           int32_t use_graph, void* stream, float* phase_ms,
+                                           float* total_ms) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  NPA_TRY(exec_prepare(e, steps, dt, use_graph, s));
+  if (!phase_ms || !total_ms) return fail(NPA_ERR_INVALID_ARGUMENT, "null timing output");
+  std::vector<cudaEvent_t> ev(size_t(steps) * (kPhases + 1) + 1, nullptr);
+  npa_status st = NPA_OK;
+  for (auto& x : ev)
+    if (cudaEventCreate(&x) != cudaSuccess) st = fail(NPA_ERR_CUDA, "cudaEventCreate");
+  if (st == NPA_OK && steps > 0) {
+    for (int64_t k = 0; k < steps && st == NPA_OK; ++k) {
+      cudaEventRecord(ev[size_t(k) * (kPhases + 1)], s);
+      for (int phase = 0; phase < kPhases && st == NPA_OK; ++phase) {
+        st = exec_run_phase(e, phase, dt, use_graph, s);
+        cudaEventRecord(ev[size_t(k) * (kPhases + 1) + phase + 1], s);
+      }
+      e->cur = 1 - e->cur;
+    }
+    if (st == NPA_OK && cudaStreamSynchronize(s) != cudaSuccess) st = fail(NPA_ERR_CUDA, "sync");
+    if (st == NPA_OK) {
+      for (int64_t k = 0; k < steps; ++k)
+        for (int phase = 0; phase < kPhases; ++phase) {
+          float ms = 0.0f;
+          cudaEventElapsedTime(&ms, ev[size_t(k) * (kPhases + 1) + phase],
+                               ev[size_t(k) * (kPhases + 1) + phase + 1]);
+          phase_ms[k * kPhases + phase] = ms;
+        }
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, ev[0], ev[size_t(steps - 1) * (kPhases + 1) + kPhases]);
+      *total_ms = ms;
+    }
+  }
+  for (auto& x : ev)
+    if (x) cudaEventDestroy(x);
+  return st;
+}
+
+npa_status npa_executor_read_state(npa_executor* e, float* positions, float* states) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  NPA_TRY(ensure_device(e->model->dm.device));
+  NPA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  const size_t total = size_t(e->batch) * e->n;
+  const size_t C = size_t(e->model->dm.state_dims);
+  if (positions) NPA_CUDA(cudaMemcpy(positions, e->pos[e->cur], total * 16, cudaMemcpyDeviceToHost), "read positions");
+  if (states && C) NPA_CUDA(cudaMemcpy(states, e->st[e->cur], total * C * 4, cudaMemcpyDeviceToHost), "read states");
+  return NPA_OK;
+}
+
+npa_status npa_executor_state_device(npa_executor* e, float** d_positions, float** d_states) {
+  if (!e || !d_positions || !d_states) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *d_positions = e->pos[e->cur];
+  *d_states = e->st[e->cur];
+  return NPA_OK;
+}
+
+npa_status npa_executor_launches_per_step(npa_executor* e, int64_t* launches) {
+  if (!e || !launches) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *launches = e->launches[0] + e->launches[1] + e->launches[2];
+  return NPA_OK;
+}
+
+npa_status npa_model_run_rollout(npa_model* m, const npa_grid_config* grid, float* positions,
+                                 int64_t positions_len, float* states, int64_t states_len,
+                                 int64_t batch, int64_t n, int64_t steps, float dt) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_step(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, m->dm.state_dims));
+  if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
+  npa_executor* e = nullptr;
+  NPA_TRY(npa_executor_create(m, grid, batch, n, &e));
+  cudaStream_t s = nullptr;
+  npa_status st = NPA_OK;
+  if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+    st = fail(NPA_ERR_CUDA, "cudaStreamCreate");
+  if (st == NPA_OK) st = npa_executor_upload_state(e, positions, states);
+  if (st == NPA_OK) st = npa_executor_step_many(e, steps, dt, steps > 2 ? 1 : 0, s);
+  if (st == NPA_OK) st = npa_executor_read_state(e, positions, states);
+  if (s) cudaStreamDestroy(s);
+  npa_executor_destroy(e);
+  return st;
+}
+
+}  // extern "C"

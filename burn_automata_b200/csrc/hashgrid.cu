@@ -1,0 +1,281 @@
+// hashgrid.cu -- build_hashgrid (crates/burn_automata_kernels/src/hashgrid.rs:16-69)
+// as a stable device-wide LSD radix sort.
+//
+// The reference runs a serial counting sort: count particles per
+// (batch, cell) bin, exclusive-prefix the counts into bin_offsets, then scatter
+// particles in ascending index order.  The result is the unique ordering by
+// key = batch * cell_count + cell with ties broken by particle index.  Any
+// stable sort by key produces exactly that ordering, so this file sorts
+// (key, index) pairs with 8-bit LSD radix passes whose per-tile ranks are
+// stable, and derives bin_offsets from the key boundaries of the sorted
+// array.  Output is bit-identical to the reference.
+//
+// Per pass: a digit histogram per 4096-item tile, one exclusive scan of the
+// digit-major [256 x tiles] table, then a scatter that ranks items inside the
+// tile in index order (warp match_any + per-warp digit counters + a
+// cross-warp prefix).  No kernel waits on another block.
+#include <utility>
+
+#include "npa_internal.h"
+
+namespace npa {
+namespace {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kItemsPerLane = 16;
+constexpr int kWarpItems = 32 * kItemsPerLane;             // 512
+constexpr int kTile = kSortWarps * kWarpItems;              // 4096
+constexpr int kDigits = 256;
+constexpr int kScanThreads = 1024;
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Keys of one tile plus the histogram of digit 0.
+__global__ void __launch_bounds__(kSortThreads)
+keys_hist_kernel(GridParams g, const float4* __restrict__ pos, uint32_t total, uint32_t n,
+                 uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                 uint32_t* __restrict__ hist, uint32_t tiles) {
+  __shared__ uint32_t h[kDigits];
+  for (int i = threadIdx.x; i < kDigits; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t seg = blockIdx.x * kTile + warp * kWarpItems;
+#pragma unroll 4
+  for (int r = 0; r < kItemsPerLane; ++r) {
+    const uint32_t i = seg + r * 32 + lane;
+    if (i < total) {
+      const uint32_t b = i / n;
+      const uint32_t key = b * g.cells + cell_for_position(g, pos[i]);
+      keys[i] = key;
+      vals[i] = i;
+      atomicAdd(&h[key & 0xffu], 1u);
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < kDigits; d += blockDim.x) hist[d * tiles + blockIdx.x] = h[d];
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+hist_kernel(const uint32_t* __restrict__ keys, uint32_t total, uint32_t shift,
+            uint32_t* __restrict__ hist, uint32_t tiles) {
+  __shared__ uint32_t h[kDigits];
+  for (int i = threadIdx.x; i < kDigits; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const uint32_t base = blockIdx.x * kTile;
+  for (uint32_t k = threadIdx.x; k < kTile; k += blockDim.x) {
+    const uint32_t i = base + k;
+    if (i < total) atomicAdd(&h[(keys[i] >> shift) & 0xffu], 1u);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < kDigits; d += blockDim.x) hist[d * tiles + blockIdx.x] = h[d];
+}
+
+// In-place exclusive scan of `count` (a multiple of 4) uint32 by one block.
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(uint32_t* __restrict__ data,
+                                                            uint32_t count) {
+  __shared__ uint32_t warp_tot[32];
+  __shared__ uint32_t carry_s;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry_s = 0;
+  __syncthreads();
+  for (uint32_t base = 0; base < count; base += kScanThreads * 4) {
+    const uint32_t idx = base + tid * 4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (idx < count) v = *reinterpret_cast<const uint4*>(data + idx);
+    const uint32_t s1 = v.x + v.y, s2 = s1 + v.z, s3 = s2 + v.w;
+    uint32_t incl = s3;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t t = warp_tot[lane];
+      uint32_t wi = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t u = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += u;
+      }
+      warp_tot[lane] = wi - t;  // exclusive warp offsets
+    }
+    __syncthreads();
+    const uint32_t carry = carry_s;
+    const uint32_t off = carry + warp_tot[warp] + (incl - s3);
+    if (idx < count) {
+      uint4 o;
+      o.x = off;
+      o.y = off + v.x;
+      o.z = off + s1;
+      o.w = off + s2;
+      *reinterpret_cast<uint4*>(data + idx) = o;
+    }
+    __syncthreads();
+    if (tid == kScanThreads - 1) carry_s = off + s3;
+    __syncthreads();
+  }
+}
+
+// One stable radix pass: keys/vals of a tile are ranked in index order and
+// scattered to their global slots.
+__global__ void __launch_bounds__(kSortThreads)
+scatter_kernel(const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+               uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t total,
+               uint32_t shift, const uint32_t* __restrict__ hist_scanned, uint32_t tiles) {
+  __shared__ uint32_t wh[kSortWarps][kDigits];
+  for (int i = threadIdx.x; i < kSortWarps * kDigits; i += blockDim.x) (&wh[0][0])[i] = 0;
+  __syncthreads();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t seg = blockIdx.x * kTile + warp * kWarpItems;
+  const uint32_t lt = lanemask_lt();
+  uint32_t k[kItemsPerLane], v[kItemsPerLane], rank[kItemsPerLane];
+#pragma unroll
+  for (int r = 0; r < kItemsPerLane; ++r) {
+    const uint32_t i = seg + r * 32 + lane;
+    const bool valid = i < total;
+    k[r] = valid ? keys_in[i] : 0u;
+    v[r] = valid ? vals_in[i] : 0u;
+    // Invalid lanes get a digit that matches no valid lane.
+    const uint32_t d = valid ? ((k[r] >> shift) & 0xffu) : (0x100u + lane);
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const uint32_t before = valid ? wh[warp][d] : 0u;
+    __syncwarp();
+    if (valid && lane == static_cast<uint32_t>(__ffs(peers) - 1))
+      wh[warp][d] = before + __popc(peers);
+    __syncwarp();
+    rank[r] = before + __popc(peers & lt);
+  }
+  __syncthreads();
+  // Cross-warp exclusive prefix per digit, offset by the tile's global base.
+  for (int d = threadIdx.x; d < kDigits; d += blockDim.x) {
+    uint32_t run = hist_scanned[d * tiles + blockIdx.x];
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t c = wh[w][d];
+      wh[w][d] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kItemsPerLane; ++r) {
+    const uint32_t i = seg + r * 32 + lane;
+    if (i < total) {
+      const uint32_t d = (k[r] >> shift) & 0xffu;
+      const uint32_t dst = wh[warp][d] + rank[r];
+      if (dst < total) {  // always true for a consistent histogram; keeps writes in bounds
+        keys_out[dst] = k[r];
+        vals_out[dst] = v[r];
+      }
+    }
+  }
+}
+
+// Reference outputs and sorted views from the sorted (key, index) pairs.
+__global__ void finalize_kernel(GridParams g, const float4* __restrict__ pos,
+                                const uint32_t* __restrict__ keys,
+                                const uint32_t* __restrict__ vals, uint32_t total, uint32_t n,
+                                uint32_t total_bins, uint32_t* __restrict__ bin_offsets,
+                                uint32_t* __restrict__ perm, uint32_t* __restrict__ inv,
+                                float4* __restrict__ spos, int4* __restrict__ scoord) {
+  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= total) return;
+  const uint32_t key = keys[q];
+  const uint32_t i = vals[q];
+  if (i >= total || key >= total_bins) return;  // only reachable if the sort were inconsistent
+  const uint32_t b = i / n;
+  perm[q] = i - b * n;
+  inv[i] = q - b * n;
+  const float4 p = pos[i];
+  spos[q] = p;
+  const int3 c = cell_coords(g, p);
+  scoord[q] = make_int4(c.x, c.y, c.z, 0);
+  // bin_offsets[bin] = first sorted slot whose key >= bin.
+  const uint32_t first = q == 0 ? 0u : keys[q - 1] + 1u;
+  for (uint32_t bin = first; bin <= key; ++bin) bin_offsets[bin] = q;
+  if (q == total - 1)
+    for (uint32_t bin = key + 1; bin <= total_bins; ++bin) bin_offsets[bin] = total;
+}
+
+__global__ void fill_u32_kernel(uint32_t* p, uint32_t count, uint32_t value) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) p[i] = value;
+}
+
+uint32_t key_bits(uint64_t bins) {
+  uint32_t bits = 0;
+  while (bits < 32 && (uint64_t(1) << bits) < bins) ++bits;
+  return bits;
+}
+
+}  // namespace
+
+size_t sorted_view_bytes(uint32_t batch, uint32_t n) {
+  const size_t total = size_t(batch) * n;
+  return ((total * sizeof(float4) + 255) & ~size_t(255)) + total * sizeof(int4) + 256;
+}
+
+size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n) {
+  const size_t total = size_t(batch) * n;
+  const size_t tiles = (total + kTile - 1) / kTile;
+  Carve c(nullptr, 0);
+  c.take<uint32_t>(total);
+  c.take<uint32_t>(total);
+  c.take<uint32_t>(total);
+  c.take<uint32_t>(total);
+  c.take<uint32_t>(tiles * kDigits);
+  return c.used + 256;
+}
+
+npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_t batch,
+                           uint32_t n, const HashgridBuffers& out, void* scratch,
+                           size_t scratch_bytes, cudaStream_t stream) {
+  const uint64_t total64 = uint64_t(batch) * n;
+  const uint64_t bins64 = uint64_t(batch) * g.cells;
+  const uint32_t total = static_cast<uint32_t>(total64);
+  const uint32_t bins = static_cast<uint32_t>(bins64);
+  if (total == 0) {
+    fill_u32_kernel<<<grid_for(bins + 1, 256), 256, 0, stream>>>(out.bin_offsets, bins + 1, 0u);
+    return after_launch("fill_u32_kernel");
+  }
+  const uint32_t tiles = static_cast<uint32_t>((total64 + kTile - 1) / kTile);
+  Carve c(scratch, scratch_bytes);
+  uint32_t* ka = c.take<uint32_t>(total);
+  uint32_t* va = c.take<uint32_t>(total);
+  uint32_t* kb = c.take<uint32_t>(total);
+  uint32_t* vb = c.take<uint32_t>(total);
+  uint32_t* hist = c.take<uint32_t>(size_t(tiles) * kDigits);
+  if (!c.fits()) return fail(NPA_ERR_INVALID_ARGUMENT, "hashgrid workspace too small");
+
+  const uint32_t bits = key_bits(bins64);
+  const uint32_t passes = bits == 0 ? 1u : (bits + 7) / 8;
+  keys_hist_kernel<<<tiles, kSortThreads, 0, stream>>>(g, positions, total, n, ka, va, hist,
+                                                        tiles);
+  NPA_TRY(after_launch("keys_hist_kernel"));
+  for (uint32_t pass = 0; pass < passes; ++pass) {
+    const uint32_t shift = pass * 8;
+    if (pass > 0) {
+      hist_kernel<<<tiles, kSortThreads, 0, stream>>>(ka, total, shift, hist, tiles);
+      NPA_TRY(after_launch("hist_kernel"));
+    }
+    scan_kernel<<<1, kScanThreads, 0, stream>>>(hist, tiles * kDigits);
+    NPA_TRY(after_launch("scan_kernel"));
+    scatter_kernel<<<tiles, kSortThreads, 0, stream>>>(ka, va, kb, vb, total, shift, hist, tiles);
+    NPA_TRY(after_launch("scatter_kernel"));
+    std::swap(ka, kb);
+    std::swap(va, vb);
+  }
+  finalize_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
+      g, positions, ka, va, total, n, bins, out.bin_offsets, out.permutation, out.inverse,
+      out.spos, out.scoord);
+  return after_launch("finalize_kernel");
+}
+
+}  // namespace npa

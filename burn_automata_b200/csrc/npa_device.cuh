@@ -1,0 +1,300 @@
+// npa_device.cuh -- device-side semantics shared by every kernel.
+//
+// Each helper restates one function of the reference's CPU path with the same
+// f32 operation order.  The library is compiled with --fmad=false, IEEE
+// division and IEEE square root (no fast-math), so `a * b + c` is a rounded
+// multiply followed by a rounded add, exactly as rustc emits it.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace npa {
+
+constexpr int kBoundaryPeriodic = 0;
+constexpr int kBoundaryClamped = 1;
+constexpr int kModeGrid = 0;
+constexpr int kModeParticle = 1;
+
+// Grid constants for the kernels.  Host code fills it from npa_grid_config so
+// that every derived f32 constant is computed once, in the reference's order.
+struct GridParams {
+  int dim;
+  int boundary;
+  int mode;
+  int grid_size[3];
+  uint32_t cells;      // HashGridConfig::cell_count (config.rs:86-88)
+  float eps;
+  float eps2;          // eps * eps (neighbor.rs:25)
+  float extent[3];     // grid_size[axis] as f32 * eps (hashgrid.rs:170 / :80)
+  float half[3];       // extent * 0.5
+  float poly6_norm;    // smoothing_poly6_normalization (kernels.rs:128-134)
+  float spiky_norm;    // gradient_spiky_normalization (kernels.rs:136-142)
+};
+
+// `f as isize` then `as i32`: saturating conversion (NaN -> 0), low 32 bits kept.
+// cvt.rzi.s64.f32 saturates and maps NaN to 0, like Rust's `as`.
+__device__ __forceinline__ int f2i_low32(float integral) {
+  return static_cast<int>(static_cast<long long>(integral));
+}
+
+__device__ __forceinline__ long long f2ll_sat(float integral) {
+  return static_cast<long long>(integral);
+}
+
+// mix_coord (hashgrid.rs:155-163).
+__device__ __forceinline__ uint32_t mix_coord(int value_low32, uint32_t salt) {
+  uint32_t x = static_cast<uint32_t>(value_low32) ^ salt;
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+// particle_cell_hash (hashgrid.rs:147-153).
+__device__ __forceinline__ uint32_t particle_cell_hash(const GridParams& g, int cx, int cy, int cz) {
+  uint32_t h = mix_coord(cx, 0x9e3779b9u) ^ mix_coord(cy, 0x85ebca6bu);
+  if (g.dim == 3) h ^= mix_coord(cz, 0xc2b2ae35u);
+  return h % g.cells;
+}
+
+// Grid-mode axis cell (hashgrid.rs:80-90 / :106-116).
+__device__ __forceinline__ int grid_axis_cell(const GridParams& g, int axis, float coordinate) {
+  long long cell = f2ll_sat(floorf((coordinate + g.half[axis]) / g.eps));
+  long long size = g.grid_size[axis];
+  if (g.boundary == kBoundaryPeriodic) {
+    long long r = cell % size;
+    return static_cast<int>(r < 0 ? r + size : r);
+  }
+  if (cell < 0) cell = 0;
+  if (cell > size - 1) cell = size - 1;
+  return static_cast<int>(cell);
+}
+
+// cell_coords_for_position (hashgrid.rs:98-121); low 32 bits of each coordinate.
+__device__ __forceinline__ int3 cell_coords(const GridParams& g, float4 p) {
+  int c[3] = {0, 0, 0};
+  const float v[3] = {p.x, p.y, p.z};
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    if (axis < g.dim) {
+      if (g.mode == kModeParticle) {
+        c[axis] = f2i_low32(floorf(v[axis] / g.eps));
+      } else {
+        c[axis] = grid_axis_cell(g, axis, v[axis]);
+      }
+    }
+  }
+  return make_int3(c[0], c[1], c[2]);
+}
+
+// cell_index_from_coords (hashgrid.rs:123-145); returns -1 for None.
+__device__ __forceinline__ long long cell_index(const GridParams& g, int cx, int cy, int cz) {
+  if (g.mode == kModeParticle) return particle_cell_hash(g, cx, cy, cz);
+  const int c[3] = {cx, cy, cz};
+  unsigned long long stride = 1, hash = 0;
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    if (axis < g.dim) {
+      int size = g.grid_size[axis];
+      int cell;
+      if (g.boundary == kBoundaryPeriodic) {
+        int r = c[axis] % size;
+        cell = r < 0 ? r + size : r;
+      } else {
+        if (c[axis] < 0 || c[axis] >= size) return -1;
+        cell = c[axis];
+      }
+      hash += static_cast<unsigned long long>(cell) * stride;
+      stride *= static_cast<unsigned long long>(size);
+    }
+  }
+  return static_cast<long long>(hash);
+}
+
+// cell_for_position (hashgrid.rs:71-96).
+__device__ __forceinline__ uint32_t cell_for_position(const GridParams& g, float4 p) {
+  int3 c = cell_coords(g, p);
+  if (g.mode == kModeParticle) return particle_cell_hash(g, c.x, c.y, c.z);
+  return static_cast<uint32_t>(cell_index(g, c.x, c.y, c.z));
+}
+
+// neighbor_delta (hashgrid.rs:165-181).
+__device__ __forceinline__ float4 neighbor_delta(const GridParams& g, float4 lhs, float4 rhs) {
+  float d[3] = {rhs.x - lhs.x, rhs.y - lhs.y, rhs.z - lhs.z};
+  float out[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    if (axis < g.dim) {
+      float v = d[axis];
+      if (g.boundary == kBoundaryPeriodic) {
+        if (v > g.half[axis]) {
+          v -= g.extent[axis];
+        } else if (v < -g.half[axis]) {
+          v += g.extent[axis];
+        }
+      }
+      out[axis] = v;
+    }
+  }
+  return make_float4(out[0], out[1], out[2], 0.0f);
+}
+
+// wrap_position (hashgrid.rs:183-193): (c + half).rem_euclid(extent) - half.
+__device__ __forceinline__ float4 wrap_position(const GridParams& g, float4 p) {
+  if (g.boundary != kBoundaryPeriodic) return p;
+  float v[3] = {p.x, p.y, p.z};
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    if (axis < g.dim) {
+      float a = v[axis] + g.half[axis];
+      float r = fmodf(a, g.extent[axis]);
+      if (r < 0.0f) r = r + fabsf(g.extent[axis]);
+      v[axis] = r - g.half[axis];
+    }
+  }
+  return make_float4(v[0], v[1], v[2], p.w);
+}
+
+// RecipFinite::recip_finite (kernels.rs:156-165).
+__device__ __forceinline__ float recip_finite(float x) {
+  if (fabsf(x) <= 1e-20f || !isfinite(x)) return 0.0f;
+  return 1.0f / x;
+}
+
+// smoothing_poly6_kernel (kernels.rs:53-60).
+__device__ __forceinline__ float poly6(const GridParams& g, float r2) {
+  if (r2 >= g.eps2) return 0.0f;
+  float x = g.eps2 - r2;
+  return g.poly6_norm * x * x * x;
+}
+
+// spiky_gradient_kernel magnitude (kernels.rs:81-98): coeff * k * 3 * (eps-r)^2 / r;
+// the gradient is mag * delta[axis].  Zero for r2 <= 0 or r2 >= eps^2.
+__device__ __forceinline__ float spiky_mag(const GridParams& g, float r2, float coeff) {
+  if (r2 <= 0.0f || r2 >= g.eps2) return 0.0f;
+  float r = sqrtf(r2);
+  float t = g.eps - r;
+  return coeff * g.spiky_norm * 3.0f * (t * t) / r;
+}
+
+// safe_inverse_symmetric (kernels.rs:3-51); reads m[0], m[1], m[3] (2D) or
+// m[0], m[1], m[2], m[4], m[5], m[8] (3D), i.e. the upper triangle.
+__device__ __forceinline__ void safe_inverse_symmetric(const float* m, int dim, float* out) {
+  const float TOL = 1e-3f;
+#pragma unroll
+  for (int i = 0; i < 9; ++i) out[i] = 0.0f;
+  if (dim == 2) {
+    float a = m[0], b = m[1], d = m[3];
+    float det = a * d - b * b;
+    if (fabsf(det) < TOL) {
+      out[0] = 1.0f;
+      out[3] = 1.0f;
+      return;
+    }
+    float inv_det = 1.0f / det;
+    out[0] = d * inv_det;
+    out[1] = -b * inv_det;
+    out[2] = -b * inv_det;
+    out[3] = a * inv_det;
+    return;
+  }
+  float a = m[0], b = m[1], c = m[2], d = m[4], e = m[5], f = m[8];
+  float t1 = d * f - e * e;
+  float t2 = c * e - b * f;
+  float t3 = b * e - c * d;
+  float det = a * t1 + b * t2 + c * t3;
+  if (fabsf(det) < TOL) {
+    out[0] = 1.0f;
+    out[4] = 1.0f;
+    out[8] = 1.0f;
+    return;
+  }
+  float inv_det = 1.0f / det;
+  out[0] = t1 * inv_det;
+  out[1] = t2 * inv_det;
+  out[2] = t3 * inv_det;
+  out[3] = t2 * inv_det;
+  out[4] = (a * f - c * c) * inv_det;
+  out[5] = (b * c - a * e) * inv_det;
+  out[6] = t3 * inv_det;
+  out[7] = (b * c - a * e) * inv_det;
+  out[8] = (a * d - b * b) * inv_det;
+}
+
+// ln(1 + x) rounded once to f32: evaluated in f64 (CUDA's log1p) and
+// converted.  The reference calls the host libm's log1pf, which is within one
+// ulp of this value.
+__device__ __forceinline__ float log1p_f32(float x) {
+  return static_cast<float>(log1p(static_cast<double>(x)));
+}
+
+// log_normalize_vector (normalize.rs:60-69) on `len` (2 or 3) values.
+__device__ __forceinline__ void log_normalize(float* v, int len) {
+  float s = 0.0f;
+  for (int i = 0; i < len; ++i) s = s + v[i] * v[i];
+  const float e = 1.0e-6f;
+  float norm = fmaxf(sqrtf(s + e * e), e);
+  float scale = log1p_f32(norm) / norm;
+  for (int i = 0; i < len; ++i) v[i] = v[i] * scale;
+}
+
+// f32::clamp (NaN passes through).
+__device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
+  if (v < lo) v = lo;
+  if (v > hi) v = hi;
+  return v;
+}
+
+// Sorted-slot view of the hashgrid used by every neighbour walk.
+struct SortedGrid {
+  const uint32_t* bin_offsets;  // [B*cells + 1], global sorted slots
+  const uint32_t* permutation;  // [B*N] local index of each sorted slot
+  const float4* spos;           // [B*N] positions in sorted order
+  const int4* scoord;           // [B*N] cell coordinates in sorted order
+  uint32_t n;                   // particles per batch
+  uint32_t total;               // B*N: sorted slots are < total
+};
+
+// for_each_neighbor (neighbor.rs:3-44): cells in dz, dy, dx order, bin
+// ranges in permutation order, Particle-mode collision filter on exact
+// coordinates, keeps r2 < eps^2 including the particle itself.
+// visit(q, delta, r2) receives the sorted slot q of the neighbour.
+template <class Visit>
+__device__ __forceinline__ void for_each_neighbor(const GridParams& g, const SortedGrid& s,
+                                                  uint32_t batch, float4 pi, int3 center,
+                                                  Visit&& visit) {
+  const int zmin = g.dim == 3 ? -1 : 0;
+  const int zmax = g.dim == 3 ? 1 : 0;
+  const uint32_t bin_base = batch * g.cells;
+  for (int dz = zmin; dz <= zmax; ++dz) {
+    for (int dy = -1; dy <= 1; ++dy) {
+      for (int dx = -1; dx <= 1; ++dx) {
+        const int cx = static_cast<int>(static_cast<uint32_t>(center.x) + static_cast<uint32_t>(dx));
+        const int cy = static_cast<int>(static_cast<uint32_t>(center.y) + static_cast<uint32_t>(dy));
+        const int cz = static_cast<int>(static_cast<uint32_t>(center.z) + static_cast<uint32_t>(dz));
+        long long cell = cell_index(g, cx, cy, cz);
+        if (cell < 0) continue;
+        const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
+        const uint32_t begin = __ldg(s.bin_offsets + bin);
+        const uint32_t end = min(__ldg(s.bin_offsets + bin + 1), s.total);
+        for (uint32_t q = begin; q < end; ++q) {
+          if (g.mode == kModeParticle) {
+            const int4 cq = __ldg(s.scoord + q);
+            if (cq.x != cx || cq.y != cy || cq.z != cz) continue;
+          }
+          const float4 pj = __ldg(s.spos + q);
+          const float4 d = neighbor_delta(g, pi, pj);
+          float r2 = d.x * d.x;
+          r2 = r2 + d.y * d.y;
+          if (g.dim == 3) r2 = r2 + d.z * d.z;
+          if (r2 < g.eps2) visit(q, d, r2);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace npa

@@ -1,0 +1,133 @@
+// npa_internal.h -- host-side plumbing shared by the library's translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/npa_b200.h"
+#include "npa_device.cuh"
+
+namespace npa {
+
+// Thread-local last-error text (npa_last_error_message).
+void set_error(const std::string& msg);
+npa_status fail(npa_status st, const std::string& msg);
+// Maps a CUDA error to NPA_ERR_CUDA / NPA_ERR_OUT_OF_MEMORY with its text.
+npa_status cuda_fail(cudaError_t err, const char* what);
+// Counts kernel launches (npa_kernel_launch_count) and checks the launch.
+npa_status after_launch(const char* kernel, int launches = 1);
+
+#define NPA_TRY(expr)                    \
+  do {                                   \
+    npa_status st__ = (expr);            \
+    if (st__ != NPA_OK) return st__;     \
+  } while (0)
+
+#define NPA_CUDA(expr, what)                          \
+  do {                                                \
+    cudaError_t e__ = (expr);                         \
+    if (e__ != cudaSuccess) return cuda_fail(e__, what); \
+  } while (0)
+
+// Validation mirroring HashGridConfig::validate (config.rs:65-84) plus the
+// limits of this implementation (cell counts and indices fit in uint32).
+npa_status validate_grid(const npa_grid_config* cfg);
+GridParams make_grid_params(const npa_grid_config& cfg);
+
+// Bump allocator over a caller workspace; every block is 256-byte aligned.
+struct Carve {
+  char* base;
+  size_t used = 0;
+  size_t cap;
+  explicit Carve(void* p, size_t bytes) : base(static_cast<char*>(p)), cap(bytes) {}
+  template <class T>
+  T* take(size_t count) {
+    size_t off = (used + 255) & ~size_t(255);
+    used = off + count * sizeof(T) + 0;
+    return reinterpret_cast<T*>(base ? base + off : nullptr);
+  }
+  bool fits() const { return used <= cap; }
+};
+
+// ---- hashgrid (hashgrid.cu) ----
+struct HashgridBuffers {
+  uint32_t* bin_offsets;   // [B*cells + 1]
+  uint32_t* permutation;   // [B*N]
+  uint32_t* inverse;       // [B*N]
+  float4* spos;            // [B*N] sorted positions
+  int4* scoord;            // [B*N] sorted cell coordinates
+};
+// Bytes of scratch the sort needs beyond HashgridBuffers.
+size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n);
+// Size of the sorted views (spos + scoord).
+size_t sorted_view_bytes(uint32_t batch, uint32_t n);
+npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_t batch,
+                           uint32_t n, const HashgridBuffers& out, void* scratch,
+                           size_t scratch_bytes, cudaStream_t stream);
+
+// ---- perception (perception.cu) ----
+struct PerceptionParams {
+  int state_grad, density_grad, scale_eq, pde, log_norm_grad, log_norm_density_grad, hybrid,
+      position_features;
+  float state_scale;    // normalize_state_gradient scale (normalize.rs:11-15)
+  float density_scale;  // normalize_density_gradient scale (normalize.rs:38-46)
+  int feature_dims;
+};
+PerceptionParams make_perception_params(const GridParams& g, const npa_perception_options& o,
+                                        uint32_t n, int state_dims);
+// density + volume per sorted slot; density_out (original order) optional.
+npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t batch,
+                          float* volume_sorted, float* density_out, cudaStream_t stream);
+// Standalone perception writing features / intermediates in original order.
+npa_status launch_perception(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
+                             uint32_t batch, const float* states, int state_dims,
+                             const float* volume_sorted, float* features, float* blurred,
+                             float* state_gradient, float* density_gradient,
+                             cudaStream_t stream);
+
+// ---- model / step (step.cu) ----
+struct DeviceModel {
+  int spatial_dims, state_dims, hidden_dims, feature_dims, update_dims;
+  float eps0, alpha;
+  int equivariance;
+  int density_grad, state_grad, log_norm_grad, log_norm_density_grad, position_features;
+  int device;
+  float* w1t;  // [F][H] (w1 transposed so a k-slice is contiguous)
+  float* b1;   // [H]
+  float* w2;   // [O][H]
+  float* b2;   // [O]
+};
+npa_status launch_forward_update(const DeviceModel& m, const float* features, uint32_t rows,
+                                 float* update, cudaStream_t stream);
+npa_status launch_euler(const GridParams& g, const float4* positions, const float* states,
+                        const float4* dx, const float* ds, uint32_t total, int state_dims,
+                        float dt, const float* mask, float4* next_positions, float* next_states,
+                        cudaStream_t stream);
+struct StepOutputs {
+  float4* next_positions;
+  float* next_states;
+  float4* dx;        // optional
+  float* ds;         // optional
+  float* features;   // optional
+};
+// Fused perception + MLP + dx/ds (+3D gates) + Euler over sorted slots.
+npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                             const SortedGrid& s, uint32_t batch, const float4* positions,
+                             const float* states, const float* volume_sorted, float dt,
+                             const float* mask, const StepOutputs& out, cudaStream_t stream);
+bool fused_step_supported(const DeviceModel& m);
+
+// ---- decode (decode.cu) ----
+npa_status launch_decode(const npa_gaussian_decode_config& cfg, const float4* positions,
+                         const float* states, uint32_t count, int state_dims, float* out,
+                         cudaStream_t stream);
+
+inline unsigned grid_for(uint64_t items, unsigned block) {
+  uint64_t g = (items + block - 1) / block;
+  return static_cast<unsigned>(g > 0 ? g : 1);
+}
+
+}  // namespace npa

@@ -1,0 +1,196 @@
+"""Operator surface of crates/burn_automata_kernels, backed by the CUDA library.
+
+Same names, argument meaning and error behaviour as the reference:
+  build_hashgrid         hashgrid.rs:16
+  perceive               reference/forward.rs:4
+  perceive_with_options  reference/forward.rs:26
+  euler_step             reference/step.rs:4
+  decode_gaussians_3d    gaussian.rs:53
+Host numpy arrays go through the host-buffer C entry points (copy in, compute
+on the GPU, copy out); torch CUDA tensors go through the npa_dev_* entry
+points on the current torch stream.  Errors raise the KernelError subclass
+matching the reference's variant.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Optional
+
+import numpy as np
+
+from . import _lib
+from .config import (GaussianDecodeConfig, GaussianDecodeMode, HashGridConfig,
+                     PerceptionOptions, feature_dims)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _fp(a):
+    return None if a is None else a.ctypes.data_as(_lib.f32p)
+
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch") and hasattr(x, "is_cuda")
+
+
+@dataclass
+class HashGridSnapshot:
+    """hashgrid.rs:3-14."""
+
+    batch_size: int
+    particle_count: int
+    cell_count: int
+    bin_offsets: np.ndarray
+    permutation: np.ndarray
+    inverse_permutation: np.ndarray
+
+
+@dataclass
+class PerceptionOutput:
+    """reference/types.rs:33-41."""
+
+    features: np.ndarray
+    density: np.ndarray
+    blurred_state: np.ndarray
+    state_gradient: np.ndarray
+    density_gradient: np.ndarray
+    feature_dims: int
+
+
+@dataclass
+class Gaussian3d:
+    """gaussian.rs:4-11."""
+
+    position_visibility: List[float]
+    spherical_harmonic: List[List[float]]
+    rotation: List[float]
+    scale_opacity: List[float]
+
+
+def build_hashgrid(positions, batch_size: int, particle_count: int,
+                   cfg: HashGridConfig) -> HashGridSnapshot:
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    L = _lib.lib()
+    g = _lib.grid_c(cfg)
+    cells = ctypes.c_int64(0)
+    _lib.check(L.npa_grid_cell_count(ctypes.byref(g), ctypes.byref(cells)), "build_hashgrid")
+    total = batch_size * particle_count
+    offsets = np.zeros(batch_size * cells.value + 1, np.uint32)
+    perm = np.zeros(max(total, 0), np.uint32)
+    inv = np.zeros(max(total, 0), np.uint32)
+    _lib.check(L.npa_build_hashgrid(ctypes.byref(g), _fp(pos), pos.shape[0], batch_size,
+                                    particle_count, offsets.ctypes.data_as(_lib.u32p),
+                                    offsets.shape[0], perm.ctypes.data_as(_lib.u32p),
+                                    inv.ctypes.data_as(_lib.u32p), perm.shape[0]),
+               "build_hashgrid")
+    return HashGridSnapshot(batch_size, particle_count, cells.value, offsets, perm, inv)
+
+
+def perceive_with_options(positions, states, batch_size: int, particle_count: int,
+                          state_dims: int, cfg: HashGridConfig,
+                          options: PerceptionOptions) -> PerceptionOutput:
+    if _is_torch(positions):
+        return _perceive_device(positions, states, batch_size, particle_count, state_dims, cfg,
+                                options)
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    st = _f32(states).reshape(-1)
+    total = batch_size * particle_count
+    fd = feature_dims(cfg, options, state_dims) if cfg.dim in (2, 3) else 0
+    feats = np.zeros(max(total * fd, 0), np.float32)
+    dens = np.zeros(max(total, 0), np.float32)
+    blur = np.zeros(max(total * state_dims, 0), np.float32)
+    sgrad = np.zeros(max(total * state_dims * cfg.dim, 0) if options.state_grad else 0, np.float32)
+    dgrad = np.zeros(max(total * cfg.dim, 0) if options.density_grad else 0, np.float32)
+    L = _lib.lib()
+    g, o = _lib.grid_c(cfg), _lib.options_c(options)
+    _lib.check(L.npa_perceive_with_options(
+        ctypes.byref(g), ctypes.byref(o), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
+        batch_size, particle_count, state_dims, _fp(feats), feats.shape[0], _fp(dens),
+        _fp(blur), _fp(sgrad) if options.state_grad else None,
+        _fp(dgrad) if options.density_grad else None), "perceive_with_options")
+    return PerceptionOutput(feats, dens, blur, sgrad, dgrad, fd)
+
+
+def perceive(positions, states, batch_size, particle_count, state_dims, cfg, state_grad: bool,
+             density_grad: bool) -> PerceptionOutput:
+    return perceive_with_options(positions, states, batch_size, particle_count, state_dims, cfg,
+                                 PerceptionOptions.new(state_grad, density_grad, cfg.eps))
+
+
+def _perceive_device(positions, states, batch, n, c, cfg, options) -> PerceptionOutput:
+    import torch
+
+    dev = positions.device
+    total = batch * n
+    fd = feature_dims(cfg, options, c)
+    L = _lib.lib()
+    g, o = _lib.grid_c(cfg), _lib.options_c(options)
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(L.npa_dev_perceive_workspace_size(ctypes.byref(g), batch, n, c,
+                                                 ctypes.byref(ws_bytes)), "perceive")
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=dev)
+    feats = torch.empty(total * fd, dtype=torch.float32, device=dev)
+    dens = torch.empty(total, dtype=torch.float32, device=dev)
+    blur = torch.empty(total * c, dtype=torch.float32, device=dev)
+    sgrad = torch.empty(total * c * cfg.dim if options.state_grad else 0, dtype=torch.float32,
+                        device=dev)
+    dgrad = torch.empty(total * cfg.dim if options.density_grad else 0, dtype=torch.float32,
+                        device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.npa_dev_perceive_with_options(
+        ctypes.byref(g), ctypes.byref(o), positions.data_ptr(), states.data_ptr(), batch, n, c,
+        feats.data_ptr(), dens.data_ptr(), blur.data_ptr(),
+        sgrad.data_ptr() if options.state_grad else None,
+        dgrad.data_ptr() if options.density_grad else None, ws.data_ptr(), ws_bytes.value,
+        stream), "perceive")
+    return PerceptionOutput(feats, dens, blur, sgrad, dgrad, fd)
+
+
+def euler_step(positions, states, dx, ds, batch_size: int, particle_count: int, state_dims: int,
+               cfg: HashGridConfig, dt: float, update_mask=None):
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    st = _f32(states).reshape(-1)
+    dxa = _f32(dx).reshape(-1, 4) if np.size(dx) else np.zeros((0, 4), np.float32)
+    dsa = _f32(ds).reshape(-1)
+    mask = _f32(update_mask).reshape(-1) if update_mask is not None else None
+    npos = np.zeros_like(pos)
+    nst = np.zeros_like(st)
+    L = _lib.lib()
+    g = _lib.grid_c(cfg)
+    _lib.check(L.npa_euler_step(ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
+                                _fp(dxa), dxa.shape[0], _fp(dsa), dsa.shape[0], batch_size,
+                                particle_count, state_dims, float(dt), _fp(mask), _fp(npos),
+                                _fp(nst)), "euler_step")
+    return npos, nst
+
+
+def decode_gaussians_3d_records(positions, states, state_dims: int,
+                                cfg: GaussianDecodeConfig) -> np.ndarray:
+    """Decoded Gaussians as the C ABI's flat records [count, 12 + 3k]:
+    [position_visibility 4][rotation 4][scale_opacity 4][spherical_harmonic 3k]."""
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    st = _f32(states).reshape(-1)
+    rec = cfg.record_floats()
+    out = np.zeros(pos.shape[0] * rec, np.float32)
+    L = _lib.lib()
+    d = _lib.decode_c(cfg)
+    _lib.check(L.npa_decode_gaussians_3d(ctypes.byref(d), _fp(pos), pos.shape[0], _fp(st),
+                                         st.shape[0], state_dims, _fp(out), out.shape[0]),
+               "decode_gaussians_3d")
+    return out.reshape(pos.shape[0], rec)
+
+
+def decode_gaussians_3d(positions, states, state_dims: int,
+                        cfg: GaussianDecodeConfig) -> List[Gaussian3d]:
+    recs = decode_gaussians_3d_records(positions, states, state_dims, cfg)
+    k = cfg.sh_coeffs()
+    out = []
+    for r in recs:
+        sh = [list(map(float, r[12 + 3 * q:15 + 3 * q])) for q in range(k)]
+        out.append(Gaussian3d(list(map(float, r[0:4])), sh, list(map(float, r[4:8])),
+                              list(map(float, r[8:12]))))
+    return out

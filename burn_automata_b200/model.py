@@ -1,0 +1,261 @@
+"""NpaModel, the rollout driver and the resident executor, backed by the CUDA library.
+
+Mirrors crates/burn_automata:
+  NpaWeights / NpaModel::{step_cpu, forward_update_from_features,
+                          forward_from_features_with_eps}   src/model.rs:11-17, :768-940
+  RolloutConfig / RolloutTrace / run_rollout_from_particles  src/rollout/mod.rs:102-283
+  WgpuAutomataExecutor::{create_state, step_state_many, read_state}
+                                                              src/gpu/executor/*
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from .config import InvalidArgument, NpaConfig, HashGridConfig
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _fp(a):
+    return None if a is None else a.ctypes.data_as(_lib.f32p)
+
+
+@dataclass
+class NpaWeights:
+    """model.rs:11-17: w1 [hidden, perception_dims], b1 [hidden], w2 [update_dims, hidden], b2."""
+
+    w1: np.ndarray
+    b1: np.ndarray
+    w2: np.ndarray
+    b2: np.ndarray
+
+    @staticmethod
+    def zeros(cfg: NpaConfig) -> "NpaWeights":
+        f, h, o = cfg.perception_dims(), cfg.hidden_dims, cfg.update_dims()
+        return NpaWeights(np.zeros(h * f, np.float32), np.zeros(h, np.float32),
+                          np.zeros(o * h, np.float32), np.zeros(o, np.float32))
+
+
+@dataclass
+class StepOutput:
+    """model.rs:735-744 (perception carries the features and density)."""
+
+    next_positions: np.ndarray
+    next_states: np.ndarray
+    dx: np.ndarray
+    ds: np.ndarray
+    features: np.ndarray
+    density: np.ndarray
+
+
+class NpaModel:
+    """NpaModel { config, weights } with the weights resident on one CUDA device."""
+
+    def __init__(self, config: NpaConfig, weights, device: int = 0):
+        self.config = config
+        self.weights = weights
+        self.device = int(device)
+        L = _lib.lib()
+        m = _lib.model_c(config)
+        ws = [_f32(getattr(weights, k)).reshape(-1) for k in ("w1", "b1", "w2", "b2")]
+        handle = ctypes.c_void_p()
+        _lib.check(L.npa_model_create(ctypes.byref(m), _fp(ws[0]), ws[0].shape[0], _fp(ws[1]),
+                                      ws[1].shape[0], _fp(ws[2]), ws[2].shape[0], _fp(ws[3]),
+                                      ws[3].shape[0], self.device, ctypes.byref(handle)),
+                   "NpaModel")
+        self._handle = handle
+
+    @property
+    def handle(self):
+        return self._handle
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            _lib.lib().npa_model_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward_update_from_features(self, features) -> np.ndarray:
+        """model.rs:900-940."""
+        f = _f32(features).reshape(-1)
+        F = self.config.perception_dims()
+        rows = f.shape[0] // F if F else 0
+        out = np.zeros(rows * self.config.update_dims(), np.float32)
+        _lib.check(_lib.lib().npa_model_forward_update_from_features(
+            self._handle, _fp(f), f.shape[0], _fp(out), out.shape[0]),
+            "forward_update_from_features")
+        return out
+
+    def forward_from_features_with_eps(self, features, eps: float):
+        """model.rs:867-898 (host-side composition of the device MLP)."""
+        update = self.forward_update_from_features(features).reshape(-1, self.config.update_dims())
+        D, C = self.config.spatial_dims, self.config.state_dims
+        rows = update.shape[0]
+        dx = np.zeros((rows, 4), np.float32)
+        ds = np.zeros((rows, C), np.float32)
+        motion_eps = np.float32(self.config.motion_eps(eps))
+        alpha = np.float32(self.config.alpha)
+        for r in range(rows):
+            u = update[r]
+            norm = np.float32(0.0)
+            for a in range(D):
+                norm = np.float32(norm + np.float32(u[a] * u[a]))
+            norm = np.float32(np.sqrt(norm))
+            for a in range(D):
+                dx[r, a] = np.float32(np.float32(np.float32(alpha * u[a]) * motion_eps)
+                                      / np.float32(1.0 + norm))
+            ds[r] = u[D:D + C]
+        return dx, ds.reshape(-1)
+
+    def step(self, positions, states, batch_size: int, particle_count: int,
+             grid: HashGridConfig, dt: float, update_mask=None) -> StepOutput:
+        """NpaModel::step_cpu (model.rs:768-858), executed on the GPU."""
+        pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+        st = _f32(states).reshape(-1)
+        total = batch_size * particle_count
+        C = self.config.state_dims
+        mask = _f32(update_mask).reshape(-1) if update_mask is not None else None
+        npos = np.zeros((max(total, 0), 4), np.float32)
+        nst = np.zeros(max(total * C, 0), np.float32)
+        dx = np.zeros((max(total, 0), 4), np.float32)
+        ds = np.zeros(max(total * C, 0), np.float32)
+        F = self.config.perception_dims()
+        feats = np.zeros(max(total * F, 0), np.float32)
+        dens = np.zeros(max(total, 0), np.float32)
+        g = _lib.grid_c(grid)
+        _lib.check(_lib.lib().npa_model_step(
+            self._handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
+            batch_size, particle_count, float(dt), _fp(mask), _fp(npos), _fp(nst), _fp(dx),
+            _fp(ds), _fp(feats), _fp(dens)), "step")
+        return StepOutput(npos, nst, dx, ds, feats, dens)
+
+    # step_cpu is the reference's name for the same operation.
+    step_cpu = step
+
+
+@dataclass
+class RolloutConfig:
+    """rollout/mod.rs:102-124 (seeding fields are unused: inputs are given)."""
+
+    batch_size: int = 1
+    particle_count: int = 4096
+    steps: int = 32
+    dt: float = 1.0
+    update_prob: float = 1.0
+    seed: int = 42
+    seed_scale: float = 0.2
+
+
+@dataclass
+class RolloutTrace:
+    """rollout/mod.rs:146-155 (mean_dx is not recorded on the device path)."""
+
+    positions: np.ndarray
+    states: np.ndarray
+    batch_size: int
+    particle_count: int
+    state_dims: int
+    steps: int
+
+
+def run_rollout_from_particles(model: NpaModel, grid: HashGridConfig, cfg: RolloutConfig,
+                               positions, states) -> RolloutTrace:
+    """rollout/mod.rs:201-283 for update_prob >= 1 (the all-ones mask).  The
+    reference's stochastic masks draw from Rust's StdRng and are not
+    reproducible here, so update_prob < 1 is rejected."""
+    if cfg.update_prob < 1.0:
+        raise InvalidArgument("update_prob < 1 needs the reference's StdRng mask stream")
+    pos = _f32(positions).reshape(-1, 4).copy()
+    st = _f32(states).reshape(-1).copy()
+    g = _lib.grid_c(grid)
+    _lib.check(_lib.lib().npa_model_run_rollout(
+        model.handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
+        cfg.batch_size, cfg.particle_count, cfg.steps, float(cfg.dt)), "run_rollout")
+    return RolloutTrace(pos, st, cfg.batch_size, cfg.particle_count, model.config.state_dims,
+                        cfg.steps)
+
+
+class CudaAutomataExecutor:
+    """Resident rollout state on one GPU (the CUDA counterpart of WgpuAutomataExecutor)."""
+
+    def __init__(self, model: NpaModel, grid: HashGridConfig, batch_size: int,
+                 particle_count: int):
+        self.model = model
+        self.grid = grid
+        self.batch_size = batch_size
+        self.particle_count = particle_count
+        h = ctypes.c_void_p()
+        g = _lib.grid_c(grid)
+        _lib.check(_lib.lib().npa_executor_create(model.handle, ctypes.byref(g), batch_size,
+                                                  particle_count, ctypes.byref(h)), "executor")
+        self._handle = h
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            _lib.lib().npa_executor_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def create_state(self, positions, states) -> None:
+        pos = _f32(positions).reshape(-1, 4)
+        st = _f32(states).reshape(-1)
+        _lib.check(_lib.lib().npa_executor_upload_state(self._handle, _fp(pos), _fp(st)),
+                   "create_state")
+
+    def set_state_device(self, d_positions, d_states, stream=None) -> None:
+        _lib.check(_lib.lib().npa_executor_set_state_device(
+            self._handle, d_positions.data_ptr(), d_states.data_ptr(), stream), "set_state")
+
+    def step_state_many(self, steps: int, dt: float, use_graph: bool = True, stream=None) -> None:
+        _lib.check(_lib.lib().npa_executor_step_many(self._handle, int(steps), float(dt),
+                                                     1 if use_graph else 0, stream),
+                   "step_state_many")
+
+    def step_state_many_profiled(self, steps: int, dt: float, use_graph: bool = True,
+                                 stream=None):
+        """step_state_many with CUDA events around every phase of every step.
+        Returns (phase_ms [steps, 3] for hashgrid / density / fused step, total_ms)."""
+        phase = np.zeros((int(steps), 3), np.float32)
+        total = ctypes.c_float(0.0)
+        _lib.check(_lib.lib().npa_executor_step_many_profiled(
+            self._handle, int(steps), float(dt), 1 if use_graph else 0, stream, _fp(phase),
+            ctypes.byref(total)), "step_state_many_profiled")
+        return phase, float(total.value)
+
+    def read_state(self):
+        total = self.batch_size * self.particle_count
+        pos = np.zeros((total, 4), np.float32)
+        st = np.zeros(total * self.model.config.state_dims, np.float32)
+        _lib.check(_lib.lib().npa_executor_read_state(self._handle, _fp(pos), _fp(st)),
+                   "read_state")
+        return pos, st
+
+    def state_device_ptrs(self):
+        p, s = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(_lib.lib().npa_executor_state_device(self._handle, ctypes.byref(p),
+                                                        ctypes.byref(s)), "state_device")
+        return p.value, s.value
+
+    def launches_per_step(self) -> int:
+        v = ctypes.c_int64(0)
+        _lib.check(_lib.lib().npa_executor_launches_per_step(self._handle, ctypes.byref(v)),
+                   "launches_per_step")
+        return v.value

@@ -1,0 +1,332 @@
+/*
+ * npa_b200.h -- C ABI of the B200 (sm_100a) implementation of the
+ * burn_automata Neural Particle Automata rollout path.
+ *
+ * The entry points replace the CPU operators of crates/burn_automata_kernels
+ * and the step / rollout of crates/burn_automata (mosure/burn_automata); each
+ * declaration cites the Rust item it stands in for.  A Rust host binds them
+ * with `extern "C"` declarations of the same signatures.
+ *
+ * Conventions
+ *  - Plain pointers and sizes; no framework types.  Lengths are element
+ *    counts (positions are counted in [f32; 4] records, like the Rust slices).
+ *  - The caller owns every output buffer.  An output whose length does not
+ *    match returns NPA_ERR_OUTPUT_SHAPE instead of being reallocated (the Rust
+ *    API returns a fresh Vec; KernelError::OutputShape, config.rs:133).
+ *  - Index outputs are uint32 (the Rust API uses usize; a binding widens).
+ *  - Host-buffer entry points (npa_*) copy in, compute on the current CUDA
+ *    device (or the model's device) and copy out before returning.
+ *  - Device entry points (npa_dev_*) take device pointers, enqueue on the
+ *    given cudaStream_t (passed as void*) and return without synchronising;
+ *    they allocate nothing: scratch comes from the caller's workspace, sized by
+ *    the matching *_workspace_size query.
+ *  - Arithmetic follows the reference's f32 operation order: no FMA
+ *    contraction, sequential sums in the reference's loop order, IEEE division
+ *    and square root.  log1p is correctly rounded (the reference calls the host
+ *    libm's log1pf, which is not).
+ *  - Every call returns an npa_status; nothing aborts the process.
+ */
+#ifndef NPA_B200_H
+#define NPA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NPA_ABI_VERSION 1
+
+/* Status codes.  1..8 mirror KernelError (crates/burn_automata_kernels/src/
+ * config.rs:101-137); 9 mirrors AutomataError::InvalidModel
+ * (crates/burn_automata/src/error.rs). */
+typedef int32_t npa_status;
+enum {
+  NPA_OK = 0,
+  NPA_ERR_INVALID_DIM = 1,                   /* KernelError::InvalidDim */
+  NPA_ERR_INVALID_EPS = 2,                   /* KernelError::InvalidEps */
+  NPA_ERR_INVALID_GRID_SIZE = 3,             /* KernelError::InvalidGridSize */
+  NPA_ERR_PARTICLE_MODE_REQUIRES_POW2 = 4,   /* KernelError::ParticleModeRequiresPowerOfTwo */
+  NPA_ERR_POSITION_SHAPE = 5,                /* KernelError::PositionShape */
+  NPA_ERR_STATE_SHAPE = 6,                   /* KernelError::StateShape */
+  NPA_ERR_OUTPUT_SHAPE = 7,                  /* KernelError::OutputShape */
+  NPA_ERR_INVALID_ARGUMENT = 8,              /* KernelError / AutomataError::InvalidArgument */
+  NPA_ERR_INVALID_MODEL = 9,                 /* AutomataError::InvalidModel */
+  NPA_ERR_CUDA = 20,                         /* a CUDA runtime call failed */
+  NPA_ERR_DEVICE_STATUS = 21,                /* a kernel flagged an error in its status word */
+  NPA_ERR_TIMEOUT = 22,                      /* a bounded device-side wait gave up */
+  NPA_ERR_OUT_OF_MEMORY = 23,                /* an allocation failed (or hit the cap) */
+  NPA_ERR_UNSUPPORTED = 24,                  /* shape outside what the kernels support */
+  NPA_ERR_NO_DEVICE = 25                     /* no CUDA device is usable */
+};
+
+/* Boundary (config.rs:6-10) and HashGridMode (config.rs:14-18). */
+enum { NPA_BOUNDARY_PERIODIC = 0, NPA_BOUNDARY_CLAMPED = 1 };
+enum { NPA_MODE_GRID = 0, NPA_MODE_PARTICLE = 1 };
+
+/* HashGridConfig (crates/burn_automata_kernels/src/config.rs:20-29). */
+typedef struct npa_grid_config {
+  int32_t dim;                     /* 2 or 3 */
+  int32_t boundary;                /* NPA_BOUNDARY_* */
+  int32_t mode;                    /* NPA_MODE_* */
+  int32_t max_particles_per_block; /* carried for parity; unused by the step */
+  int64_t grid_size[3];
+  float eps;
+  int32_t reserved;
+} npa_grid_config;
+
+/* PerceptionOptions (crates/burn_automata_kernels/src/reference/types.rs:4-15). */
+typedef struct npa_perception_options {
+  uint8_t state_grad;
+  uint8_t density_grad;
+  uint8_t scale_equivariance;
+  uint8_t particle_density_equivariance;
+  uint8_t log_norm_grad;
+  uint8_t log_norm_density_grad;
+  uint8_t hybrid_state_gradient;
+  uint8_t position_features;
+  float eps0;
+  int32_t reserved;
+} npa_perception_options;
+
+/* EquivarianceMode (crates/burn_automata/src/config.rs:22-28). */
+enum { NPA_EQUIV_NONE = 0, NPA_EQUIV_PARTICLE_DENSITY = 1, NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE = 2 };
+
+/* NpaConfig fields read by NpaModel::step_cpu (crates/burn_automata/src/config.rs:30-53). */
+typedef struct npa_model_config {
+  int32_t spatial_dims;
+  int32_t state_dims;
+  int32_t hidden_dims;
+  int32_t auxiliary_input_dims;    /* must be 0: step_cpu has no auxiliary inputs */
+  float eps0;
+  float alpha;
+  int32_t equivariance;            /* NPA_EQUIV_* */
+  uint8_t density_grad;
+  uint8_t state_grad;
+  uint8_t log_norm_grad;
+  uint8_t log_norm_density_grad;
+  uint8_t position_features;
+  uint8_t reserved[7];
+} npa_model_config;
+
+/* GaussianDecodeMode (crates/burn_automata_kernels/src/gaussian.rs:13-21). */
+enum {
+  NPA_DECODE_PARTICLE_POINT = 0,
+  NPA_DECODE_SH0_FIXED_SCALE = 1,
+  NPA_DECODE_SH0_LEARNED_SCALE = 2,
+  NPA_DECODE_SH0_ORIENTED = 3
+};
+
+/* GaussianDecodeConfig (crates/burn_automata_kernels/src/gaussian.rs:23-35). */
+typedef struct npa_gaussian_decode_config {
+  int32_t mode;
+  int32_t sh_degree;
+  float sigma;
+  float min_scale;
+  float max_scale;
+  float max_anisotropy;
+  float opacity_scale;
+  float min_opacity;
+  float max_opacity;
+  int32_t reserved;
+} npa_gaussian_decode_config;
+
+/* ------------------------------------------------------------------ */
+/* Library                                                             */
+/* ------------------------------------------------------------------ */
+
+int32_t npa_abi_version(void);
+const char* npa_status_string(npa_status status);
+/* Text of the last error on the calling thread (CUDA message, failing shape). */
+const char* npa_last_error_message(void);
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t npa_kernel_launch_count(void);
+
+/* HashGridConfig::validate (config.rs:65-84). */
+npa_status npa_grid_validate(const npa_grid_config* cfg);
+/* HashGridConfig::cell_count (config.rs:86-88). */
+npa_status npa_grid_cell_count(const npa_grid_config* cfg, int64_t* cell_count);
+/* Feature row width, forward.rs:100-103. */
+npa_status npa_feature_dims(const npa_grid_config* cfg, const npa_perception_options* options,
+                            int64_t state_dims, int64_t* feature_dims);
+/* Floats per decoded Gaussian record: [position_visibility 4][rotation 4]
+ * [scale_opacity 4][spherical_harmonic 3*k], k = (sh_degree+1)^2 for
+ * GaussianSh0Oriented, else 1. */
+npa_status npa_gaussian_record_floats(const npa_gaussian_decode_config* cfg, int64_t* floats);
+
+/* ------------------------------------------------------------------ */
+/* Host-buffer operators (drop-in for crates/burn_automata_kernels)    */
+/* ------------------------------------------------------------------ */
+
+/* build_hashgrid (crates/burn_automata_kernels/src/hashgrid.rs:16-69).
+ * positions: positions_len records of [f32; 4]; must equal batch*n.
+ * bin_offsets: batch*cell_count+1; permutation / inverse_permutation: batch*n
+ * local indices.  Bit-exact with the reference, including the stable
+ * ascending order of particles inside a cell. */
+npa_status npa_build_hashgrid(const npa_grid_config* cfg, const float* positions,
+                              int64_t positions_len, int64_t batch, int64_t n,
+                              uint32_t* bin_offsets, int64_t bin_offsets_len,
+                              uint32_t* permutation, uint32_t* inverse_permutation,
+                              int64_t permutation_len);
+
+/* perceive_with_options (crates/burn_automata_kernels/src/reference/forward.rs:26-143).
+ * features: batch*n*feature_dims (required).  density (batch*n), blurred_state
+ * (batch*n*c), state_gradient (batch*n*c*dim, only if state_grad) and
+ * density_gradient (batch*n*dim, only if density_grad) may be NULL. */
+npa_status npa_perceive_with_options(const npa_grid_config* cfg,
+                                     const npa_perception_options* options,
+                                     const float* positions, int64_t positions_len,
+                                     const float* states, int64_t states_len, int64_t batch,
+                                     int64_t n, int64_t state_dims, float* features,
+                                     int64_t features_len, float* density, float* blurred_state,
+                                     float* state_gradient, float* density_gradient);
+
+/* euler_step (crates/burn_automata_kernels/src/reference/step.rs:4-55).
+ * dx: [f32; 4] records; update_mask may be NULL (all ones). */
+npa_status npa_euler_step(const npa_grid_config* cfg, const float* positions,
+                          int64_t positions_len, const float* states, int64_t states_len,
+                          const float* dx, int64_t dx_len, const float* ds, int64_t ds_len,
+                          int64_t batch, int64_t n, int64_t state_dims, float dt,
+                          const float* update_mask, float* next_positions, float* next_states);
+
+/* decode_gaussians_3d (crates/burn_automata_kernels/src/gaussian.rs:53-100).
+ * out: count * npa_gaussian_record_floats floats.  A state layout too small for
+ * the mode returns NPA_ERR_STATE_SHAPE (the reference panics, gaussian.rs:102-125). */
+npa_status npa_decode_gaussians_3d(const npa_gaussian_decode_config* cfg, const float* positions,
+                                   int64_t positions_len, const float* states,
+                                   int64_t states_len, int64_t state_dims, float* out,
+                                   int64_t out_len);
+
+/* ------------------------------------------------------------------ */
+/* Model: NpaModel (crates/burn_automata/src/model.rs)                 */
+/* ------------------------------------------------------------------ */
+
+typedef struct npa_model npa_model;
+
+/* NpaModel { config, weights } with weights resident on `device`.
+ * w1 [hidden, perception_dims] row-major, b1 [hidden], w2 [update_dims, hidden],
+ * b2 [update_dims] (NpaWeights, model.rs:11-17; checked like
+ * NpaWeights::validate, model.rs:77-107). */
+npa_status npa_model_create(const npa_model_config* cfg, const float* w1, int64_t w1_len,
+                            const float* b1, int64_t b1_len, const float* w2, int64_t w2_len,
+                            const float* b2, int64_t b2_len, int32_t device, npa_model** out);
+void npa_model_destroy(npa_model* model);
+
+/* NpaModel::forward_update_from_features (model.rs:900-940); update: rows*update_dims. */
+npa_status npa_model_forward_update_from_features(npa_model* model, const float* features,
+                                                  int64_t features_len, float* update,
+                                                  int64_t update_len);
+
+/* NpaModel::step_cpu (model.rs:768-858).  update_mask, dx ([f32;4] records),
+ * ds, features and density may be NULL. */
+npa_status npa_model_step(npa_model* model, const npa_grid_config* grid, const float* positions,
+                          int64_t positions_len, const float* states, int64_t states_len,
+                          int64_t batch, int64_t n, float dt, const float* update_mask,
+                          float* next_positions, float* next_states, float* dx, float* ds,
+                          float* features, float* density);
+
+/* run_rollout_from_particles (crates/burn_automata/src/rollout/mod.rs:201-283)
+ * with update_prob >= 1: `steps` steps, positions / states updated in place. */
+npa_status npa_model_run_rollout(npa_model* model, const npa_grid_config* grid, float* positions,
+                                 int64_t positions_len, float* states, int64_t states_len,
+                                 int64_t batch, int64_t n, int64_t steps, float dt);
+
+/* ------------------------------------------------------------------ */
+/* Device operators (caller-owned device buffers, async on a stream)   */
+/* ------------------------------------------------------------------ */
+
+/* Workspace bytes needed by npa_dev_build_hashgrid. */
+npa_status npa_dev_hashgrid_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,
+                                           size_t* bytes);
+/* build_hashgrid on device buffers (hashgrid.rs:16-69). */
+npa_status npa_dev_build_hashgrid(const npa_grid_config* cfg, const float* d_positions,
+                                  int64_t batch, int64_t n, uint32_t* d_bin_offsets,
+                                  uint32_t* d_permutation, uint32_t* d_inverse_permutation,
+                                  void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes needed by npa_dev_perceive_with_options. */
+npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,
+                                           int64_t state_dims, size_t* bytes);
+/* perceive_with_options on device buffers (forward.rs:26-143).  Same optional
+ * outputs as the host variant. */
+npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
+                                         const npa_perception_options* options,
+                                         const float* d_positions, const float* d_states,
+                                         int64_t batch, int64_t n, int64_t state_dims,
+                                         float* d_features, float* d_density,
+                                         float* d_blurred_state, float* d_state_gradient,
+                                         float* d_density_gradient, void* d_workspace,
+                                         size_t workspace_bytes, void* stream);
+
+/* forward_update_from_features on device buffers (model.rs:900-940). */
+npa_status npa_dev_model_forward_update(npa_model* model, const float* d_features, int64_t rows,
+                                        float* d_update, void* stream);
+
+/* euler_step on device buffers (step.rs:4-55). */
+npa_status npa_dev_euler_step(const npa_grid_config* cfg, const float* d_positions,
+                              const float* d_states, const float* d_dx, const float* d_ds,
+                              int64_t batch, int64_t n, int64_t state_dims, float dt,
+                              const float* d_update_mask, float* d_next_positions,
+                              float* d_next_states, void* stream);
+
+/* decode_gaussians_3d on device buffers (gaussian.rs:53-100). */
+npa_status npa_dev_decode_gaussians_3d(const npa_gaussian_decode_config* cfg,
+                                       const float* d_positions, const float* d_states,
+                                       int64_t count, int64_t state_dims, float* d_out,
+                                       void* stream);
+
+/* Workspace bytes needed by npa_dev_model_step. */
+npa_status npa_dev_step_workspace_size(npa_model* model, const npa_grid_config* grid,
+                                       int64_t batch, int64_t n, size_t* bytes);
+/* NpaModel::step_cpu on device buffers (model.rs:768-858): hashgrid, density,
+ * then one fused kernel for perception + MLP + dx/ds + Euler.  Optional
+ * outputs (d_update_mask, d_dx, d_ds, d_features, d_density) may be NULL. */
+npa_status npa_dev_model_step(npa_model* model, const npa_grid_config* grid,
+                              const float* d_positions, const float* d_states, int64_t batch,
+                              int64_t n, float dt, const float* d_update_mask,
+                              float* d_next_positions, float* d_next_states, float* d_dx,
+                              float* d_ds, float* d_features, float* d_density,
+                              void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Executor: resident rollout state (the CUDA counterpart of            */
+/* WgpuAutomataExecutor, crates/burn_automata/src/gpu/executor/*)      */
+/* ------------------------------------------------------------------ */
+
+typedef struct npa_executor npa_executor;
+
+/* create_state (executor/state.rs:6-82): device buffers for batch*n particles
+ * of the model's state width, on the model's device. */
+npa_status npa_executor_create(npa_model* model, const npa_grid_config* grid, int64_t batch,
+                               int64_t n, npa_executor** out);
+void npa_executor_destroy(npa_executor* exec);
+/* Upload host state (blocking). */
+npa_status npa_executor_upload_state(npa_executor* exec, const float* positions,
+                                     const float* states);
+/* Copy state from device buffers of the same shape (async on stream). */
+npa_status npa_executor_set_state_device(npa_executor* exec, const float* d_positions,
+                                         const float* d_states, void* stream);
+/* step_state_many (executor/steps.rs:25): `steps` rollout steps on `stream`.
+ * With use_graph != 0 the step sequence is captured once into a CUDA graph
+ * and replayed. */
+npa_status npa_executor_step_many(npa_executor* exec, int64_t steps, float dt, int32_t use_graph,
+                                  void* stream);
+/* step_state_many with CUDA events recorded on `stream` around each phase of
+ * each step: phase_ms receives steps*3 durations (hashgrid, density, fused
+ * perception+MLP+Euler) and total_ms the whole span.  Synchronises `stream`. */
+npa_status npa_executor_step_many_profiled(npa_executor* exec, int64_t steps, float dt,
+                                           int32_t use_graph, void* stream, float* phase_ms,
+                                           float* total_ms);
+/* read_state (executor/readback.rs:85): synchronises and copies to host. */
+npa_status npa_executor_read_state(npa_executor* exec, float* positions, float* states);
+/* Current resident device buffers ([f32;4] positions, states). */
+npa_status npa_executor_state_device(npa_executor* exec, float** d_positions, float** d_states);
+/* Kernels launched per rollout step by this executor. */
+npa_status npa_executor_launches_per_step(npa_executor* exec, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NPA_B200_H */

@@ -1,0 +1,168 @@
+/*
+ * npa_oracle.h -- CPU restatement of the burn_automata NPA rollout path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA
+ * product in burn_automata_b200/.  Only tests/, __graft_entry__.smoke() and the
+ * CPU-baseline legs of bench.py may load it.  The product never links, calls
+ * or falls back to it.
+ *
+ * It restates, in plain C with the reference's f32 operation order (no FMA
+ * contraction, left-to-right sums, binary-exponentiation powi), these files of
+ * mosure/burn_automata:
+ *   crates/burn_automata_kernels/src/config.rs          (HashGridConfig::validate)
+ *   crates/burn_automata_kernels/src/hashgrid.rs        (build_hashgrid, cell math)
+ *   crates/burn_automata_kernels/src/reference/{forward,neighbor,kernels,normalize,step}.rs
+ *   crates/burn_automata_kernels/src/gaussian.rs        (decode_gaussians_3d)
+ *   crates/burn_automata/src/config.rs:133-162          (NpaConfig dims / eps)
+ *   crates/burn_automata/src/model.rs:768-940           (step_cpu, MLP)
+ *   crates/burn_automata/src/rollout/mod.rs:240-283     (rollout loop)
+ * Each function in npa_oracle.c cites the file:line it follows.
+ *
+ * Index arrays are int64 (the reference uses usize).  Status codes are the
+ * same numbers the product's C ABI uses (include/npa_b200.h).
+ */
+#ifndef NPA_ORACLE_H
+#define NPA_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ORA_OK = 0,
+  ORA_ERR_INVALID_DIM = 1,
+  ORA_ERR_INVALID_EPS = 2,
+  ORA_ERR_INVALID_GRID_SIZE = 3,
+  ORA_ERR_PARTICLE_MODE_REQUIRES_POW2 = 4,
+  ORA_ERR_POSITION_SHAPE = 5,
+  ORA_ERR_STATE_SHAPE = 6,
+  ORA_ERR_OUTPUT_SHAPE = 7,
+  ORA_ERR_INVALID_ARGUMENT = 8,
+  ORA_ERR_INVALID_MODEL = 9,
+};
+
+/* Same layout as npa_grid_config in include/npa_b200.h. */
+typedef struct ora_grid_config {
+  int32_t dim;       /* 2 or 3 */
+  int32_t boundary;  /* 0 = Periodic, 1 = Clamped */
+  int32_t mode;      /* 0 = Grid, 1 = Particle */
+  int32_t max_particles_per_block;
+  int64_t grid_size[3];
+  float eps;
+  int32_t reserved;
+} ora_grid_config;
+
+/* Same layout as npa_perception_options. */
+typedef struct ora_perception_options {
+  uint8_t state_grad;
+  uint8_t density_grad;
+  uint8_t scale_equivariance;
+  uint8_t particle_density_equivariance;
+  uint8_t log_norm_grad;
+  uint8_t log_norm_density_grad;
+  uint8_t hybrid_state_gradient;
+  uint8_t position_features;
+  float eps0;
+  int32_t reserved;
+} ora_perception_options;
+
+/* Same layout as npa_model_config. equivariance: 0 None, 1 ParticleDensity,
+ * 2 ParticleDensityAndScale. */
+typedef struct ora_model_config {
+  int32_t spatial_dims;
+  int32_t state_dims;
+  int32_t hidden_dims;
+  int32_t auxiliary_input_dims;
+  float eps0;
+  float alpha;
+  int32_t equivariance;
+  uint8_t density_grad;
+  uint8_t state_grad;
+  uint8_t log_norm_grad;
+  uint8_t log_norm_density_grad;
+  uint8_t position_features;
+  uint8_t reserved[7];
+} ora_model_config;
+
+/* Same layout as npa_gaussian_decode_config. mode: 0 ParticlePoint,
+ * 1 GaussianSh0FixedScale, 2 GaussianSh0LearnedScale, 3 GaussianSh0Oriented. */
+typedef struct ora_decode_config {
+  int32_t mode;
+  int32_t sh_degree;
+  float sigma;
+  float min_scale;
+  float max_scale;
+  float max_anisotropy;
+  float opacity_scale;
+  float min_opacity;
+  float max_opacity;
+  int32_t reserved;
+} ora_decode_config;
+
+int ora_grid_validate(const ora_grid_config* cfg);
+int64_t ora_cell_count(const ora_grid_config* cfg);
+/* cell index of one position (hashgrid.rs:71 cell_for_position). */
+int64_t ora_cell_for_position(const ora_grid_config* cfg, const float* pos4);
+
+int ora_build_hashgrid(const ora_grid_config* cfg, const float* positions,
+                       int64_t batch, int64_t n, int64_t* bin_offsets,
+                       int64_t* permutation, int64_t* inverse_permutation);
+
+int64_t ora_feature_dims(const ora_grid_config* cfg, const ora_perception_options* opt,
+                         int64_t state_dims);
+
+/* perceive_with_options.  Every output pointer may be NULL except features. */
+int ora_perceive(const ora_grid_config* cfg, const ora_perception_options* opt,
+                 const float* positions, const float* states, int64_t batch,
+                 int64_t n, int64_t state_dims, float* features, float* density,
+                 float* blurred_state, float* state_gradient,
+                 float* density_gradient);
+
+int ora_forward_update(const float* features, int64_t rows, int64_t in_dims,
+                       int64_t hidden_dims, int64_t out_dims, const float* w1,
+                       const float* b1, const float* w2, const float* b2,
+                       float* update);
+
+int ora_euler_step(const ora_grid_config* cfg, const float* positions,
+                   const float* states, const float* dx, const float* ds,
+                   int64_t batch, int64_t n, int64_t state_dims, float dt,
+                   const float* update_mask, float* next_positions,
+                   float* next_states);
+
+int64_t ora_model_perception_dims(const ora_model_config* m);
+
+/* NpaModel::step_cpu.  features/density/dx/ds outputs may be NULL. */
+int ora_step(const ora_model_config* m, const float* w1, const float* b1,
+             const float* w2, const float* b2, const ora_grid_config* grid,
+             const float* positions, const float* states, int64_t batch,
+             int64_t n, float dt, const float* update_mask,
+             float* next_positions, float* next_states, float* dx, float* ds,
+             float* features, float* density);
+
+/* run_rollout_from_particles with update_prob >= 1 (mask of ones) or a fixed
+ * per-step mask callback-free variant: masks == NULL means all ones,
+ * otherwise masks holds steps * batch * n values.  positions/states are
+ * updated in place; mean_dx (may be NULL) receives one value per step. */
+int ora_rollout(const ora_model_config* m, const float* w1, const float* b1,
+                const float* w2, const float* b2, const ora_grid_config* grid,
+                float* positions, float* states, int64_t batch, int64_t n,
+                int64_t steps, float dt, const float* masks, float* mean_dx);
+
+int64_t ora_gaussian_record_floats(const ora_decode_config* cfg);
+/* decode_gaussians_3d; record layout per particle:
+ * [position_visibility 4][rotation 4][scale_opacity 4][sh 3*k]. */
+int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
+                         const float* states, int64_t count, int64_t state_dims,
+                         float* out);
+
+/* Threads used by the OpenMP loops (0 = OpenMP default). */
+void ora_set_threads(int threads);
+int ora_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,299 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Bars, from the path's parity contract:
+  - hashgrid (bin_offsets, permutation, inverse_permutation): bit-exact;
+  - per-step perception, MLP output and decoded Gaussians: within
+    rtol 1e-5 / atol 1e-6 (np.allclose);
+  - final state after 64 steps: within 1e-3 relative (normwise, since the
+    rollout is chaotic).
+The device arithmetic follows the reference's f32 operation order, so the
+only sources of difference are log1p (correctly rounded on the device, the host
+libm's log1pf on the oracle side) and exp/tanh in the decode.  With log
+normalisation switched off the step is therefore checked for bit equality.
+"""
+
+import numpy as np
+import pytest
+
+import burn_automata_b200 as ba
+from burn_automata_b200 import workloads
+from burn_automata_b200.config import (Boundary, GaussianDecodeConfig, GaussianDecodeMode,
+                                       HashGridConfig, HashGridMode, NpaConfig,
+                                       PerceptionOptions)
+from burn_automata_b200.model import NpaModel, NpaWeights
+from tests.golden_cases import CASES, load_case
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def assert_hashgrid_equal(oracle_mod, pos, batch, n, grid):
+    snap = ba.build_hashgrid(pos, batch, n, grid)
+    off, perm, inv = oracle_mod.build_hashgrid(pos, batch, n, grid)
+    np.testing.assert_array_equal(snap.bin_offsets.astype(np.int64), off)
+    np.testing.assert_array_equal(snap.permutation.astype(np.int64), perm)
+    np.testing.assert_array_equal(snap.inverse_permutation.astype(np.int64), inv)
+    return snap
+
+
+@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 8, 4096),
+                                          ("cfg3", 1, 16384), ("cfg1", 1, 1 << 16),
+                                          ("cfg4", 1, 1 << 16)])
+def test_hashgrid_bit_exact_on_configs(oracle_mod, name, batch, n):
+    w = workloads.make(name, batch=batch, n=n, steps=1)
+    assert_hashgrid_equal(oracle_mod, w.positions, w.batch, w.n, w.grid)
+
+
+def test_hashgrid_full_size_cfg1(oracle_mod):
+    w = workloads.make("cfg1")
+    assert_hashgrid_equal(oracle_mod, w.positions, w.batch, w.n, w.grid)
+
+
+def test_hashgrid_edge_cases(oracle_mod):
+    g2 = HashGridConfig.growing_2d()
+    # empty batch and empty rollouts
+    snap = ba.build_hashgrid(np.zeros((0, 4), np.float32), 3, 0, g2)
+    assert np.all(snap.bin_offsets == 0) and snap.bin_offsets.shape[0] == 3 * 4096 + 1
+    # one particle
+    assert_hashgrid_equal(oracle_mod, np.array([[0.3, -0.2, 0, 0]], np.float32), 1, 1, g2)
+    # every particle in one cell (ties resolved by index)
+    same = np.tile(np.array([[0.01, 0.02, 0, 0]], np.float32), (5000, 1))
+    assert_hashgrid_equal(oracle_mod, same, 2, 2500, g2)
+    # far outside the domain, negative coordinates, huge values and NaN
+    rng = np.random.default_rng(3)
+    wild = np.zeros((4096, 4), np.float32)
+    wild[:, :2] = rng.uniform(-1e6, 1e6, size=(4096, 2))
+    wild[:10, 0] = [np.nan, np.inf, -np.inf, 3e38, -3e38, 1e20, -1e20, 0.0, -0.0, 1e-40]
+    assert_hashgrid_equal(oracle_mod, wild, 1, 4096, g2)
+    # Grid mode, periodic and clamped, non power-of-two grids
+    for boundary in (Boundary.Periodic, Boundary.Clamped):
+        gg = HashGridConfig(2, boundary, HashGridMode.Grid, (10, 7, 1), 0.2, 32)
+        assert_hashgrid_equal(oracle_mod, wild, 4, 1024, gg)
+    g3 = HashGridConfig.growing_3dgs()
+    p3 = np.zeros((3000, 4), np.float32)
+    p3[:, :3] = rng.uniform(-2, 2, size=(3000, 3))
+    assert_hashgrid_equal(oracle_mod, p3, 3, 1000, g3)
+
+
+def perception_cases():
+    rng = np.random.default_rng(7)
+    cases = []
+    g = HashGridConfig.growing_2d().with_(eps=0.05, grid_size=(64, 64, 1))
+    pos = workloads.uniform_positions_2d(2048, 1, -0.5, 0.5)
+    for c in (1, 5, 16):
+        st = (rng.standard_normal(2048 * c) * 0.3).astype(np.float32)
+        for opt in (PerceptionOptions.new(True, True, 0.1),
+                    NpaConfig.growing_2d().perception_options(),
+                    NpaConfig.growing_2d().with_(density_grad=False).perception_options(),
+                    PerceptionOptions(state_grad=False, density_grad=True, eps0=0.07,
+                                      position_features=True),
+                    PerceptionOptions(state_grad=True, density_grad=False, hybrid_state_gradient=False,
+                                      scale_equivariance=False, eps0=0.2)):
+            cases.append((f"2d_c{c}", g, pos, st, 2, 1024, c, opt))
+    gp = HashGridConfig(2, Boundary.Periodic, HashGridMode.Grid, (10, 10, 1), 0.2, 32)
+    pp = workloads.uniform_positions_2d(1500, 2, -1.0, 1.0)
+    sp = (rng.standard_normal(1500 * 4) * 0.3).astype(np.float32)
+    cases.append(("periodic_grid", gp, pp, sp, 1, 1500, 4, NpaConfig.texture_2d().perception_options()))
+    g3 = HashGridConfig.growing_3dgs().with_(eps=0.1)
+    p3 = workloads.torus_positions(3000, 4)
+    for c in (8, 32):
+        s3 = (rng.standard_normal(3000 * c) * 0.3).astype(np.float32)
+        cases.append((f"3d_c{c}", g3, p3, s3, 1, 3000, c, NpaConfig.growing_3dgs().perception_options()))
+    return cases
+
+
+@pytest.mark.parametrize("case", perception_cases(), ids=lambda c: c[0])
+def test_perception_parity(oracle_mod, case):
+    _, grid, pos, st, batch, n, c, opt = case
+    gpu = ba.perceive_with_options(pos, st, batch, n, c, grid, opt)
+    ref = oracle_mod.perceive_with_options(pos, st, batch, n, c, grid, opt)
+    np.testing.assert_array_equal(gpu.density, ref["density"])
+    np.testing.assert_array_equal(gpu.blurred_state, ref["blurred_state"])
+    exact_keys = [] if (opt.log_norm_grad or opt.log_norm_density_grad) else ["features"]
+    for key in ("features", "state_gradient", "density_gradient"):
+        a, b = getattr(gpu, key), ref[key]
+        np.testing.assert_allclose(a, b, rtol=RTOL, atol=ATOL, err_msg=key)
+        if key in exact_keys:
+            np.testing.assert_array_equal(a, b)
+
+
+def test_mlp_bit_exact(oracle_mod):
+    for (f, h, o) in ((64, 128, 18), (160, 256, 35), (13, 5, 3), (130, 100, 34)):
+        cfg = NpaConfig(spatial_dims=2, state_dims=o - 2, hidden_dims=h)
+        # pick a feature width by toggling options until it matches f
+        rng = np.random.default_rng(f + h)
+        rows = 1000
+        feats = rng.standard_normal(rows * cfg.perception_dims()).astype(np.float32)
+        w = NpaWeights(
+            (rng.standard_normal(h * cfg.perception_dims()) * 0.2).astype(np.float32),
+            (rng.standard_normal(h) * 0.1).astype(np.float32),
+            (rng.standard_normal(cfg.update_dims() * h) * 0.2).astype(np.float32),
+            (rng.standard_normal(cfg.update_dims()) * 0.1).astype(np.float32))
+        model = NpaModel(cfg, w)
+        gpu = model.forward_update_from_features(feats)
+        ref = oracle_mod.forward_update(feats, rows, cfg.perception_dims(), h, cfg.update_dims(),
+                                        w.w1, w.b1, w.w2, w.b2)
+        np.testing.assert_array_equal(gpu, ref)
+
+
+def test_euler_bit_exact(oracle_mod):
+    rng = np.random.default_rng(5)
+    for grid, c in ((HashGridConfig.growing_2d(), 16), (HashGridConfig.texture_2d(), 3),
+                    (HashGridConfig.growing_3dgs(), 12)):
+        n = 777
+        pos = rng.uniform(-2, 2, size=(n, 4)).astype(np.float32)
+        st = (rng.standard_normal(n * c) * 10).astype(np.float32)
+        dx = rng.standard_normal((n, 4)).astype(np.float32)
+        ds = (rng.standard_normal(n * c) * 10).astype(np.float32)
+        mask = (rng.uniform(size=n) < 0.5).astype(np.float32)
+        for m in (None, mask):
+            a = ba.euler_step(pos, st, dx, ds, 1, n, c, grid, 0.37, m)
+            b = oracle_mod.euler_step(pos, st, dx, ds, 1, n, c, grid, 0.37, m)
+            np.testing.assert_array_equal(a[0], b[0])
+            np.testing.assert_array_equal(a[1], b[1])
+
+
+def test_euler_kats_on_gpu():
+    from tests.test_oracle_kat import euler_mask_case
+
+    cfg, pos, st, dx, ds, mask = euler_mask_case()
+    npos, nst = ba.euler_step(pos, st, dx, ds, 1, 2, 1, cfg, 1.0, mask)
+    assert npos[0, 0] == 0.5 and npos[1, 0] == np.float32(0.9) and list(nst) == [1.0, 1.0]
+
+
+def test_sph_constants_on_gpu():
+    from tests.test_oracle_kat import check_sph_constants, sph_constants_case
+
+    cfg, pos, st = sph_constants_case()
+    out = ba.perceive(pos, st, 1, 2, 2, cfg, True, True)
+    check_sph_constants(out.density, out.blurred_state, out.state_gradient, out.density_gradient)
+
+
+@pytest.mark.parametrize("mode", list(GaussianDecodeMode))
+def test_decode_parity(oracle_mod, mode):
+    rng = np.random.default_rng(int(mode))
+    n, c = 5000, 32
+    pos = rng.standard_normal((n, 4)).astype(np.float32)
+    st = (rng.standard_normal(n * c) * 3).astype(np.float32)
+    for sh in ((0, 1, 2) if mode == GaussianDecodeMode.GaussianSh0Oriented else (0,)):
+        cfg = GaussianDecodeConfig(mode=mode, sh_degree=sh)
+        a = ba.decode_gaussians_3d_records(pos, st, c, cfg)
+        b = oracle_mod.decode_gaussians(pos, st, c, cfg)
+        np.testing.assert_allclose(a, b, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_gpu_matches_reference_python_golden(name):
+    z, grid, model = load_case(name)
+    n = z["n"]
+    out = ba.perceive_with_options(z["positions"], z["states"], 1, n, model.state_dims, grid,
+                                   model.perception_options())
+    np.testing.assert_allclose(out.features, z["features"], rtol=1e-4, atol=2e-5)
+    m = NpaModel(model, NpaWeights(z["w1"], z["b1"], z["w2"], z["b2"]))
+    st = m.step(z["positions"], z["states"], 1, n, grid, 1.0)
+    np.testing.assert_allclose(st.next_states, z["next_states"], rtol=1e-4, atol=2e-5)
+
+
+def make_model(w):
+    return NpaModel(w.model, NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2, w.weights.b2))
+
+
+@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg3", 1, 4096)])
+def test_step_parity(oracle_mod, name, batch, n):
+    w = workloads.make(name, batch=batch, n=n, steps=1)
+    m = make_model(w)
+    gpu = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, w.dt)
+    np.testing.assert_array_equal(gpu.density, ref["density"])
+    np.testing.assert_allclose(gpu.features, ref["features"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gpu.ds, ref["ds"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gpu.dx, ref["dx"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gpu.next_states, ref["next_states"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gpu.next_positions, ref["next_positions"], rtol=RTOL, atol=ATOL)
+
+
+def test_step_bit_exact_without_log_norm(oracle_mod):
+    w = workloads.make("cfg0", steps=1)
+    w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
+    m = make_model(w)
+    rng = np.random.default_rng(0)
+    mask = (rng.uniform(size=w.n) < 0.7).astype(np.float32)
+    gpu = m.step(w.positions, w.states, 1, w.n, w.grid, w.dt, mask)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, 1, w.n, w.dt, mask)
+    for key in ("features", "ds", "dx", "next_states", "next_positions", "density"):
+        np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
+
+
+def test_3d_position_gates(oracle_mod):
+    w = workloads.make("cfg3", n=2048, steps=1)
+    w.model = w.model.with_(position_features=True)
+    w.weights = workloads.kaiming_weights(w.model, 9)
+    pos = w.positions.copy()
+    pos[::3, 3] = 1.0  # anchored particles
+    st = w.states.reshape(-1, 32).copy()
+    st[:, 3] = np.linspace(2.0, 5.0, st.shape[0])  # liveness across the gate
+    st[:, 7] = np.linspace(-0.05, 0.05, st.shape[0])  # signed distance across the gate
+    m = make_model(w)
+    gpu = m.step(pos, st.reshape(-1), 1, w.n, w.grid, w.dt)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, pos, st.reshape(-1), 1, w.n, w.dt)
+    np.testing.assert_allclose(gpu.next_states, ref["next_states"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gpu.next_positions, ref["next_positions"], rtol=RTOL, atol=ATOL)
+
+
+def normwise(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def test_rollout_64_steps_cfg0(oracle_mod):
+    w = workloads.make("cfg0")
+    m = make_model(w)
+    trace = ba.run_rollout_from_particles(
+        m, w.grid, ba.RolloutConfig(batch_size=1, particle_count=w.n, steps=64, dt=w.dt),
+        w.positions, w.states)
+    pos, st, _ = oracle_mod.rollout(w.model, w.weights, w.grid, w.positions, w.states, 1, w.n,
+                                    64, w.dt)
+    assert normwise(trace.states, st) <= 1e-3
+    assert normwise(trace.positions, pos) <= 1e-3
+
+
+def test_rollout_64_steps_bit_exact_without_log_norm(oracle_mod):
+    w = workloads.make("cfg0")
+    w.model = w.model.with_(log_norm_grad=False)
+    m = make_model(w)
+    trace = ba.run_rollout_from_particles(
+        m, w.grid, ba.RolloutConfig(batch_size=1, particle_count=w.n, steps=64, dt=w.dt),
+        w.positions, w.states)
+    pos, st, _ = oracle_mod.rollout(w.model, w.weights, w.grid, w.positions, w.states, 1, w.n,
+                                    64, w.dt)
+    np.testing.assert_array_equal(trace.states, st)
+    np.testing.assert_array_equal(trace.positions, pos)
+
+
+def test_executor_graph_matches_eager():
+    import torch
+
+    w = workloads.make("cfg2", batch=4, steps=8)
+    m = make_model(w)
+    outs = []
+    for use_graph in (False, True):
+        ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
+        ex.create_state(w.positions, w.states)
+        s = torch.cuda.Stream()
+        ex.step_state_many(8, w.dt, use_graph=use_graph, stream=s.cuda_stream)
+        outs.append(ex.read_state())
+        ex.close()
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+def test_device_tensor_perception_matches_host():
+    import torch
+
+    w = workloads.make("cfg1", n=1 << 15, steps=1)
+    host = ba.perceive_with_options(w.positions, w.states, 1, w.n, 32, w.grid, w.options)
+    dev = ba.perceive_with_options(torch.from_numpy(w.positions).cuda(),
+                                   torch.from_numpy(w.states).cuda(), 1, w.n, 32, w.grid,
+                                   w.options)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dev.features.cpu().numpy(), host.features)
