@@ -223,8 +223,8 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=timedelta(seconds=180),
                                 device_id=torch.device("cuda", local_rank))
     lib = ba.load_library()
-    per_rank = BATCH_TOTAL // world if args.strong else BATCH_TOTAL
-    first = rank * per_rank if args.strong else rank * per_rank
+    per_rank = args.rollouts or (BATCH_TOTAL // world if args.strong else BATCH_TOTAL)
+    first = rank * per_rank
     w = workloads.make(args.workload, batch=per_rank, first=first)
     model = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
                                                w.weights.b2), device=local_rank)
@@ -355,6 +355,8 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=["cfg2"])
     ap.add_argument("--strong", action="store_true",
                     help="split the 256 rollouts over the ranks instead of 256 per rank")
+    ap.add_argument("--rollouts", type=int, default=None,
+                    help="rollouts per rank (default: 256, or 256 / ranks with --strong)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -32,14 +32,19 @@ struct GridParams {
   float spiky_norm;    // gradient_spiky_normalization (kernels.rs:136-142)
 };
 
-// `f as isize` then `as i32`: saturating conversion (NaN -> 0), low 32 bits kept.
-// cvt.rzi.s64.f32 saturates and maps NaN to 0, like Rust's `as`.
-__device__ __forceinline__ int f2i_low32(float integral) {
-  return static_cast<int>(static_cast<long long>(integral));
+// `f as isize`: saturating conversion with NaN -> 0 (Rust semantics).  The
+// hardware conversion maps NaN to INT64_MIN, so NaN and the range ends are
+// handled explicitly.
+__device__ __forceinline__ long long f2ll_sat(float integral) {
+  if (integral != integral) return 0;
+  if (integral >= 9223372036854775808.0f) return 0x7fffffffffffffffLL;
+  if (integral <= -9223372036854775808.0f) return static_cast<long long>(0x8000000000000000ULL);
+  return static_cast<long long>(integral);
 }
 
-__device__ __forceinline__ long long f2ll_sat(float integral) {
-  return static_cast<long long>(integral);
+// `f as isize as i32`: the saturated value's low 32 bits.
+__device__ __forceinline__ int f2i_low32(float integral) {
+  return static_cast<int>(static_cast<unsigned long long>(f2ll_sat(integral)) & 0xffffffffULL);
 }
 
 // mix_coord (hashgrid.rs:155-163).
