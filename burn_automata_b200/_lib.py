@@ -87,6 +87,8 @@ SIGNATURES = [
     ("npa_dev_hashgrid_workspace_size", c_i32, [P(GridConfigC), c_i64, c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_build_hashgrid", c_i32,
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp, ctypes.c_size_t, vp]),
+    ("npa_dev_build_hashgrid_noalloc", c_i32,
+     [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp]),
     ("npa_dev_perceive_workspace_size", c_i32,
      [P(GridConfigC), c_i64, c_i64, c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_perceive_with_options", c_i32,

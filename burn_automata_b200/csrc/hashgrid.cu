@@ -14,6 +14,8 @@
 // digit-major [256 x tiles] table, then a scatter that ranks items inside the
 // tile in index order (warp match_any + per-warp digit counters + a
 // cross-warp prefix).  No kernel waits on another block.
+#include <mutex>
+#include <string>
 #include <utility>
 
 #include "npa_internal.h"
@@ -278,4 +280,78 @@ npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_
   return after_launch("finalize_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// Hashgrid build that allocates nothing.
+//
+// Some callers cannot allocate device memory: a host that only holds buffers
+// handed to it by another framework's allocator (a Burn / CubeCL tensor, a
+// viewer's storage buffer) and owns no allocator of its own, or code that must
+// not call cudaMalloc because of its implicit device synchronisation (a
+// render or control loop with a latency budget).  For them the sort scratch
+// lives in this fixed device array instead of a caller workspace.  The array
+// exists once per device that loads the library and is held until exit, so it
+// is sized for a modest maximum of kStaticMaxParticles particles (~6.3 MB).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr uint32_t kStaticMaxParticles = 1u << 17;  // batch * n limit (131,072)
+constexpr size_t kStaticScratchBytes = size_t(6656) * 1024;  // 6.5 MiB
+
+__device__ __align__(256) unsigned char g_hashgrid_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void* g_static_ptr[128] = {};
+
+// Device address of the array on the current device, looked up once per device.
+npa_status static_scratch_address(void** out) {
+  int dev = 0;
+  NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 128) return fail(NPA_ERR_UNSUPPORTED, "device ordinal above 127");
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    NPA_CUDA(cudaGetSymbolAddress(&p, g_hashgrid_static_scratch), "cudaGetSymbolAddress");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return NPA_OK;
+}
+
+}  // namespace
 }  // namespace npa
+
+extern "C" npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg,
+                                                     const float* d_positions, int64_t batch,
+                                                     int64_t n, uint32_t* d_bin_offsets,
+                                                     uint32_t* d_permutation,
+                                                     uint32_t* d_inverse_permutation,
+                                                     void* stream) {
+  using namespace npa;
+  NPA_TRY(validate_grid(cfg));
+  if (batch < 0 || n < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "batch and particle count must be >= 0");
+  if (batch > 0 && uint64_t(n) > kStaticMaxParticles / uint64_t(batch))
+    return fail(NPA_ERR_UNSUPPORTED,
+                "batch * particle_count = " + std::to_string(uint64_t(batch) * uint64_t(n)) +
+                    " exceeds the allocation-free hashgrid limit of " +
+                    std::to_string(kStaticMaxParticles) + " particles");
+  const GridParams g = make_grid_params(*cfg);
+  if (batch > 0 && uint64_t(g.cells) > uint64_t(0xFFFFFFFEu) / uint64_t(batch))
+    return fail(NPA_ERR_UNSUPPORTED, "batch * cell_count + 1 does not fit in uint32");
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  if (!d_bin_offsets || (total > 0 && (!d_positions || !d_permutation || !d_inverse_permutation)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  void* base = nullptr;
+  NPA_TRY(static_scratch_address(&base));
+  Carve c(base, kStaticScratchBytes);
+  HashgridBuffers hb;
+  hb.bin_offsets = d_bin_offsets;
+  hb.permutation = d_permutation;
+  hb.inverse = d_inverse_permutation;
+  hb.spos = c.take<float4>(total);
+  hb.scoord = c.take<int4>(total);
+  const size_t sb = hashgrid_scratch_bytes(g, B, N);
+  char* scratch = c.take<char>(sb);
+  if (!c.fits()) return fail(NPA_ERR_UNSUPPORTED, "allocation-free hashgrid scratch is too small");
+  return launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, hb, scratch, sb,
+                         static_cast<cudaStream_t>(stream));
+}

@@ -245,6 +245,23 @@ npa_status npa_dev_build_hashgrid(const npa_grid_config* cfg, const float* d_pos
                                   uint32_t* d_permutation, uint32_t* d_inverse_permutation,
                                   void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* build_hashgrid on device buffers without allocating anything and without a
+ * workspace.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory (they only hold buffers owned by another
+ * framework, or must not call cudaMalloc because it synchronises the device).
+ * The sort scratch is a fixed device array inside this library (6.5 MiB per
+ * device that loads it, held until process exit), so batch * n is limited to
+ * 131,072 particles; larger sizes return NPA_ERR_UNSUPPORTED.  The first call
+ * on each device looks up the array's device address (make it before any
+ * stream capture on that device).  All calls on a device share the one array:
+ * calls whose GPU work overlaps (different streams, or different host threads)
+ * race on it and must be serialised by the caller.  Results are identical to
+ * npa_dev_build_hashgrid. */
+npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg, const float* d_positions,
+                                          int64_t batch, int64_t n, uint32_t* d_bin_offsets,
+                                          uint32_t* d_permutation,
+                                          uint32_t* d_inverse_permutation, void* stream);
+
 /* Workspace bytes needed by npa_dev_perceive_with_options. */
 npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,
                                            int64_t state_dims, size_t* bytes);
