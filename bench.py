@@ -45,10 +45,10 @@ sys.path.insert(0, str(ROOT))
 
 BATCH_TOTAL = 256
 PARTICLES = 4096
-# Algorithmic HBM bytes of the fused step kernel per particle (C = 16):
-# position read + write (32), state read + write (2 * 4C = 128), volume and
-# permutation read (8).
-FUSED_BYTES_PER_PARTICLE = 168
+# Algorithmic HBM bytes of the MLP step kernel per particle (C = 16, F = 64):
+# feature row read (4F = 256), position read + write (32), next state write
+# (4C = 64), permutation read (4).
+FUSED_BYTES_PER_PARTICLE = 356
 # Whole rollout step per particle-step (hashgrid keys / permutation and the
 # density round trip added): 184 + bin offsets (4 * 4097 / 4096).
 STEP_BYTES_PER_PARTICLE = 188
@@ -253,7 +253,7 @@ def run_ours(args, rank, world, local_rank):
     launches = lib.npa_kernel_launch_count() - launches0
     if world > 1:
         dist.barrier()
-    t = torch.tensor([total_ms, float(phase_ms[:, 2].mean())], dtype=torch.float64,
+    t = torch.tensor([total_ms, float(phase_ms[:, 3].mean())], dtype=torch.float64,
                      device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -317,7 +317,7 @@ def run_ours(args, rank, world, local_rank):
                        "eps": w.grid.eps, "grid": list(w.grid.grid_size[:2]),
                        "parallelism": f"{world} independent shards (no step-path collective)",
                        "l2": "no flush: per-step working set (~220 MB) exceeds the 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": "fused_step_kernel",
+            "roofline": {"bound": "hbm", "kernel": "mlp_step_kernel",
                          "achieved": fused_achieved, "peak": peak, "unit": "GB/s",
                          "frac": fused_achieved / peak, "peak_source": peak_kind,
                          "traffic": None,
@@ -332,7 +332,8 @@ def run_ours(args, rank, world, local_rank):
                              "frac": fp32_achieved / fp32_peak},
             "phase_ms": {"hashgrid": float(phase_ms[:, 0].mean()),
                          "density": float(phase_ms[:, 1].mean()),
-                         "fused_step": float(phase_ms[:, 2].mean())},
+                         "perception": float(phase_ms[:, 2].mean()),
+                         "mlp_step": float(phase_ms[:, 3].mean())},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,

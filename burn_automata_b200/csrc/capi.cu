@@ -246,9 +246,18 @@ struct PerceiveWorkspace {
   float* volume;
   void* sort_scratch;
   size_t sort_scratch_bytes;
+  float* tiles;  // step path only: feature tiles [tiles][F][tile_rows]
 };
 
-size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n) {
+size_t tiles_floats(uint32_t batch, uint32_t n, int feature_dims, int tile_rows) {
+  if (tile_rows <= 0) return 0;
+  const size_t total = size_t(batch) * n;
+  const size_t padded = (total + tile_rows - 1) / tile_rows * size_t(tile_rows);
+  return padded * size_t(feature_dims);
+}
+
+size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n,
+                                size_t extra_floats = 0) {
   const size_t total = size_t(batch) * n;
   Carve c(nullptr, 0);
   c.take<uint32_t>(size_t(batch) * g.cells + 1);
@@ -259,11 +268,12 @@ size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n)
   c.take<float>(total);
   const size_t sort = hashgrid_scratch_bytes(g, batch, n);
   c.take<char>(sort);
+  c.take<float>(extra_floats);
   return c.used + 256;
 }
 
 bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, size_t bytes,
-                    PerceiveWorkspace* out) {
+                    PerceiveWorkspace* out, size_t extra_floats = 0) {
   const size_t total = size_t(batch) * n;
   Carve c(ws, bytes);
   out->hg.bin_offsets = c.take<uint32_t>(size_t(batch) * g.cells + 1);
@@ -274,6 +284,7 @@ bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, s
   out->volume = c.take<float>(total);
   out->sort_scratch_bytes = hashgrid_scratch_bytes(g, batch, n);
   out->sort_scratch = c.take<char>(out->sort_scratch_bytes);
+  out->tiles = extra_floats ? c.take<float>(extra_floats) : nullptr;
   return c.fits();
 }
 
@@ -591,10 +602,19 @@ npa_status npa_model_create(const npa_model_config* cfg, const float* w1, int64_
   if (!w1 || !b1 || !w2 || !b2) return fail(NPA_ERR_INVALID_ARGUMENT, "null weights");
   if (cfg->auxiliary_input_dims != 0)
     return fail(NPA_ERR_UNSUPPORTED, "auxiliary input dims are not part of the rollout step");
-  if (H > 256 || O > 64)
-    return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range (hidden <= 256, update dims <= 64)");
+  if (H > 256) return fail(NPA_ERR_UNSUPPORTED, "hidden_dims above 256 is not supported");
+  {
+    DeviceModel probe{};
+    probe.state_dims = cfg->state_dims;
+    probe.hidden_dims = int(H);
+    probe.feature_dims = int(F);
+    probe.update_dims = int(O);
+    probe.hidden_padded = hidden_padded_for(int(H));
+    if (!mlp_step_supported(probe))
+      return fail(NPA_ERR_UNSUPPORTED, "update dims too large for the MLP's hidden width");
+  }
   NPA_TRY(ensure_device(device));
-  const int64_t Hp = (H + 127) / 128 * 128;
+  const int64_t Hp = hidden_padded_for(int(H));
   std::vector<float> w1t(size_t(F) * Hp, 0.0f);
   for (int64_t h = 0; h < H; ++h)
     for (int64_t f = 0; f < F; ++f) w1t[size_t(f) * Hp + h] = w1[h * F + f];
@@ -615,6 +635,7 @@ npa_status npa_model_create(const npa_model_config* cfg, const float* w1, int64_
   d.log_norm_density_grad = cfg->log_norm_density_grad;
   d.position_features = cfg->position_features;
   d.device = device;
+  d.hidden_padded = int(Hp);
   auto up = [&](float** dst, const float* src, size_t count) -> npa_status {
     NPA_CUDA(cudaMalloc(dst, std::max<size_t>(count, 4) * sizeof(float)), "cudaMalloc weights");
     NPA_CUDA(cudaMemcpy(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice), "cudaMemcpy weights");
@@ -833,7 +854,14 @@ npa_status npa_dev_step_workspace_size(npa_model* m, const npa_grid_config* grid
                                        int64_t n, size_t* bytes) {
   if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
   NPA_TRY(check_step(m, grid));
-  return npa_dev_perceive_workspace_size(grid, batch, n, m->dm.state_dims, bytes);
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(grid, batch));
+  if (!bytes) return fail(NPA_ERR_INVALID_ARGUMENT, "null output");
+  const GridParams g = make_grid_params(*grid);
+  *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n),
+                                    tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims,
+                                                 step_tile_rows(m->dm)));
+  return NPA_OK;
 }
 
 npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const float* d_positions,
@@ -850,10 +878,12 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   if (total > 0 && (!d_positions || !d_next_positions || !d_workspace ||
                     (m->dm.state_dims > 0 && (!d_states || !d_next_states))))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
-  if (!fused_step_supported(m->dm))
-    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the fused kernel's range (state_dims <= 32)");
+  if (!mlp_step_supported(m->dm))
+    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the supported range");
   PerceiveWorkspace w;
-  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w))
+  const int tile_rows = step_tile_rows(m->dm);
+  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w,
+                      tiles_floats(B, N, m->dm.feature_dims, tile_rows)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
   const PerceptionParams p = make_perception_params(g, model_options(m->cfg), N, m->dm.state_dims);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -861,14 +891,15 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
                           w.sort_scratch, w.sort_scratch_bytes, st));
   const SortedGrid sv = sorted_view(w, N, B);
   NPA_TRY(launch_density(g, sv, B, w.volume, d_density, st));
+  NPA_TRY(launch_perception_tiles(g, p, sv, B, d_states, m->dm.state_dims, w.volume, tile_rows,
+                                  w.tiles, st));
   StepOutputs out;
   out.next_positions = reinterpret_cast<float4*>(d_next_positions);
   out.next_states = d_next_states;
   out.dx = reinterpret_cast<float4*>(d_dx);
   out.ds = d_ds;
   out.features = d_features;
-  return launch_fused_step(m->dm, g, p, sv, B, reinterpret_cast<const float4*>(d_positions),
-                           d_states, w.volume, dt, d_update_mask, out, st);
+  return launch_mlp_step(m->dm, g, sv, B, w.tiles, dt, d_update_mask, out, st);
 }
 
 }  // extern "C"
@@ -876,11 +907,11 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
 // ---------------------------------------------------------------------------
 // executor
 // ---------------------------------------------------------------------------
-// One rollout step is three phases, each captured into its own CUDA graph per
-// ping-pong parity: (0) hashgrid, (1) density, (2) fused perception + MLP +
-// Euler.  Replaying the phases as separate graphs lets a caller bracket the
-// dominant kernel with CUDA events on the launching stream.
-constexpr int kPhases = 3;
+// One rollout step is four phases, each captured into its own CUDA graph per
+// ping-pong parity: (0) hashgrid, (1) density, (2) perception into feature
+// tiles, (3) MLP + dx/ds + Euler.  Replaying the phases as separate graphs
+// lets a caller bracket each kernel with CUDA events on the launching stream.
+constexpr int kPhases = 4;
 
 struct npa_executor {
   npa_model* model = nullptr;
@@ -897,7 +928,8 @@ struct npa_executor {
   cudaGraphExec_t graph[2][kPhases] = {};
   float graph_dt = 0.0f;
   cudaStream_t graph_stream = nullptr;
-  int64_t launches[kPhases] = {0, 0, 0};
+  int64_t launches[kPhases] = {0, 0, 0, 0};
+  int tile_rows = 0;
 };
 
 namespace {
@@ -911,6 +943,9 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
                              e->w.sort_scratch, e->w.sort_scratch_bytes, s);
     case 1:
       return launch_density(e->g, sv, B, e->w.volume, nullptr, s);
+    case 2:
+      return launch_perception_tiles(e->g, e->p, sv, B, e->st[from], e->model->dm.state_dims,
+                                     e->w.volume, e->tile_rows, e->w.tiles, s);
     default: {
       StepOutputs out;
       out.next_positions = reinterpret_cast<float4*>(e->pos[1 - from]);
@@ -918,9 +953,7 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
       out.dx = nullptr;
       out.ds = nullptr;
       out.features = nullptr;
-      return launch_fused_step(e->model->dm, e->g, e->p, sv, B,
-                               reinterpret_cast<const float4*>(e->pos[from]), e->st[from],
-                               e->w.volume, dt, nullptr, out, s);
+      return launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, dt, nullptr, out, s);
     }
   }
 }
@@ -980,8 +1013,8 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   NPA_TRY(check_step(m, grid));
   NPA_TRY(check_counts(batch, n));
   NPA_TRY(check_bins(grid, batch));
-  if (!fused_step_supported(m->dm))
-    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the fused kernel's range (state_dims <= 32)");
+  if (!mlp_step_supported(m->dm))
+    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the supported range");
   NPA_TRY(ensure_device(m->dm.device));
   npa_executor* e = new npa_executor();
   e->model = m;
@@ -992,7 +1025,9 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   e->n = n;
   const size_t total = size_t(batch) * n;
   const size_t C = size_t(m->dm.state_dims);
-  e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n));
+  e->tile_rows = step_tile_rows(m->dm);
+  const size_t tf = tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims, e->tile_rows);
+  e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n), tf);
   npa_status st = NPA_OK;
   auto alloc = [&](void** p, size_t b) -> npa_status {
     NPA_CUDA(cudaMalloc(p, std::max<size_t>(b, 256)), "cudaMalloc executor");
@@ -1003,7 +1038,7 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
     if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->st[i]), total * C * 4);
   }
   if (st == NPA_OK) st = alloc(&e->ws, e->ws_bytes);
-  if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w))
+  if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w, tf))
     st = fail(NPA_ERR_INVALID_ARGUMENT, "executor workspace layout");
   if (st != NPA_OK) {
     npa_executor_destroy(e);
@@ -1131,7 +1166,7 @@ npa_status npa_executor_state_device(npa_executor* e, float** d_positions, float
 
 npa_status npa_executor_launches_per_step(npa_executor* e, int64_t* launches) {
   if (!e || !launches) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
-  *launches = e->launches[0] + e->launches[1] + e->launches[2];
+  *launches = e->launches[0] + e->launches[1] + e->launches[2] + e->launches[3];
   return NPA_OK;
 }
 

@@ -75,6 +75,7 @@ struct PerceptionParams {
   float state_scale;    // normalize_state_gradient scale (normalize.rs:11-15)
   float density_scale;  // normalize_density_gradient scale (normalize.rs:38-46)
   int feature_dims;
+  int vec_states;       // state rows may be read as float4 (16-byte aligned, C % 4 == 0)
 };
 PerceptionParams make_perception_params(const GridParams& g, const npa_perception_options& o,
                                         uint32_t n, int state_dims);
@@ -87,6 +88,12 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
                              const float* volume_sorted, float* features, float* blurred,
                              float* state_gradient, float* density_gradient,
                              cudaStream_t stream);
+// Step path: feature rows of `tile_rows` sorted slots stored feature-major per
+// tile ([tile][F][tile_rows]); rows past B*N are zero.
+npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
+                                   const SortedGrid& s, uint32_t batch, const float* states,
+                                   int state_dims, const float* volume_sorted, int tile_rows,
+                                   float* tiles, cudaStream_t stream);
 
 // ---- model / step (step.cu) ----
 struct DeviceModel {
@@ -95,7 +102,8 @@ struct DeviceModel {
   int equivariance;
   int density_grad, state_grad, log_norm_grad, log_norm_density_grad, position_features;
   int device;
-  float* w1t;  // [F][H] (w1 transposed so a k-slice is contiguous)
+  int hidden_padded;  // H rounded up to 64, 128 or 256 (the MLP's thread grid)
+  float* w1t;  // [F][hidden_padded], w1 transposed and zero-padded
   float* b1;   // [H]
   float* w2;   // [O][H]
   float* b2;   // [O]
@@ -113,12 +121,14 @@ struct StepOutputs {
   float* ds;         // optional
   float* features;   // optional
 };
-// Fused perception + MLP + dx/ds (+3D gates) + Euler over sorted slots.
-npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
-                             const SortedGrid& s, uint32_t batch, const float4* positions,
-                             const float* states, const float* volume_sorted, float dt,
-                             const float* mask, const StepOutputs& out, cudaStream_t stream);
-bool fused_step_supported(const DeviceModel& m);
+int hidden_padded_for(int hidden);
+// Rows per feature tile of the MLP stage (depends on the padded hidden width).
+int step_tile_rows(const DeviceModel& m);
+bool mlp_step_supported(const DeviceModel& m);
+// MLP + dx/ds (+3D gates) + Euler over feature tiles in sorted order.
+npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& s,
+                           uint32_t batch, const float* tiles, float dt, const float* mask,
+                           const StepOutputs& out, cudaStream_t stream);
 
 // ---- decode (decode.cu) ----
 npa_status launch_decode(const npa_gaussian_decode_config& cfg, const float4* positions,

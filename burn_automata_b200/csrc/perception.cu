@@ -1,18 +1,22 @@
-// perception.cu -- density pass and the standalone perception operator
+// perception.cu -- density pass and SPH perception
 // (perceive_with_options, crates/burn_automata_kernels/src/reference/forward.rs:26-143).
 //
-// Both kernels run one thread per sorted slot (the standalone perception
-// kernel one thread per slot and 8-channel chunk), so threads of a warp walk
+// All kernels run over sorted slots, so the threads of a warp walk
 // neighbouring bins and read the sorted position / coordinate views
-// contiguously.  Results are written back in the caller's original particle
-// order through the permutation.
+// contiguously.  DIM (2 or 3) and the channel chunk CH are template
+// parameters: every accumulator is a register.
+//   density_kernel          rho and 1/rho per sorted slot (forward.rs:145-160)
+//   perception_kernel       API output: features and intermediates in the
+//                           caller's particle order
+//   perception_tiles_kernel step path: the feature rows of kTileRows sorted
+//                           slots stored feature-major ([tile][F][rows]), the
+//                           layout the MLP kernel stages into shared memory
 #include "perception_core.cuh"
 
 namespace npa {
 namespace {
 
-constexpr int kChunk = 8;
-
+template <int DIM>
 __global__ void __launch_bounds__(256)
 density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ volume,
                float* __restrict__ density_out) {
@@ -28,6 +32,14 @@ density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ v
   if (density_out) density_out[size_t(batch) * s.n + s.permutation[q]] = rho;
 }
 
+template <int DIM, int CH>
+__device__ __forceinline__ void load_own(const float* __restrict__ states, size_t row, int C,
+                                         int c0, float (&si)[CH]) {
+#pragma unroll
+  for (int c = 0; c < CH; ++c) si[c] = (c0 + c < C) ? __ldg(states + row * C + c0 + c) : 0.0f;
+}
+
+template <int DIM, int CH>
 __global__ void __launch_bounds__(128)
 perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total,
                   const float* __restrict__ states, int C, int chunks,
@@ -38,49 +50,62 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total
   if (t >= uint64_t(total) * chunks) return;
   const uint32_t q = static_cast<uint32_t>(t / chunks);
   const int chunk = static_cast<int>(t - uint64_t(q) * chunks);
-  const int c0 = chunk * kChunk;
+  const int c0 = chunk * CH;
   const uint32_t batch = q / s.n;
   const size_t row = size_t(batch) * s.n + s.permutation[q];
   const float4 pi = s.spos[q];
   const int4 c4 = s.scoord[q];
-  float si[kChunk];
-#pragma unroll
-  for (int c = 0; c < kChunk; ++c) si[c] = (c0 + c < C) ? states[row * C + c0 + c] : 0.0f;
-  PerceptionOut out;
-  perceive_chunk<kChunk>(g, p, s, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
-                         volume, si, out);
-  const int dim = g.dim;
+  float si[CH];
+  load_own<DIM, CH>(states, row, C, c0, si);
+  PerceptionAcc<DIM, CH> a;
+  perceive_chunk<DIM, CH>(g, p, s, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
+                          volume, si, a);
   const size_t F = p.feature_dims;
   float* f = features + row * F;
+  emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi, [&](int k, float v) { f[k] = v; });
 #pragma unroll
-  for (int c = 0; c < kChunk; ++c) {
+  for (int c = 0; c < CH; ++c) {
     const int ch = c0 + c;
     if (ch < C) {
-      f[ch] = si[c];
-      f[C + ch] = out.blur[c];
-      if (blurred) blurred[row * C + ch] = out.blur[c];
-      if (p.state_grad) {
-        for (int a = 0; a < dim; ++a) {
-          f[2 * C + ch * dim + a] = out.sgrad[c * 3 + a];
-          if (state_gradient) state_gradient[(row * C + ch) * dim + a] = out.sgrad[c * 3 + a];
-        }
-      }
+      if (blurred) blurred[row * C + ch] = a.blur[c];
+      if (state_gradient && p.state_grad)
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) state_gradient[(row * C + ch) * DIM + d] = a.sgrad[c][d];
     }
   }
-  if (chunk == 0) {
-    int cursor = 2 * C + (p.state_grad ? C * dim : 0);
-    if (p.density_grad) {
-      for (int a = 0; a < dim; ++a) {
-        f[cursor + a] = out.dgrad[a];
-        if (density_gradient) density_gradient[row * dim + a] = out.dgrad[a];
-      }
-      cursor += dim;
-    }
-    if (p.position_features) {
-      const float pv[3] = {pi.x, pi.y, pi.z};
-      for (int a = 0; a < dim; ++a) f[cursor + a] = pv[a];
-    }
+  if (chunk == 0 && density_gradient && p.density_grad)
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) density_gradient[row * DIM + d] = a.dgrad[d];
+}
+
+template <int DIM, int CH>
+__global__ void __launch_bounds__(128)
+perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total,
+                        uint32_t padded, const float* __restrict__ states, int C, int chunks,
+                        const float* __restrict__ volume, int tile_rows,
+                        float* __restrict__ tiles) {
+  const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= uint64_t(padded) * chunks) return;
+  const uint32_t q = static_cast<uint32_t>(t / chunks);
+  const int chunk = static_cast<int>(t - uint64_t(q) * chunks);
+  const int c0 = chunk * CH;
+  const size_t F = p.feature_dims;
+  float* tile = tiles + size_t(q / tile_rows) * F * tile_rows + (q % tile_rows);
+  if (q >= total) {
+    for (int k = chunk; k < int(F); k += chunks) tile[size_t(k) * tile_rows] = 0.0f;
+    return;
   }
+  const uint32_t batch = q / s.n;
+  const size_t row = size_t(batch) * s.n + s.permutation[q];
+  const float4 pi = s.spos[q];
+  const int4 c4 = s.scoord[q];
+  float si[CH];
+  load_own<DIM, CH>(states, row, C, c0, si);
+  PerceptionAcc<DIM, CH> a;
+  perceive_chunk<DIM, CH>(g, p, s, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
+                          volume, si, a);
+  emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
+                         [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
 }
 
 // f32::powi by binary exponentiation (LLVM's expansion for constant exponents).
@@ -98,6 +123,9 @@ float powi_f32(float x, int n) {
   }
   return have ? result : 1.0f;
 }
+
+// Channels per thread: all of them up to 16, else chunks of 16.
+int chunk_channels(int C) { return C <= 4 ? 4 : (C <= 8 ? 8 : 16); }
 
 }  // namespace
 
@@ -127,9 +155,24 @@ npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t bat
                           float* volume_sorted, float* density_out, cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
-  density_kernel<<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted,
-                                                           density_out);
+  if (g.dim == 2)
+    density_kernel<2><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted, density_out);
+  else
+    density_kernel<3><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted, density_out);
   return after_launch("density_kernel");
+}
+
+template <int DIM, int CH>
+static void launch_perception_t(const GridParams& g, const PerceptionParams& p,
+                                const SortedGrid& s, uint32_t total, const float* states, int C,
+                                const float* volume, float* features, float* blurred,
+                                float* state_gradient, float* density_gradient,
+                                cudaStream_t stream) {
+  const int chunks = C > 0 ? (C + CH - 1) / CH : 1;
+  const uint64_t threads = uint64_t(total) * chunks;
+  perception_kernel<DIM, CH><<<grid_for(threads, 128), 128, 0, stream>>>(
+      g, p, s, total, states, C, chunks, volume, features, blurred, state_gradient,
+      density_gradient);
 }
 
 npa_status launch_perception(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
@@ -139,12 +182,52 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
                              cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
-  const int chunks = state_dims > 0 ? (state_dims + kChunk - 1) / kChunk : 1;
-  const uint64_t threads = uint64_t(total) * chunks;
-  perception_kernel<<<grid_for(threads, 128), 128, 0, stream>>>(
-      g, p, s, total, states, state_dims, chunks, volume_sorted, features, blurred,
-      state_gradient, density_gradient);
+  PerceptionParams pp = p;
+  pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+  const int ch = chunk_channels(state_dims);
+#define NPA_PERC(D, CHV)                                                                      \
+  launch_perception_t<D, CHV>(g, pp, s, total, states, state_dims, volume_sorted, features,   \
+                              blurred, state_gradient, density_gradient, stream)
+  if (g.dim == 2) {
+    if (ch == 4) NPA_PERC(2, 4); else if (ch == 8) NPA_PERC(2, 8); else NPA_PERC(2, 16);
+  } else {
+    if (ch == 4) NPA_PERC(3, 4); else if (ch == 8) NPA_PERC(3, 8); else NPA_PERC(3, 16);
+  }
+#undef NPA_PERC
   return after_launch("perception_kernel");
+}
+
+template <int DIM, int CH>
+static void launch_tiles_t(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
+                           uint32_t total, uint32_t padded, const float* states, int C,
+                           const float* volume, int tile_rows, float* tiles,
+                           cudaStream_t stream) {
+  const int chunks = C > 0 ? (C + CH - 1) / CH : 1;
+  const uint64_t threads = uint64_t(padded) * chunks;
+  perception_tiles_kernel<DIM, CH><<<grid_for(threads, 128), 128, 0, stream>>>(
+      g, p, s, total, padded, states, C, chunks, volume, tile_rows, tiles);
+}
+
+npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
+                                   const SortedGrid& s, uint32_t batch, const float* states,
+                                   int state_dims, const float* volume_sorted, int tile_rows,
+                                   float* tiles, cudaStream_t stream) {
+  const uint32_t total = batch * s.n;
+  if (total == 0) return NPA_OK;
+  const uint32_t padded = (total + tile_rows - 1) / tile_rows * tile_rows;
+  const int ch = chunk_channels(state_dims);
+  PerceptionParams pp = p;
+  pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+#define NPA_TILES(D, CHV)                                                                    \
+  launch_tiles_t<D, CHV>(g, pp, s, total, padded, states, state_dims, volume_sorted,         \
+                         tile_rows, tiles, stream)
+  if (g.dim == 2) {
+    if (ch == 4) NPA_TILES(2, 4); else if (ch == 8) NPA_TILES(2, 8); else NPA_TILES(2, 16);
+  } else {
+    if (ch == 4) NPA_TILES(3, 4); else if (ch == 8) NPA_TILES(3, 8); else NPA_TILES(3, 16);
+  }
+#undef NPA_TILES
+  return after_launch("perception_tiles_kernel");
 }
 
 }  // namespace npa

@@ -1,8 +1,6 @@
-// perception_core.cuh -- per-particle SPH perception shared by the standalone
-// perception kernel and the fused step kernel.
+// perception_core.cuh -- per-particle SPH perception shared by the perception kernels.
 //
 // Restates, for one particle and one chunk of CH state channels:
-//   density pass            forward.rs:145-160 (done by density_kernel)
 //   second pass             forward.rs:249-295 (state_grad && density_grad) or
 //                           blur_state :162, compute_state_gradient :297,
 //                           moment_matrix :357, compute_density_gradient :335
@@ -10,49 +8,79 @@
 //   gradient normalisation  normalize.rs:5-58
 // One neighbour walk updates every accumulator; each accumulator receives its
 // terms in the reference's walk order, so each sum is the reference's sum.
+// DIM and CH are compile-time so every accumulator lives in registers.
 #pragma once
 
 #include "npa_internal.h"
 
 namespace npa {
 
-struct PerceptionOut {
-  float blur[8];
-  float sgrad[8 * 3];  // [channel][axis]
-  float dgrad[3];
+template <int DIM, int CH>
+struct PerceptionAcc {
+  float blur[CH];
+  float sgrad[CH][DIM];
+  float dgrad[DIM];
 };
 
-// CH channels starting at c0 of particle slot q (original row `row`).
-// `states` is the original-order state matrix [B*N][C]; `volume` is
-// recip_finite(density) per sorted slot.  Channels >= C are left zero.
-template <int CH>
+template <int DIM>
+__device__ __forceinline__ void log_normalize_n(float (&v)[DIM]) {
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < DIM; ++i) s = s + v[i] * v[i];
+  const float e = 1.0e-6f;
+  const float norm = fmaxf(sqrtf(s + e * e), e);
+  const float scale = log1p_f32(norm) / norm;
+#pragma unroll
+  for (int i = 0; i < DIM; ++i) v[i] = v[i] * scale;
+}
+
+// CH channels [c0, c0 + CH) of the particle in sorted slot q.  `states` is the
+// caller-order state matrix [B*N][C]; `volume` is recip_finite(density) per
+// sorted slot; `si` holds the particle's own channels.  Channels >= C stay 0.
+template <int DIM, int CH>
 __device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
                                                const SortedGrid& s, uint32_t batch, uint32_t q,
-                                               float4 pi, int3 center, const float* __restrict__ states,
-                                               int C, int c0, const float* __restrict__ volume,
-                                               const float* si, PerceptionOut& out) {
-  const int dim = g.dim;
+                                               float4 pi, int3 center,
+                                               const float* __restrict__ states, int C, int c0,
+                                               const float* __restrict__ volume,
+                                               const float (&si)[CH],
+                                               PerceptionAcc<DIM, CH>& out) {
   const bool both = p.state_grad && p.density_grad;
   const uint32_t batch_base = batch * s.n;
-  float moment[9];
+  float moment[DIM][DIM];
 #pragma unroll
-  for (int i = 0; i < 9; ++i) moment[i] = 0.0f;
+  for (int r = 0; r < DIM; ++r)
+#pragma unroll
+    for (int c = 0; c < DIM; ++c) moment[r][c] = 0.0f;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     out.blur[c] = 0.0f;
 #pragma unroll
-    for (int a = 0; a < 3; ++a) out.sgrad[c * 3 + a] = 0.0f;
+    for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = 0.0f;
   }
 #pragma unroll
-  for (int a = 0; a < 3; ++a) out.dgrad[a] = 0.0f;
+  for (int a = 0; a < DIM; ++a) out.dgrad[a] = 0.0f;
+  const bool full_chunk = c0 + CH <= C;
+  const bool vec4 = p.vec_states && ((C & 3) == 0) && ((c0 & 3) == 0) && (CH % 4 == 0) && full_chunk;
 
   for_each_neighbor(g, s, batch, pi, center, [&](uint32_t qj, float4 d, float r2) {
     const float vol = __ldg(volume + qj);
     const float smooth = poly6(g, r2);
     const float* sj = states + size_t(batch_base + __ldg(s.permutation + qj)) * C + c0;
     float sjv[CH];
+    if (vec4) {
 #pragma unroll
-    for (int c = 0; c < CH; ++c) sjv[c] = (c0 + c < C) ? __ldg(sj + c) : 0.0f;
+      for (int c = 0; c < CH; c += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(sj + c));
+        sjv[c] = v.x;
+        sjv[c + 1] = v.y;
+        sjv[c + 2] = v.z;
+        sjv[c + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < CH; ++c) sjv[c] = (c0 + c < C) ? __ldg(sj + c) : 0.0f;
+    }
     if (both) {
 #pragma unroll
       for (int c = 0; c < CH; ++c) out.blur[c] = out.blur[c] + sjv[c] * smooth * vol;
@@ -66,59 +94,95 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
     if (p.density_grad) {
       const float m1 = spiky_mag(g, r2, 1.0f);
 #pragma unroll
-      for (int a = 0; a < 3; ++a)
-        if (a < dim) out.dgrad[a] = out.dgrad[a] + m1 * dv[a];
+      for (int a = 0; a < DIM; ++a) out.dgrad[a] = out.dgrad[a] + m1 * dv[a];
     }
     if (p.state_grad) {
       const float mv = spiky_mag(g, r2, vol);
-      float gv[3];
+      float gv[DIM];
 #pragma unroll
-      for (int a = 0; a < 3; ++a) gv[a] = mv * dv[a];
+      for (int a = 0; a < DIM; ++a) gv[a] = mv * dv[a];
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         const float diff = sjv[c] - si[c];
 #pragma unroll
-        for (int a = 0; a < 3; ++a)
-          if (a < dim) out.sgrad[c * 3 + a] = out.sgrad[c * 3 + a] + diff * gv[a];
+        for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = out.sgrad[c][a] + diff * gv[a];
       }
       if (p.hybrid) {
 #pragma unroll
-        for (int r = 0; r < 3; ++r)
+        for (int r = 0; r < DIM; ++r)
 #pragma unroll
-          for (int col = 0; col < 3; ++col)
-            if (r < dim && col < dim) moment[r * dim + col] = moment[r * dim + col] + dv[r] * gv[col];
+          for (int col = 0; col < DIM; ++col) moment[r][col] = moment[r][col] + dv[r] * gv[col];
       }
     }
   });
 
   if (p.state_grad) {
     if (p.hybrid) {
-      float inv[9];
-      safe_inverse_symmetric(moment, dim, inv);
+      float m9[9], inv[9];
+#pragma unroll
+      for (int r = 0; r < DIM; ++r)
+#pragma unroll
+        for (int c = 0; c < DIM; ++c) m9[r * DIM + c] = moment[r][c];
+      safe_inverse_symmetric(m9, DIM, inv);
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
-        float corrected[3] = {0.0f, 0.0f, 0.0f};
+        float corrected[DIM];
 #pragma unroll
-        for (int oa = 0; oa < 3; ++oa)
+        for (int oa = 0; oa < DIM; ++oa) {
+          corrected[oa] = 0.0f;
 #pragma unroll
-          for (int ia = 0; ia < 3; ++ia)
-            if (oa < dim && ia < dim)
-              corrected[oa] = corrected[oa] + out.sgrad[c * 3 + ia] * inv[ia * dim + oa];
+          for (int ia = 0; ia < DIM; ++ia)
+            corrected[oa] = corrected[oa] + out.sgrad[c][ia] * inv[ia * DIM + oa];
+        }
 #pragma unroll
-        for (int a = 0; a < 3; ++a) out.sgrad[c * 3 + a] = corrected[a];
+        for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = corrected[a];
       }
     }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
 #pragma unroll
-      for (int a = 0; a < 3; ++a) out.sgrad[c * 3 + a] = out.sgrad[c * 3 + a] * p.state_scale;
-      if (p.log_norm_grad) log_normalize(&out.sgrad[c * 3], dim);
+      for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = out.sgrad[c][a] * p.state_scale;
+      if (p.log_norm_grad) log_normalize_n<DIM>(out.sgrad[c]);
     }
   }
   if (p.density_grad) {
 #pragma unroll
-    for (int a = 0; a < 3; ++a) out.dgrad[a] = out.dgrad[a] * p.density_scale;
-    if (p.log_norm_density_grad) log_normalize(out.dgrad, dim);
+    for (int a = 0; a < DIM; ++a) out.dgrad[a] = out.dgrad[a] * p.density_scale;
+    if (p.log_norm_density_grad) log_normalize_n<DIM>(out.dgrad);
+  }
+}
+
+// Visits the feature row [s | blur | grad (c*DIM+a) | dgrad? | pos?] of one
+// chunk as emit(feature_index, value) (forward.rs:100-133).
+template <int DIM, int CH, class Emit>
+__device__ __forceinline__ void emit_features(const PerceptionParams& p, int C, int c0, bool lead,
+                                              const float (&si)[CH],
+                                              const PerceptionAcc<DIM, CH>& a, float4 pi,
+                                              Emit&& emit) {
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int ch = c0 + c;
+    if (ch < C) {
+      emit(ch, si[c]);
+      emit(C + ch, a.blur[c]);
+      if (p.state_grad) {
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) emit(2 * C + ch * DIM + d, a.sgrad[c][d]);
+      }
+    }
+  }
+  if (lead) {
+    int cursor = 2 * C + (p.state_grad ? C * DIM : 0);
+    if (p.density_grad) {
+#pragma unroll
+      for (int d = 0; d < DIM; ++d) emit(cursor + d, a.dgrad[d]);
+      cursor += DIM;
+    }
+    if (p.position_features) {
+      const float pv[3] = {pi.x, pi.y, pi.z};
+#pragma unroll
+      for (int d = 0; d < DIM; ++d) emit(cursor + d, pv[d]);
+    }
   }
 }
 

@@ -1,4 +1,4 @@
-// step.cu -- the update MLP, the Euler step and the fused rollout step.
+// step.cu -- the update MLP, the Euler step and the MLP stage of the rollout step.
 //
 // MLP: NpaModel::forward_update_from_features (crates/burn_automata/src/model.rs:900-940)
 //   hidden[h] = max(b1[h] + sum_i w1[h][i] * f[i], 0);  u[o] = b2[o] + sum_h w2[o][h] * hidden[h]
@@ -9,39 +9,46 @@
 // the reference-order MLP stays at ~3.5e-4, so the MLP runs on the FP32
 // pipe as separate multiply and add (the library is built with --fmad=false).
 //
-// Work layout (both MLP kernels): a tile of 64 rows per block of 256 threads.
-//   layer 1: thread = 4 rows x 8 hidden units per 128-unit column block, k
-//            streamed through shared memory in 16-wide slices of w1^T;
-//   layer 2: thread = 1 row x ceil(O/4) outputs, sequential over h.
-// Fused step (one kernel after hashgrid + density): each tile first runs SPH
-// perception (4 threads per particle, channel-split) into the transposed
-// feature tile in shared memory, then the MLP, then forward_from_features_with_eps
+// Work layout: 256 threads per block, HG x RG thread grid with HG = Hp / 8
+// hidden groups and RG = 256 / HG row groups; a tile holds M = 8 * RG rows.
+//   layer 1: each thread owns an 8 rows x 8 hidden-unit register tile and
+//            walks k = 0..F-1 in order (features of the tile feature-major in
+//            shared memory, w1 transposed in shared memory);
+//   layer 2: 256 / M threads per row, each owning ceil(O / (256 / M))
+//            outputs, sequential over h.
+// The rollout's MLP stage consumes the feature tiles written by
+// perception_tiles_kernel ([tile][F][M], sorted order), double-buffered with
+// cp.async, and finishes each row with forward_from_features_with_eps
 // (model.rs:867-898), the 3D position gates (model.rs:806-837) and euler_step
-// (crates/burn_automata_kernels/src/reference/step.rs:4-55).
+// (crates/burn_automata_kernels/src/reference/step.rs:4-55), writing the next
+// position / state in the caller's particle order.
 #include <algorithm>
 
-#include "perception_core.cuh"
+#include "npa_internal.h"
 
 namespace npa {
 namespace {
 
-constexpr int kM = 64;          // rows per tile
-constexpr int kThreads = 256;   // threads per block
-constexpr int kKC = 16;         // k slice staged per iteration
-constexpr int kMaxOutPerThread = 16;  // ceil(O / 4) <= 16  ->  O <= 64
+constexpr int kThreads = 256;
+constexpr int kKC = 16;              // k slice when w1 is streamed
+constexpr int kMaxOut = 32;          // outputs per thread in layer 2
+constexpr size_t kSmemBudget = 220 * 1024;
 
 struct MlpShape {
   int F, H, Hp, O;
+  int M;           // rows per tile
+  int tpr;         // layer-2 threads per row (256 / M)
   int hid_stride;  // Hp + 4
   int w2_stride;   // Hp + 4
   int out_stride;  // O + 1
+  int w1_resident; // w1^T [F][Hp] kept in shared memory for the whole kernel
 };
 
 struct SmemLayout {
-  size_t ft, hid, w1s, w2s, outs, total;  // offsets in floats
+  size_t ft0, ft1, hid, w1, w2, outs, total;  // offsets in floats
 };
 
-__host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
+__host__ __device__ inline SmemLayout smem_layout(const MlpShape& s, bool double_buffer) {
   SmemLayout l;
   size_t off = 0;
   auto take = [&](size_t floats) {
@@ -49,151 +56,218 @@ __host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
     off += (floats + 3) & ~size_t(3);
     return o;
   };
-  l.ft = take(size_t(s.F) * kM);
-  l.hid = take(size_t(kM) * s.hid_stride);
-  l.w1s = take(size_t(kKC) * s.Hp);
-  l.w2s = take(size_t(s.O) * s.w2_stride);
-  l.outs = take(size_t(kM) * s.out_stride);
+  l.ft0 = take(size_t(s.F) * s.M);
+  l.ft1 = double_buffer ? take(size_t(s.F) * s.M) : l.ft0;
+  l.hid = take(size_t(s.M) * s.hid_stride);
+  l.w1 = take(size_t(s.w1_resident ? s.F : kKC) * s.Hp);
+  l.w2 = take(size_t(s.O) * s.w2_stride);
+  l.outs = take(size_t(s.M) * s.out_stride);
   l.total = off;
   return l;
 }
 
-// Layer 1 for the tile held transposed in ft[F][kM]; writes relu'd hidden units.
-template <int HCH>
-__device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
-                                           const float* __restrict__ b1, const float* ft,
-                                           float* hid, float* w1s) {
-  const int t = threadIdx.x;
-  const int rg = t >> 4;       // rows rg*4 .. rg*4+3
-  const int hg = t & 15;       // hidden h = hch*128 + hg*8 .. +7
-  float acc[HCH][4][8];
-#pragma unroll
-  for (int hc = 0; hc < HCH; ++hc) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int h = hc * 128 + hg * 8 + j;
-      const float bias = h < s.H ? __ldg(b1 + h) : 0.0f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[hc][i][j] = bias;
-    }
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Weights into shared memory: w2 [O][H] -> rows of w2_stride; w1^T when resident.
+__device__ __forceinline__ void load_weights(const MlpShape& s, const float* __restrict__ w1t,
+                                             const float* __restrict__ w2, float* w1s,
+                                             float* w2s) {
+  for (int e = threadIdx.x; e < s.O * s.H; e += kThreads) {
+    const int o = e / s.H, h = e - o * s.H;
+    w2s[o * s.w2_stride + h] = __ldg(w2 + e);
   }
-  const int hp4 = s.Hp >> 2;
-  for (int kc = 0; kc < s.F; kc += kKC) {
-    const int kn = min(kKC, s.F - kc);
-    __syncthreads();  // previous slice consumed
-    const float4* src = reinterpret_cast<const float4*>(w1t + size_t(kc) * s.Hp);
+  if (s.w1_resident) {
+    const float4* src = reinterpret_cast<const float4*>(w1t);
     float4* dst = reinterpret_cast<float4*>(w1s);
-    for (int e = t; e < kn * hp4; e += kThreads) dst[e] = __ldg(src + e);
-    __syncthreads();
-    for (int kk = 0; kk < kn; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(ft + (kc + kk) * kM + rg * 4);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-      for (int hc = 0; hc < HCH; ++hc) {
-        const float* wrow = w1s + kk * s.Hp + hc * 128 + hg * 8;
-        const float4 b0 = *reinterpret_cast<const float4*>(wrow);
-        const float4 b1v = *reinterpret_cast<const float4*>(wrow + 4);
-        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1v.x, b1v.y, b1v.z, b1v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[hc][i][j] = acc[hc][i][j] + bv[j] * av[i];
-      }
-    }
-  }
-#pragma unroll
-  for (int hc = 0; hc < HCH; ++hc) {
-    const int h0 = hc * 128 + hg * 8;
-    if (h0 < s.Hp) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float* row = hid + (rg * 4 + i) * s.hid_stride + h0;
-        float4 v0 = make_float4(fmaxf(acc[hc][i][0], 0.0f), fmaxf(acc[hc][i][1], 0.0f),
-                                fmaxf(acc[hc][i][2], 0.0f), fmaxf(acc[hc][i][3], 0.0f));
-        float4 v1 = make_float4(fmaxf(acc[hc][i][4], 0.0f), fmaxf(acc[hc][i][5], 0.0f),
-                                fmaxf(acc[hc][i][6], 0.0f), fmaxf(acc[hc][i][7], 0.0f));
-        *reinterpret_cast<float4*>(row) = v0;
-        *reinterpret_cast<float4*>(row + 4) = v1;
-      }
-    }
+    const int n4 = s.F * s.Hp / 4;
+    for (int e = threadIdx.x; e < n4; e += kThreads) dst[e] = __ldg(src + e);
   }
 }
 
-// Layer 2: out[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
+// One k step of the 8 x 8 register tile: acc[i][j] += w[j] * f[i], each a
+// rounded product then a rounded sum.  All 64 products are formed before the
+// 64 sums so no sum waits on the product issued just before it.  (The packed
+// mul.rn.f32x2 / add.rn.f32x2 pair was measured not to reproduce the scalar
+// results bit for bit, so the scalar form stays.)
+__device__ __forceinline__ void micro_tile(float (&acc)[8][8], float4 a0, float4 a1, float4 b0,
+                                           float4 b1) {
+  const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  float p[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[i][j] = bv[j] * av[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = acc[i][j] + p[i][j];
+}
+
+// Layer 1 for the tile in ft[F][M]: hid[r][h] = max(b1[h] + sum_k w1[h][k] f[r][k], 0).
+template <int HG>
+__device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
+                                           const float* __restrict__ b1, const float* ft,
+                                           float* w1s, float* hid) {
+  constexpr int RG = kThreads / HG;
+  constexpr int M = RG * 8;
+  const int t = threadIdx.x;
+  const int rg = t / HG;
+  const int hg = t - rg * HG;
+  const int h0 = hg * 8;
+  float acc[8][8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float bias = (h0 + j < s.H) ? __ldg(b1 + h0 + j) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][j] = bias;
+  }
+  const float* arow = ft + rg * 8;
+  if (s.w1_resident) {
+    const float* wcol = w1s + h0;
+#pragma unroll 2
+    for (int k = 0; k < s.F; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
+      const float4 a1 = *reinterpret_cast<const float4*>(arow + k * M + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(wcol + k * s.Hp);
+      const float4 b1v = *reinterpret_cast<const float4*>(wcol + k * s.Hp + 4);
+      micro_tile(acc, a0, a1, b0, b1v);
+    }
+  } else {
+    const int hp4 = s.Hp >> 2;
+    for (int kc = 0; kc < s.F; kc += kKC) {
+      const int kn = min(kKC, s.F - kc);
+      __syncthreads();  // previous slice consumed
+      const float4* src = reinterpret_cast<const float4*>(w1t + size_t(kc) * s.Hp);
+      float4* dst = reinterpret_cast<float4*>(w1s);
+      for (int e = t; e < kn * hp4; e += kThreads) dst[e] = __ldg(src + e);
+      __syncthreads();
+      const float* wcol = w1s + h0;
+      for (int kk = 0; kk < kn; ++kk) {
+        const int k = kc + kk;
+        const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
+        const float4 a1 = *reinterpret_cast<const float4*>(arow + k * M + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(wcol + kk * s.Hp);
+        const float4 b1v = *reinterpret_cast<const float4*>(wcol + kk * s.Hp + 4);
+        micro_tile(acc, a0, a1, b0, b1v);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float* row = hid + (rg * 8 + i) * s.hid_stride + h0;
+    *reinterpret_cast<float4*>(row) =
+        make_float4(fmaxf(acc[i][0], 0.0f), fmaxf(acc[i][1], 0.0f), fmaxf(acc[i][2], 0.0f),
+                    fmaxf(acc[i][3], 0.0f));
+    *reinterpret_cast<float4*>(row + 4) =
+        make_float4(fmaxf(acc[i][4], 0.0f), fmaxf(acc[i][5], 0.0f), fmaxf(acc[i][6], 0.0f),
+                    fmaxf(acc[i][7], 0.0f));
+  }
+}
+
+// Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
+// tpr threads per row; thread j owns outputs o = j + tpr * u, u < NOUT
+// (NOUT = ceil(O / tpr), the last one masked for threads past O).
+template <int NOUT>
 __device__ __forceinline__ void mlp_layer2(const MlpShape& s, const float* __restrict__ b2,
                                            const float* hid, const float* w2s, float* outs) {
   const int t = threadIdx.x;
-  const int r = t >> 2;
-  const int j = t & 3;
-  float acc[kMaxOutPerThread];
-  const int nout = (s.O - j + 3) >> 2;  // outputs o = j, j+4, ... < O
+  const int r = t / s.tpr;
+  const int j = t - r * s.tpr;
+  const bool last_ok = j + s.tpr * (NOUT - 1) < s.O;
+  float acc[NOUT];
+  const float* wrow[NOUT];
 #pragma unroll
-  for (int u = 0; u < kMaxOutPerThread; ++u) acc[u] = (u < nout) ? __ldg(b2 + j + 4 * u) : 0.0f;
+  for (int u = 0; u < NOUT; ++u) {
+    const int o = (u == NOUT - 1 && !last_ok) ? j : j + s.tpr * u;
+    acc[u] = __ldg(b2 + o);
+    wrow[u] = w2s + o * s.w2_stride;
+  }
   const float* hrow = hid + r * s.hid_stride;
   const int H4 = s.H & ~3;
   for (int h = 0; h < H4; h += 4) {
     const float4 hv = *reinterpret_cast<const float4*>(hrow + h);
 #pragma unroll
-    for (int u = 0; u < kMaxOutPerThread; ++u) {
-      if (u < nout) {
-        const float4 w = *reinterpret_cast<const float4*>(w2s + (j + 4 * u) * s.w2_stride + h);
-        float a = acc[u];
-        a = a + w.x * hv.x;
-        a = a + w.y * hv.y;
-        a = a + w.z * hv.z;
-        a = a + w.w * hv.w;
-        acc[u] = a;
-      }
+    for (int u = 0; u < NOUT; ++u) {
+      const float4 w = *reinterpret_cast<const float4*>(wrow[u] + h);
+      const float p0 = w.x * hv.x, p1 = w.y * hv.y, p2 = w.z * hv.z, p3 = w.w * hv.w;
+      float a = acc[u];
+      a = a + p0;
+      a = a + p1;
+      a = a + p2;
+      a = a + p3;
+      acc[u] = a;
     }
   }
   for (int h = H4; h < s.H; ++h) {
     const float hv = hrow[h];
 #pragma unroll
-    for (int u = 0; u < kMaxOutPerThread; ++u)
-      if (u < nout) acc[u] = acc[u] + w2s[(j + 4 * u) * s.w2_stride + h] * hv;
+    for (int u = 0; u < NOUT; ++u) acc[u] = acc[u] + wrow[u][h] * hv;
   }
 #pragma unroll
-  for (int u = 0; u < kMaxOutPerThread; ++u)
-    if (u < nout) outs[r * s.out_stride + j + 4 * u] = acc[u];
+  for (int u = 0; u < NOUT; ++u)
+    if (u < NOUT - 1 || last_ok) outs[r * s.out_stride + j + s.tpr * u] = acc[u];
 }
 
-__device__ __forceinline__ void load_w2(const MlpShape& s, const float* __restrict__ w2,
-                                        float* w2s) {
-  for (int e = threadIdx.x; e < s.O * s.H; e += kThreads) {
-    const int o = e / s.H, h = e - o * s.H;
-    w2s[o * s.w2_stride + h] = __ldg(w2 + e);
+// Dispatches layer 2 on the per-thread output count.
+__device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
+                                               const float* hid, const float* w2s, float* outs) {
+  switch ((s.O + s.tpr - 1) / s.tpr) {
+#define NPA_L2(N) \
+  case N:         \
+    mlp_layer2<N>(s, b2, hid, w2s, outs); \
+    break;
+    NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
+    NPA_L2(9) NPA_L2(10) NPA_L2(11) NPA_L2(12) NPA_L2(13) NPA_L2(14) NPA_L2(15) NPA_L2(16)
+    NPA_L2(17) NPA_L2(18) NPA_L2(19) NPA_L2(20) NPA_L2(21) NPA_L2(22) NPA_L2(23) NPA_L2(24)
+    NPA_L2(25) NPA_L2(26) NPA_L2(27) NPA_L2(28) NPA_L2(29) NPA_L2(30) NPA_L2(31) NPA_L2(32)
+#undef NPA_L2
+    default:
+      break;
   }
 }
 
-template <int HCH>
-__global__ void __launch_bounds__(kThreads)
+// API MLP: rows of the caller's row-major feature matrix.
+template <int HG>
+__global__ void __launch_bounds__(kThreads, 1)
 forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __restrict__ b1,
                       const float* __restrict__ w2, const float* __restrict__ b2,
                       const float* __restrict__ features, uint32_t rows,
                       float* __restrict__ update) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
-  const SmemLayout L = smem_layout(s);
-  float* ft = smem + L.ft;
+  const SmemLayout L = smem_layout(s, false);
+  float* ft = smem + L.ft0;
   float* hid = smem + L.hid;
-  float* w1s = smem + L.w1s;
-  float* w2s = smem + L.w2s;
+  float* w1s = smem + L.w1;
+  float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
-  load_w2(s, w2, w2s);
-  const uint32_t tiles = (rows + kM - 1) / kM;
+  load_weights(s, w1t, w2, w1s, w2s);
+  const uint32_t tiles = (rows + s.M - 1) / s.M;
   for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     __syncthreads();
-    const uint32_t row0 = tile * kM;
-    for (int e = threadIdx.x; e < kM * s.F; e += kThreads) {
+    const uint32_t row0 = tile * s.M;
+    for (int e = threadIdx.x; e < s.M * s.F; e += kThreads) {
       const int r = e / s.F, f = e - r * s.F;
       const uint32_t row = row0 + r;
-      ft[f * kM + r] = row < rows ? __ldg(features + size_t(row) * s.F + f) : 0.0f;
+      ft[f * s.M + r] = row < rows ? __ldg(features + size_t(row) * s.F + f) : 0.0f;
     }
-    mlp_layer1<HCH>(s, w1t, b1, ft, hid, w1s);
     __syncthreads();
-    mlp_layer2(s, b2, hid, w2s, outs);
+    mlp_layer1<HG>(s, w1t, b1, ft, w1s, hid);
     __syncthreads();
-    for (int e = threadIdx.x; e < kM * s.O; e += kThreads) {
+    mlp_layer2_any(s, b2, hid, w2s, outs);
+    __syncthreads();
+    for (int e = threadIdx.x; e < s.M * s.O; e += kThreads) {
       const int r = e / s.O, o = e - r * s.O;
       const uint32_t row = row0 + r;
       if (row < rows) update[size_t(row) * s.O + o] = outs[r * s.out_stride + o];
@@ -203,8 +277,8 @@ forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __
 
 struct EulerParams {
   float dt;
-  int mem_dims;     // spatial_mem_dims (config.rs:90-92)
-  int clamp3d;      // dim == 3 && C > 3 (step.rs:48)
+  int mem_dims;  // spatial_mem_dims (config.rs:90-92)
+  int clamp3d;   // dim == 3 && C > 3 (step.rs:48)
 };
 
 // euler_step (step.rs:4-55) for one row.
@@ -241,84 +315,60 @@ __global__ void euler_kernel(GridParams g, EulerParams e, const float4* __restri
   }
 }
 
-struct FusedParams {
+struct StepParams {
   float alpha;
   float motion_eps;  // NpaConfig::motion_eps (config.rs:156-162)
   int gates3d;       // dim == 3 && position_features && C > 3 (model.rs:806-809)
+  int C;
+  int D;
 };
 
-// Fused rollout step over sorted slots; CH = channels per perception thread.
-template <int CH, int HCH>
-__global__ void __launch_bounds__(kThreads)
-fused_step_kernel(MlpShape s, GridParams g, PerceptionParams p, SortedGrid sg, uint32_t total,
-                  int C, const float* __restrict__ w1t, const float* __restrict__ b1,
-                  const float* __restrict__ w2, const float* __restrict__ b2,
-                  const float4* __restrict__ positions, const float* __restrict__ states,
-                  const float* __restrict__ volume, FusedParams fp, EulerParams ep,
-                  const float* __restrict__ mask, float4* __restrict__ next_pos,
-                  float* __restrict__ next_states, float4* __restrict__ dx_out,
-                  float* __restrict__ ds_out, float* __restrict__ features_out) {
+// The rollout step's MLP stage over feature tiles in sorted order.
+template <int HG>
+__global__ void __launch_bounds__(kThreads, 1)
+mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
+                const float* __restrict__ tiles_in, const float* __restrict__ w1t,
+                const float* __restrict__ b1, const float* __restrict__ w2,
+                const float* __restrict__ b2, StepParams sp, EulerParams ep,
+                const float* __restrict__ mask, float4* __restrict__ next_pos,
+                float* __restrict__ next_states, float4* __restrict__ dx_out,
+                float* __restrict__ ds_out, float* __restrict__ features_out) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
-  const SmemLayout L = smem_layout(s);
-  float* ft = smem + L.ft;
+  const SmemLayout L = smem_layout(s, true);
+  float* ftb[2] = {smem + L.ft0, smem + L.ft1};
   float* hid = smem + L.hid;
-  float* w1s = smem + L.w1s;
-  float* w2s = smem + L.w2s;
+  float* w1s = smem + L.w1;
+  float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
-  load_w2(s, w2, w2s);
-  const int D = g.dim;
-  const uint32_t tiles = (total + kM - 1) / kM;
-  const int r = threadIdx.x >> 2;    // particle within the tile
-  const int part = threadIdx.x & 3;  // channel chunk
-  const int c0 = part * CH;
-  for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    __syncthreads();  // previous tile's epilogue done with ft / outs
-    const uint32_t q = tile * kM + r;
-    const bool live = q < total;
-    // ---- perception into ft[F][kM] ----
-    if (live) {
-      const uint32_t batch = q / sg.n;
-      const size_t row = size_t(batch) * sg.n + sg.permutation[q];
-      const float4 pi = sg.spos[q];
-      const int4 c4 = sg.scoord[q];
-      float si[CH];
-#pragma unroll
-      for (int c = 0; c < CH; ++c) si[c] = (c0 + c < C) ? __ldg(states + row * C + c0 + c) : 0.0f;
-      PerceptionOut po;
-      perceive_chunk<CH>(g, p, sg, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
-                         volume, si, po);
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int ch = c0 + c;
-        if (ch < C) {
-          ft[ch * kM + r] = si[c];
-          ft[(C + ch) * kM + r] = po.blur[c];
-          if (p.state_grad)
-            for (int a = 0; a < D; ++a) ft[(2 * C + ch * D + a) * kM + r] = po.sgrad[c * 3 + a];
-        }
-      }
-      if (part == 0) {
-        int cursor = 2 * C + (p.state_grad ? C * D : 0);
-        if (p.density_grad) {
-          for (int a = 0; a < D; ++a) ft[(cursor + a) * kM + r] = po.dgrad[a];
-          cursor += D;
-        }
-        if (p.position_features) {
-          const float pv[3] = {pi.x, pi.y, pi.z};
-          for (int a = 0; a < D; ++a) ft[(cursor + a) * kM + r] = pv[a];
-        }
-      }
-    } else {
-      for (int f = part; f < s.F; f += 4) ft[f * kM + r] = 0.0f;
-    }
-    // ---- MLP ----
-    mlp_layer1<HCH>(s, w1t, b1, ft, hid, w1s);
+  const int C = sp.C, D = sp.D;
+  const uint32_t tiles = (total + s.M - 1) / s.M;
+  const int chunks16 = s.F * s.M / 4;  // 16-byte chunks per feature tile
+  auto issue = [&](uint32_t tile, float* dst) {
+    const float* src = tiles_in + size_t(tile) * s.F * s.M;
+    for (int e = threadIdx.x; e < chunks16; e += kThreads) cp_async16(dst + 4 * e, src + 4 * e);
+  };
+  uint32_t tile = blockIdx.x;
+  if (tile < tiles) issue(tile, ftb[0]);
+  cp_async_commit();
+  load_weights(s, w1t, w2, w1s, w2s);
+  int buf = 0;
+  for (; tile < tiles; tile += gridDim.x, buf ^= 1) {
+    const uint32_t next = tile + gridDim.x;
+    if (next < tiles) issue(next, ftb[buf ^ 1]);
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
-    mlp_layer2(s, b2, hid, w2s, outs);
+    const float* ft = ftb[buf];
+    mlp_layer1<HG>(s, w1t, b1, ft, w1s, hid);
     __syncthreads();
-    // ---- forward_from_features_with_eps + gates + euler_step ----
-    if (live) {
+    mlp_layer2_any(s, b2, hid, w2s, outs);
+    __syncthreads();
+    // forward_from_features_with_eps + gates + euler_step, tpr threads per row
+    const int r = threadIdx.x / s.tpr;
+    const int part = threadIdx.x - r * s.tpr;
+    const uint32_t q = tile * s.M + r;
+    if (q < total) {
       const uint32_t batch = q / sg.n;
       const size_t row = size_t(batch) * sg.n + sg.permutation[q];
       const float* u = outs + r * s.out_stride;
@@ -326,54 +376,51 @@ fused_step_kernel(MlpShape s, GridParams g, PerceptionParams p, SortedGrid sg, u
       for (int a = 0; a < D; ++a) norm = norm + u[a] * u[a];
       norm = sqrtf(norm);
       float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int a = 0; a < D; ++a) dx[a] = fp.alpha * u[a] * fp.motion_eps / (1.0f + norm);
+      for (int a = 0; a < D; ++a) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
       const float4 pi = sg.spos[q];
       float state_gate = 1.0f;
-      bool gated = false;
-      if (fp.gates3d) {
+      if (sp.gates3d) {
         // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
-        const float liveness = ft[3 * kM + r];
-        const float sd = ft[7 * kM + r];
+        const float liveness = ft[3 * s.M + r];
+        const float sd = ft[7 * s.M + r];
         state_gate = clamp_rs((4.0f - liveness) * 2.0f, 0.0f, 1.0f);
         float motion_gate = 0.0f;
-        if (!(pi.w >= 0.5f)) {
-          const float dg = clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
-          motion_gate = state_gate * dg;
-        }
+        if (!(pi.w >= 0.5f)) motion_gate = state_gate * clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
         for (int a = 0; a < D; ++a) dx[a] = dx[a] * motion_gate;
-        gated = true;
       }
       const float m = mask ? __ldg(mask + row) : 1.0f;
       if (part == 0) {
         next_pos[row] = euler_position(g, ep, pi, dx, m);
         if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
       }
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int ch = c0 + c;
-        if (ch < C) {
-          float dsv = u[D + ch];
-          if (gated) dsv = dsv * state_gate;
-          const float sv = ft[ch * kM + r];
-          next_states[row * C + ch] = euler_state(ep, C, ch, sv, dsv, m);
-          if (ds_out) ds_out[row * C + ch] = dsv;
-        }
+      for (int ch = part; ch < C; ch += s.tpr) {
+        float dsv = u[D + ch];
+        if (sp.gates3d) dsv = dsv * state_gate;
+        next_states[row * C + ch] = euler_state(ep, C, ch, ft[ch * s.M + r], dsv, m);
+        if (ds_out) ds_out[row * C + ch] = dsv;
       }
       if (features_out)
-        for (int f = part; f < s.F; f += 4) features_out[row * s.F + f] = ft[f * kM + r];
+        for (int f = part; f < s.F; f += s.tpr) features_out[row * s.F + f] = ft[f * s.M + r];
     }
+    __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
-MlpShape make_shape(const DeviceModel& m) {
+MlpShape make_shape(const DeviceModel& m, bool double_buffer) {
   MlpShape s;
   s.F = m.feature_dims;
   s.H = m.hidden_dims;
-  s.Hp = (m.hidden_dims + 127) / 128 * 128;
+  s.Hp = m.hidden_padded;
   s.O = m.update_dims;
+  const int HG = s.Hp / 8;
+  s.M = (kThreads / HG) * 8;
+  s.tpr = kThreads / s.M;
   s.hid_stride = s.Hp + 4;
   s.w2_stride = s.Hp + 4;
   s.out_stride = s.O + 1;
+  s.w1_resident = 1;
+  if (smem_layout(s, double_buffer).total * sizeof(float) > kSmemBudget) s.w1_resident = 0;
   return s;
 }
 
@@ -383,8 +430,8 @@ struct LaunchCfg {
 };
 
 template <class K>
-npa_status plan(K kernel, const MlpShape& s, uint64_t tiles, LaunchCfg* out) {
-  const size_t smem = smem_layout(s).total * sizeof(float);
+npa_status plan(K kernel, const MlpShape& s, bool double_buffer, uint64_t tiles, LaunchCfg* out) {
+  const size_t smem = smem_layout(s, double_buffer).total * sizeof(float);
   int dev = 0;
   NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   int max_optin = 0, sms = 0;
@@ -406,30 +453,42 @@ npa_status plan(K kernel, const MlpShape& s, uint64_t tiles, LaunchCfg* out) {
   return NPA_OK;
 }
 
+bool shape_ok(const DeviceModel& m) {
+  if (m.hidden_padded != 64 && m.hidden_padded != 128 && m.hidden_padded != 256) return false;
+  const int M = (kThreads / (m.hidden_padded / 8)) * 8;
+  const int tpr = kThreads / M;
+  return (m.update_dims + tpr - 1) / tpr <= kMaxOut && m.feature_dims >= 1;
+}
+
 }  // namespace
 
-bool fused_step_supported(const DeviceModel& m) {
-  return m.state_dims >= 0 && m.state_dims <= 32 && m.update_dims <= 4 * kMaxOutPerThread &&
-         m.hidden_dims >= 1 && m.hidden_dims <= 256 && m.feature_dims >= 1;
+int hidden_padded_for(int hidden) { return hidden <= 64 ? 64 : (hidden <= 128 ? 128 : 256); }
+
+int step_tile_rows(const DeviceModel& m) { return (kThreads / (m.hidden_padded / 8)) * 8; }
+
+bool mlp_step_supported(const DeviceModel& m) {
+  return m.state_dims >= 0 && m.hidden_dims >= 1 && m.hidden_dims <= 256 && shape_ok(m);
 }
 
 npa_status launch_forward_update(const DeviceModel& m, const float* features, uint32_t rows,
                                  float* update, cudaStream_t stream) {
   if (rows == 0) return NPA_OK;
-  const MlpShape s = make_shape(m);
-  if (s.O > 4 * kMaxOutPerThread || s.Hp > 256)
-    return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range (H <= 256, O <= 64)");
-  const uint64_t tiles = (uint64_t(rows) + kM - 1) / kM;
+  if (!mlp_step_supported(m))
+    return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range");
+  const MlpShape s = make_shape(m, false);
+  const uint64_t tiles = (uint64_t(rows) + s.M - 1) / s.M;
   LaunchCfg lc;
-  if (s.Hp <= 128) {
-    NPA_TRY(plan(forward_update_kernel<1>, s, tiles, &lc));
-    forward_update_kernel<1><<<lc.grid, kThreads, lc.smem, stream>>>(s, m.w1t, m.b1, m.w2, m.b2,
-                                                                     features, rows, update);
-  } else {
-    NPA_TRY(plan(forward_update_kernel<2>, s, tiles, &lc));
-    forward_update_kernel<2><<<lc.grid, kThreads, lc.smem, stream>>>(s, m.w1t, m.b1, m.w2, m.b2,
-                                                                     features, rows, update);
-  }
+#define NPA_FWD(HGV)                                                                          \
+  do {                                                                                        \
+    NPA_TRY(plan(forward_update_kernel<HGV>, s, false, tiles, &lc));                          \
+    forward_update_kernel<HGV><<<lc.grid, kThreads, lc.smem, stream>>>(s, m.w1t, m.b1, m.w2,  \
+                                                                       m.b2, features, rows,  \
+                                                                       update);               \
+  } while (0)
+  if (s.Hp == 64) NPA_FWD(8);
+  else if (s.Hp == 128) NPA_FWD(16);
+  else NPA_FWD(32);
+#undef NPA_FWD
   return after_launch("forward_update_kernel");
 }
 
@@ -445,38 +504,35 @@ npa_status launch_euler(const GridParams& g, const float4* positions, const floa
   return after_launch("euler_kernel");
 }
 
-npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
-                             const SortedGrid& sgrid, uint32_t batch, const float4* positions,
-                             const float* states, const float* volume_sorted, float dt,
-                             const float* mask, const StepOutputs& out, cudaStream_t stream) {
+npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
+                           uint32_t batch, const float* tiles, float dt, const float* mask,
+                           const StepOutputs& out, cudaStream_t stream) {
   const uint32_t total = batch * sgrid.n;
   if (total == 0) return NPA_OK;
-  if (!fused_step_supported(m))
-    return fail(NPA_ERR_UNSUPPORTED, "step shape outside the fused kernel's range (C <= 32, H <= 256)");
-  const MlpShape s = make_shape(m);
-  FusedParams fp;
-  fp.alpha = m.alpha;
-  fp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
-  fp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;
+  if (!mlp_step_supported(m))
+    return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range");
+  const MlpShape s = make_shape(m, true);
+  StepParams sp;
+  sp.alpha = m.alpha;
+  sp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
+  sp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;
+  sp.C = m.state_dims;
+  sp.D = g.dim;
   EulerParams e{dt, g.dim == 3 ? 4 : 2, (g.dim == 3 && m.state_dims > 3) ? 1 : 0};
-  const uint64_t tiles = (uint64_t(total) + kM - 1) / kM;
+  const uint64_t ntiles = (uint64_t(total) + s.M - 1) / s.M;
   LaunchCfg lc;
-#define NPA_FUSED(CH, HCH)                                                                     \
-  do {                                                                                         \
-    NPA_TRY(plan(fused_step_kernel<CH, HCH>, s, tiles, &lc));                                  \
-    fused_step_kernel<CH, HCH><<<lc.grid, kThreads, lc.smem, stream>>>(                        \
-        s, g, p, sgrid, total, m.state_dims, m.w1t, m.b1, m.w2, m.b2, positions, states,      \
-        volume_sorted, fp, e, mask, out.next_positions, out.next_states, out.dx, out.ds,       \
-        out.features);                                                                         \
+#define NPA_MLP(HGV)                                                                          \
+  do {                                                                                        \
+    NPA_TRY(plan(mlp_step_kernel<HGV>, s, true, ntiles, &lc));                                \
+    mlp_step_kernel<HGV><<<lc.grid, kThreads, lc.smem, stream>>>(                             \
+        s, g, sgrid, total, tiles, m.w1t, m.b1, m.w2, m.b2, sp, e, mask, out.next_positions,  \
+        out.next_states, out.dx, out.ds, out.features);                                       \
   } while (0)
-  const bool small_c = m.state_dims <= 16;
-  const bool small_h = s.Hp <= 128;
-  if (small_c && small_h) NPA_FUSED(4, 1);
-  else if (small_c) NPA_FUSED(4, 2);
-  else if (small_h) NPA_FUSED(8, 1);
-  else NPA_FUSED(8, 2);
-#undef NPA_FUSED
-  return after_launch("fused_step_kernel");
+  if (s.Hp == 64) NPA_MLP(8);
+  else if (s.Hp == 128) NPA_MLP(16);
+  else NPA_MLP(32);
+#undef NPA_MLP
+  return after_launch("mlp_step_kernel");
 }
 
 }  // namespace npa

@@ -232,8 +232,9 @@ class CudaAutomataExecutor:
     def step_state_many_profiled(self, steps: int, dt: float, use_graph: bool = True,
                                  stream=None):
         """step_state_many with CUDA events around every phase of every step.
-        Returns (phase_ms [steps, 3] for hashgrid / density / fused step, total_ms)."""
-        phase = np.zeros((int(steps), 3), np.float32)
+        Returns (phase_ms [steps, 4] for hashgrid / density / perception / MLP step,
+        total_ms)."""
+        phase = np.zeros((int(steps), 4), np.float32)
         total = ctypes.c_float(0.0)
         _lib.check(_lib.lib().npa_executor_step_many_profiled(
             self._handle, int(steps), float(dt), 1 if use_graph else 0, stream, _fp(phase),

@@ -297,8 +297,9 @@ npa_status npa_dev_decode_gaussians_3d(const npa_gaussian_decode_config* cfg,
 npa_status npa_dev_step_workspace_size(npa_model* model, const npa_grid_config* grid,
                                        int64_t batch, int64_t n, size_t* bytes);
 /* NpaModel::step_cpu on device buffers (model.rs:768-858): hashgrid, density,
- * then one fused kernel for perception + MLP + dx/ds + Euler.  Optional
- * outputs (d_update_mask, d_dx, d_ds, d_features, d_density) may be NULL. */
+ * perception into feature tiles, then one kernel for MLP + dx/ds + Euler.
+ * Optional outputs (d_update_mask, d_dx, d_ds, d_features, d_density) may be
+ * NULL. */
 npa_status npa_dev_model_step(npa_model* model, const npa_grid_config* grid,
                               const float* d_positions, const float* d_states, int64_t batch,
                               int64_t n, float dt, const float* d_update_mask,
@@ -330,8 +331,8 @@ npa_status npa_executor_set_state_device(npa_executor* exec, const float* d_posi
 npa_status npa_executor_step_many(npa_executor* exec, int64_t steps, float dt, int32_t use_graph,
                                   void* stream);
 /* step_state_many with CUDA events recorded on `stream` around each phase of
- * each step: phase_ms receives steps*3 durations (hashgrid, density, fused
- * perception+MLP+Euler) and total_ms the whole span.  Synchronises `stream`. */
+ * each step: phase_ms receives steps*4 durations (hashgrid, density,
+ * perception, MLP+Euler) and total_ms the whole span.  Synchronises `stream`. */
 npa_status npa_executor_step_many_profiled(npa_executor* exec, int64_t steps, float dt,
                                            int32_t use_graph, void* stream, float* phase_ms,
                                            float* total_ms);
