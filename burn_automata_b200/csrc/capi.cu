@@ -247,7 +247,12 @@ struct PerceiveWorkspace {
   void* sort_scratch;
   size_t sort_scratch_bytes;
   float* tiles;  // step path only: feature tiles [tiles][F][tile_rows]
+  HitLists hits; // neighbour hits recorded by the density pass
 };
+
+// Hits kept per particle by the density pass (a particle with more is walked
+// again by the perception kernels).
+constexpr int kHitCap = 32;
 
 size_t tiles_floats(uint32_t batch, uint32_t n, int feature_dims, int tile_rows) {
   if (tile_rows <= 0) return 0;
@@ -264,8 +269,10 @@ size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n,
   c.take<uint32_t>(total);
   c.take<uint32_t>(total);
   c.take<float4>(total);
-  c.take<int4>(total);
+  c.take<int2>(total);
   c.take<float>(total);
+  c.take<uint32_t>(total * kHitCap);
+  c.take<uint32_t>(total);
   const size_t sort = hashgrid_scratch_bytes(g, batch, n);
   c.take<char>(sort);
   c.take<float>(extra_floats);
@@ -279,21 +286,27 @@ bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, s
   out->hg.bin_offsets = c.take<uint32_t>(size_t(batch) * g.cells + 1);
   out->hg.permutation = c.take<uint32_t>(total);
   out->hg.inverse = c.take<uint32_t>(total);
-  out->hg.spos = c.take<float4>(total);
-  out->hg.scoord = c.take<int4>(total);
+  out->hg.srec = c.take<float4>(total);
+  out->hg.scyz = c.take<int2>(total);
   out->volume = c.take<float>(total);
+  out->hits.slots = c.take<uint32_t>(total * kHitCap);
+  out->hits.count = c.take<uint32_t>(total);
+  out->hits.cap = kHitCap;
+  out->hits.stride = static_cast<uint32_t>(total);
   out->sort_scratch_bytes = hashgrid_scratch_bytes(g, batch, n);
   out->sort_scratch = c.take<char>(out->sort_scratch_bytes);
   out->tiles = extra_floats ? c.take<float>(extra_floats) : nullptr;
   return c.fits();
 }
 
-SortedGrid sorted_view(const PerceiveWorkspace& w, uint32_t n, uint32_t batch) {
+SortedGrid sorted_view(const PerceiveWorkspace& w, uint32_t n, uint32_t batch,
+                       const float* positions) {
   SortedGrid s;
   s.bin_offsets = w.hg.bin_offsets;
   s.permutation = w.hg.permutation;
-  s.spos = w.hg.spos;
-  s.scoord = w.hg.scoord;
+  s.srec = w.hg.srec;
+  s.scyz = w.hg.scyz;
+  s.positions = reinterpret_cast<const float4*>(positions);
   s.n = n;
   s.total = n * batch;
   return s;
@@ -457,8 +470,8 @@ npa_status npa_build_hashgrid(const npa_grid_config* cfg, const float* positions
   NPA_TRY(s.alloc(&hb.bin_offsets, size_t(B) * g.cells + 1));
   NPA_TRY(s.alloc(&hb.permutation, total));
   NPA_TRY(s.alloc(&hb.inverse, total));
-  NPA_TRY(s.alloc(&hb.spos, total));
-  NPA_TRY(s.alloc(&hb.scoord, total));
+  NPA_TRY(s.alloc(&hb.srec, total));
+  NPA_TRY(s.alloc(&hb.scyz, total));
   const size_t sb = hashgrid_scratch_bytes(g, B, N);
   char* scratch;
   NPA_TRY(s.alloc(&scratch, sb));
@@ -766,8 +779,8 @@ npa_status npa_dev_build_hashgrid(const npa_grid_config* cfg, const float* d_pos
   hb.bin_offsets = d_bin_offsets;
   hb.permutation = d_permutation;
   hb.inverse = d_inverse_permutation;
-  hb.spos = c.take<float4>(total);
-  hb.scoord = c.take<int4>(total);
+  hb.srec = c.take<float4>(total);
+  hb.scyz = c.take<int2>(total);
   const size_t sb = hashgrid_scratch_bytes(g, B, N);
   char* scratch = c.take<char>(sb);
   if (!c.fits()) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
@@ -809,9 +822,9 @@ npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
                           w.sort_scratch, w.sort_scratch_bytes, st));
-  const SortedGrid sv = sorted_view(w, N, B);
-  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, st));
-  return launch_perception(g, p, sv, B, d_states, int(state_dims), w.volume, d_features,
+  const SortedGrid sv = sorted_view(w, N, B, d_positions);
+  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, w.hits, st));
+  return launch_perception(g, p, sv, w.hits, B, d_states, int(state_dims), w.volume, d_features,
                            d_blurred_state, p.state_grad ? d_state_gradient : nullptr,
                            p.density_grad ? d_density_gradient : nullptr, st);
 }
@@ -889,9 +902,9 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
                           w.sort_scratch, w.sort_scratch_bytes, st));
-  const SortedGrid sv = sorted_view(w, N, B);
-  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, st));
-  NPA_TRY(launch_perception_tiles(g, p, sv, B, d_states, m->dm.state_dims, w.volume, tile_rows,
+  const SortedGrid sv = sorted_view(w, N, B, d_positions);
+  NPA_TRY(launch_density(g, sv, B, w.volume, d_density, w.hits, st));
+  NPA_TRY(launch_perception_tiles(g, p, sv, w.hits, B, d_states, m->dm.state_dims, w.volume, tile_rows,
                                   w.tiles, st));
   StepOutputs out;
   out.next_positions = reinterpret_cast<float4*>(d_next_positions);
@@ -936,15 +949,15 @@ namespace {
 
 npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cudaStream_t s) {
   const uint32_t B = uint32_t(e->batch), N = uint32_t(e->n);
-  const SortedGrid sv = sorted_view(e->w, N, B);
+  const SortedGrid sv = sorted_view(e->w, N, B, e->pos[from]);
   switch (phase) {
     case 0:
       return launch_hashgrid(e->g, reinterpret_cast<const float4*>(e->pos[from]), B, N, e->w.hg,
                              e->w.sort_scratch, e->w.sort_scratch_bytes, s);
     case 1:
-      return launch_density(e->g, sv, B, e->w.volume, nullptr, s);
+      return launch_density(e->g, sv, B, e->w.volume, nullptr, e->w.hits, s);
     case 2:
-      return launch_perception_tiles(e->g, e->p, sv, B, e->st[from], e->model->dm.state_dims,
+      return launch_perception_tiles(e->g, e->p, sv, e->w.hits, B, e->st[from], e->model->dm.state_dims,
                                      e->w.volume, e->tile_rows, e->w.tiles, s);
     default: {
       StepOutputs out;

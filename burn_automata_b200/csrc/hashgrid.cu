@@ -186,7 +186,7 @@ __global__ void finalize_kernel(GridParams g, const float4* __restrict__ pos,
                                 const uint32_t* __restrict__ vals, uint32_t total, uint32_t n,
                                 uint32_t total_bins, uint32_t* __restrict__ bin_offsets,
                                 uint32_t* __restrict__ perm, uint32_t* __restrict__ inv,
-                                float4* __restrict__ spos, int4* __restrict__ scoord) {
+                                float4* __restrict__ srec, int2* __restrict__ scyz) {
   const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= total) return;
   const uint32_t key = keys[q];
@@ -196,9 +196,13 @@ __global__ void finalize_kernel(GridParams g, const float4* __restrict__ pos,
   perm[q] = i - b * n;
   inv[i] = q - b * n;
   const float4 p = pos[i];
-  spos[q] = p;
   const int3 c = cell_coords(g, p);
-  scoord[q] = make_int4(c.x, c.y, c.z, 0);
+  if (g.dim == 2) {
+    srec[q] = make_float4(p.x, p.y, __int_as_float(c.x), __int_as_float(c.y));
+  } else {
+    srec[q] = make_float4(p.x, p.y, p.z, __int_as_float(c.x));
+    scyz[q] = make_int2(c.y, c.z);
+  }
   // bin_offsets[bin] = first sorted slot whose key >= bin.
   const uint32_t first = q == 0 ? 0u : keys[q - 1] + 1u;
   for (uint32_t bin = first; bin <= key; ++bin) bin_offsets[bin] = q;
@@ -221,7 +225,7 @@ uint32_t key_bits(uint64_t bins) {
 
 size_t sorted_view_bytes(uint32_t batch, uint32_t n) {
   const size_t total = size_t(batch) * n;
-  return ((total * sizeof(float4) + 255) & ~size_t(255)) + total * sizeof(int4) + 256;
+  return ((total * sizeof(float4) + 255) & ~size_t(255)) + total * sizeof(int2) + 256;
 }
 
 size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n) {
@@ -276,7 +280,7 @@ npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_
   }
   finalize_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
       g, positions, ka, va, total, n, bins, out.bin_offsets, out.permutation, out.inverse,
-      out.spos, out.scoord);
+      out.srec, out.scyz);
   return after_launch("finalize_kernel");
 }
 
@@ -347,8 +351,8 @@ extern "C" npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg,
   hb.bin_offsets = d_bin_offsets;
   hb.permutation = d_permutation;
   hb.inverse = d_inverse_permutation;
-  hb.spos = c.take<float4>(total);
-  hb.scoord = c.take<int4>(total);
+  hb.srec = c.take<float4>(total);
+  hb.scyz = c.take<int2>(total);
   const size_t sb = hashgrid_scratch_bytes(g, B, N);
   char* scratch = c.take<char>(sb);
   if (!c.fits()) return fail(NPA_ERR_UNSUPPORTED, "allocation-free hashgrid scratch is too small");

@@ -257,49 +257,135 @@ __device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
 struct SortedGrid {
   const uint32_t* bin_offsets;  // [B*cells + 1], global sorted slots
   const uint32_t* permutation;  // [B*N] local index of each sorted slot
-  const float4* spos;           // [B*N] positions in sorted order
-  const int4* scoord;           // [B*N] cell coordinates in sorted order
+  const float4* srec;           // [B*N] 2D {x, y, cx, cy}; 3D {x, y, z, cx} (cells as int bits)
+  const int2* scyz;             // [B*N] 3D only: {cy, cz}
+  const float4* positions;      // [B*N] caller-order positions (own position, w included)
   uint32_t n;                   // particles per batch
   uint32_t total;               // B*N: sorted slots are < total
 };
 
-// for_each_neighbor (neighbor.rs:3-44): cells in dz, dy, dx order, bin
-// ranges in permutation order, Particle-mode collision filter on exact
-// coordinates, keeps r2 < eps^2 including the particle itself.
-// visit(q, delta, r2) receives the sorted slot q of the neighbour.
-template <class Visit>
+// Neighbour record of sorted slot q: position (xyz) and cell coordinates.
+template <int DIM>
+__device__ __forceinline__ void load_record(const SortedGrid& s, uint32_t q, float4& pos,
+                                            int3& cell) {
+  const float4 r = __ldg(s.srec + q);
+  if (DIM == 2) {
+    pos = make_float4(r.x, r.y, 0.0f, 0.0f);
+    cell = make_int3(__float_as_int(r.z), __float_as_int(r.w), 0);
+  } else {
+    const int2 yz = __ldg(s.scyz + q);
+    pos = make_float4(r.x, r.y, r.z, 0.0f);
+    cell = make_int3(__float_as_int(r.w), yz.x, yz.y);
+  }
+}
+
+// Offsets of neighbour bin b in walk order (dz, dy, dx nested).
+template <int DIM>
+__device__ __forceinline__ int3 bin_delta(int b) {
+  if (DIM == 3) return make_int3(b % 3 - 1, (b / 3) % 3 - 1, b / 9 - 1);
+  return make_int3(b % 3 - 1, b / 3 - 1, 0);
+}
+
+__device__ __forceinline__ int3 add_wrapping(int3 c, int3 d) {
+  return make_int3(static_cast<int>(static_cast<uint32_t>(c.x) + static_cast<uint32_t>(d.x)),
+                   static_cast<int>(static_cast<uint32_t>(c.y) + static_cast<uint32_t>(d.y)),
+                   static_cast<int>(static_cast<uint32_t>(c.z) + static_cast<uint32_t>(d.z)));
+}
+
+// for_each_neighbor (neighbor.rs:3-44): cells in dz, dy, dx order, bin ranges
+// in permutation order, Particle-mode collision filter on exact coordinates,
+// keeps r2 < eps^2 including the particle itself.  The candidates of all
+// bins are walked as one flattened sequence (same order), so the threads of a
+// warp iterate max(total candidates) rather than the per-bin maximum once per
+// bin, and the records of KB consecutive candidates are loaded before any is
+// tested, so their round trips to L2 overlap.  visit(q, delta, r2) receives
+// the neighbour's sorted slot, in walk order.
+template <int DIM, int KB = 4, class Visit>
 __device__ __forceinline__ void for_each_neighbor(const GridParams& g, const SortedGrid& s,
                                                   uint32_t batch, float4 pi, int3 center,
                                                   Visit&& visit) {
-  const int zmin = g.dim == 3 ? -1 : 0;
-  const int zmax = g.dim == 3 ? 1 : 0;
+  constexpr int NB = DIM == 3 ? 27 : 9;
   const uint32_t bin_base = batch * g.cells;
-  for (int dz = zmin; dz <= zmax; ++dz) {
-    for (int dy = -1; dy <= 1; ++dy) {
-      for (int dx = -1; dx <= 1; ++dx) {
-        const int cx = static_cast<int>(static_cast<uint32_t>(center.x) + static_cast<uint32_t>(dx));
-        const int cy = static_cast<int>(static_cast<uint32_t>(center.y) + static_cast<uint32_t>(dy));
-        const int cz = static_cast<int>(static_cast<uint32_t>(center.z) + static_cast<uint32_t>(dz));
-        long long cell = cell_index(g, cx, cy, cz);
-        if (cell < 0) continue;
-        const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
-        const uint32_t begin = __ldg(s.bin_offsets + bin);
-        const uint32_t end = min(__ldg(s.bin_offsets + bin + 1), s.total);
-        for (uint32_t q = begin; q < end; ++q) {
-          if (g.mode == kModeParticle) {
-            const int4 cq = __ldg(s.scoord + q);
-            if (cq.x != cx || cq.y != cy || cq.z != cz) continue;
-          }
-          const float4 pj = __ldg(s.spos + q);
-          const float4 d = neighbor_delta(g, pi, pj);
-          float r2 = d.x * d.x;
-          r2 = r2 + d.y * d.y;
-          if (g.dim == 3) r2 = r2 + d.z * d.z;
-          if (r2 < g.eps2) visit(q, d, r2);
+  uint32_t beg[NB], cum[NB];
+  uint32_t ncand = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int3 nc = add_wrapping(center, bin_delta<DIM>(b));
+    const long long cell = cell_index(g, nc.x, nc.y, nc.z);
+    uint32_t lo = 0, cnt = 0;
+    if (cell >= 0) {
+      const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
+      lo = __ldg(s.bin_offsets + bin);
+      const uint32_t hi = min(__ldg(s.bin_offsets + bin + 1), s.total);
+      cnt = hi > lo ? hi - lo : 0u;
+    }
+    beg[b] = lo;
+    ncand += cnt;
+    cum[b] = ncand;
+  }
+  int b = 0;
+  uint32_t cur_beg = beg[0], cur_lo = 0, cur_hi = cum[0];
+  for (uint32_t v0 = 0; v0 < ncand; v0 += KB) {
+    uint32_t qs[KB];
+    int bs[KB];
+    float4 pj[KB];
+    int3 cj[KB];
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      const uint32_t v = v0 + u;
+      qs[u] = 0;
+      bs[u] = b;
+      if (v < ncand) {
+        while (v >= cur_hi) {  // advance to the bin holding candidate v
+          ++b;
+          cur_lo = cur_hi;
+#pragma unroll
+          for (int k = 1; k < NB; ++k)
+            if (k == b) {
+              cur_beg = beg[k];
+              cur_hi = cum[k];
+            }
         }
+        bs[u] = b;
+        qs[u] = cur_beg + (v - cur_lo);
+        load_record<DIM>(s, qs[u], pj[u], cj[u]);
       }
     }
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      if (v0 + u >= ncand) break;
+      if (g.mode == kModeParticle) {
+        const int3 want = add_wrapping(center, bin_delta<DIM>(bs[u]));
+        if (cj[u].x != want.x || cj[u].y != want.y || cj[u].z != want.z) continue;
+      }
+      const float4 d = neighbor_delta(g, pi, pj[u]);
+      float r2 = d.x * d.x;
+      r2 = r2 + d.y * d.y;
+      if (DIM == 3) r2 = r2 + d.z * d.z;
+      if (r2 < g.eps2) visit(qs[u], d, r2);
+    }
   }
+}
+
+// Neighbour lists recorded by the density pass: the sorted slots of a
+// particle's hits in walk order, at most `cap` per particle; a particle with
+// more hits stores count = cap + 1 and is walked again from the hashgrid.
+// Hit e of slot q lives at slots[e * stride + q], so the threads of a warp
+// (consecutive slots) write and read consecutive words.
+struct HitLists {
+  uint32_t* slots;   // [cap][stride]
+  uint32_t* count;   // [B*N]
+  int cap;
+  uint32_t stride;   // >= B*N
+};
+
+// Cell coordinates of sorted slot q (from its record).
+template <int DIM>
+__device__ __forceinline__ int3 slot_cell(const SortedGrid& s, uint32_t q) {
+  float4 p;
+  int3 c;
+  load_record<DIM>(s, q, p, c);
+  return c;
 }
 
 }  // namespace npa

@@ -57,12 +57,12 @@ struct HashgridBuffers {
   uint32_t* bin_offsets;   // [B*cells + 1]
   uint32_t* permutation;   // [B*N]
   uint32_t* inverse;       // [B*N]
-  float4* spos;            // [B*N] sorted positions
-  int4* scoord;            // [B*N] sorted cell coordinates
+  float4* srec;            // [B*N] sorted neighbour records (position + cell)
+  int2* scyz;              // [B*N] 3D cell y, z (unused in 2D)
 };
 // Bytes of scratch the sort needs beyond HashgridBuffers.
 size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n);
-// Size of the sorted views (spos + scoord).
+// Size of the sorted views (srec + scyz).
 size_t sorted_view_bytes(uint32_t batch, uint32_t n);
 npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_t batch,
                            uint32_t n, const HashgridBuffers& out, void* scratch,
@@ -79,19 +79,21 @@ struct PerceptionParams {
 };
 PerceptionParams make_perception_params(const GridParams& g, const npa_perception_options& o,
                                         uint32_t n, int state_dims);
-// density + volume per sorted slot; density_out (original order) optional.
+// density + volume per sorted slot; density_out (original order) optional;
+// hit lists recorded when hl.slots is set.
 npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t batch,
-                          float* volume_sorted, float* density_out, cudaStream_t stream);
+                          float* volume_sorted, float* density_out, const HitLists& hl,
+                          cudaStream_t stream);
 // Standalone perception writing features / intermediates in original order.
 npa_status launch_perception(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
-                             uint32_t batch, const float* states, int state_dims,
+                             const HitLists& hl, uint32_t batch, const float* states, int state_dims,
                              const float* volume_sorted, float* features, float* blurred,
                              float* state_gradient, float* density_gradient,
                              cudaStream_t stream);
 // Step path: feature rows of `tile_rows` sorted slots stored feature-major per
 // tile ([tile][F][tile_rows]); rows past B*N are zero.
 npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
-                                   const SortedGrid& s, uint32_t batch, const float* states,
+                                   const SortedGrid& s, const HitLists& hl, uint32_t batch, const float* states,
                                    int state_dims, const float* volume_sorted, int tile_rows,
                                    float* tiles, cudaStream_t stream);
 

@@ -1,14 +1,13 @@
 // perception.cu -- density pass and SPH perception
 // (perceive_with_options, crates/burn_automata_kernels/src/reference/forward.rs:26-143).
 //
-// All kernels run over sorted slots, so the threads of a warp walk
-// neighbouring bins and read the sorted position / coordinate views
-// contiguously.  DIM (2 or 3) and the channel chunk CH are template
-// parameters: every accumulator is a register.
+// All kernels run one thread per sorted slot and 8-channel chunk, so the threads of a warp walk neighbouring bins and read the
+// sorted neighbour records contiguously.  DIM (2 or 3) and the channel chunk
+// CH are template parameters: every accumulator is a register.
 //   density_kernel          rho and 1/rho per sorted slot (forward.rs:145-160)
 //   perception_kernel       API output: features and intermediates in the
 //                           caller's particle order
-//   perception_tiles_kernel step path: the feature rows of kTileRows sorted
+//   perception_tiles_kernel step path: the feature rows of `tile_rows` sorted
 //                           slots stored feature-major ([tile][F][rows]), the
 //                           layout the MLP kernel stages into shared memory
 #include "perception_core.cuh"
@@ -19,20 +18,27 @@ namespace {
 template <int DIM>
 __global__ void __launch_bounds__(256)
 density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ volume,
-               float* __restrict__ density_out) {
+               float* __restrict__ density_out, HitLists hl) {
   const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= total) return;
   const uint32_t batch = q / s.n;
-  const float4 pi = s.spos[q];
-  const int4 c4 = s.scoord[q];
+  float4 pi;
+  int3 c;
+  load_record<DIM>(s, q, pi, c);
   float rho = 0.0f;
-  for_each_neighbor(g, s, batch, pi, make_int3(c4.x, c4.y, c4.z),
-                    [&](uint32_t, float4, float r2) { rho = rho + poly6(g, r2); });
+  uint32_t hits = 0;
+  uint32_t* list = hl.slots ? hl.slots + q : nullptr;
+  for_each_neighbor<DIM, 4>(g, s, batch, pi, c, [&](uint32_t qj, float4, float r2) {
+    rho = rho + poly6(g, r2);
+    if (list && hits < uint32_t(hl.cap)) list[size_t(hits) * hl.stride] = qj;
+    ++hits;
+  });
+  if (list) hl.count[q] = min(hits, uint32_t(hl.cap + 1));
   volume[q] = recip_finite(rho);
   if (density_out) density_out[size_t(batch) * s.n + s.permutation[q]] = rho;
 }
 
-template <int DIM, int CH>
+template <int CH>
 __device__ __forceinline__ void load_own(const float* __restrict__ states, size_t row, int C,
                                          int c0, float (&si)[CH]) {
 #pragma unroll
@@ -41,7 +47,7 @@ __device__ __forceinline__ void load_own(const float* __restrict__ states, size_
 
 template <int DIM, int CH>
 __global__ void __launch_bounds__(128)
-perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total,
+perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, uint32_t total,
                   const float* __restrict__ states, int C, int chunks,
                   const float* __restrict__ volume, float* __restrict__ features,
                   float* __restrict__ blurred, float* __restrict__ state_gradient,
@@ -53,24 +59,23 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total
   const int c0 = chunk * CH;
   const uint32_t batch = q / s.n;
   const size_t row = size_t(batch) * s.n + s.permutation[q];
-  const float4 pi = s.spos[q];
-  const int4 c4 = s.scoord[q];
+  const float4 pi = __ldg(s.positions + row);
+  const int3 c = slot_cell<DIM>(s, q);
   float si[CH];
-  load_own<DIM, CH>(states, row, C, c0, si);
+  load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
-                          volume, si, a);
+  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a);
   const size_t F = p.feature_dims;
   float* f = features + row * F;
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi, [&](int k, float v) { f[k] = v; });
 #pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const int ch = c0 + c;
+  for (int k = 0; k < CH; ++k) {
+    const int ch = c0 + k;
     if (ch < C) {
-      if (blurred) blurred[row * C + ch] = a.blur[c];
+      if (blurred) blurred[row * C + ch] = a.blur[k];
       if (state_gradient && p.state_grad)
 #pragma unroll
-        for (int d = 0; d < DIM; ++d) state_gradient[(row * C + ch) * DIM + d] = a.sgrad[c][d];
+        for (int d = 0; d < DIM; ++d) state_gradient[(row * C + ch) * DIM + d] = a.sgrad[k][d];
     }
   }
   if (chunk == 0 && density_gradient && p.density_grad)
@@ -80,8 +85,8 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total
 
 template <int DIM, int CH>
 __global__ void __launch_bounds__(128)
-perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t total,
-                        uint32_t padded, const float* __restrict__ states, int C, int chunks,
+perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl,
+                        uint32_t total, uint32_t padded, const float* __restrict__ states, int C, int chunks,
                         const float* __restrict__ volume, int tile_rows,
                         float* __restrict__ tiles) {
   const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -97,13 +102,12 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, uint32_t
   }
   const uint32_t batch = q / s.n;
   const size_t row = size_t(batch) * s.n + s.permutation[q];
-  const float4 pi = s.spos[q];
-  const int4 c4 = s.scoord[q];
+  const float4 pi = __ldg(s.positions + row);
+  const int3 c = slot_cell<DIM>(s, q);
   float si[CH];
-  load_own<DIM, CH>(states, row, C, c0, si);
+  load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, batch, q, pi, make_int3(c4.x, c4.y, c4.z), states, C, c0,
-                          volume, si, a);
+  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a);
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
                          [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
 }
@@ -124,8 +128,9 @@ float powi_f32(float x, int n) {
   return have ? result : 1.0f;
 }
 
-// Channels per thread: all of them up to 16, else chunks of 16.
-int chunk_channels(int C) { return C <= 4 ? 4 : (C <= 8 ? 8 : 16); }
+// Channels per thread: 8 (measured on cfg2: two threads of 8 channels per
+// particle beat one of 16 -- 0.54 vs 0.72 ms -- through twice the occupancy).
+int chunk_channels(int C) { return C <= 4 ? 4 : 8; }
 
 }  // namespace
 
@@ -152,31 +157,21 @@ PerceptionParams make_perception_params(const GridParams& g, const npa_perceptio
 }
 
 npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t batch,
-                          float* volume_sorted, float* density_out, cudaStream_t stream) {
+                          float* volume_sorted, float* density_out, const HitLists& hl,
+                          cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
   if (g.dim == 2)
-    density_kernel<2><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted, density_out);
+    density_kernel<2><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted,
+                                                                density_out, hl);
   else
-    density_kernel<3><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted, density_out);
+    density_kernel<3><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted,
+                                                                density_out, hl);
   return after_launch("density_kernel");
 }
 
-template <int DIM, int CH>
-static void launch_perception_t(const GridParams& g, const PerceptionParams& p,
-                                const SortedGrid& s, uint32_t total, const float* states, int C,
-                                const float* volume, float* features, float* blurred,
-                                float* state_gradient, float* density_gradient,
-                                cudaStream_t stream) {
-  const int chunks = C > 0 ? (C + CH - 1) / CH : 1;
-  const uint64_t threads = uint64_t(total) * chunks;
-  perception_kernel<DIM, CH><<<grid_for(threads, 128), 128, 0, stream>>>(
-      g, p, s, total, states, C, chunks, volume, features, blurred, state_gradient,
-      density_gradient);
-}
-
 npa_status launch_perception(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
-                             uint32_t batch, const float* states, int state_dims,
+                             const HitLists& hl, uint32_t batch, const float* states, int state_dims,
                              const float* volume_sorted, float* features, float* blurred,
                              float* state_gradient, float* density_gradient,
                              cudaStream_t stream) {
@@ -185,9 +180,13 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
   PerceptionParams pp = p;
   pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
   const int ch = chunk_channels(state_dims);
+  const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
+  const unsigned blocks = grid_for(uint64_t(total) * chunks, 128);
 #define NPA_PERC(D, CHV)                                                                      \
-  launch_perception_t<D, CHV>(g, pp, s, total, states, state_dims, volume_sorted, features,   \
-                              blurred, state_gradient, density_gradient, stream)
+  perception_kernel<D, CHV><<<blocks, 128, 0, stream>>>(g, pp, s, hl, total, states, state_dims, \
+                                                        chunks, volume_sorted, features,      \
+                                                        blurred, state_gradient,              \
+                                                        density_gradient)
   if (g.dim == 2) {
     if (ch == 4) NPA_PERC(2, 4); else if (ch == 8) NPA_PERC(2, 8); else NPA_PERC(2, 16);
   } else {
@@ -197,30 +196,21 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
   return after_launch("perception_kernel");
 }
 
-template <int DIM, int CH>
-static void launch_tiles_t(const GridParams& g, const PerceptionParams& p, const SortedGrid& s,
-                           uint32_t total, uint32_t padded, const float* states, int C,
-                           const float* volume, int tile_rows, float* tiles,
-                           cudaStream_t stream) {
-  const int chunks = C > 0 ? (C + CH - 1) / CH : 1;
-  const uint64_t threads = uint64_t(padded) * chunks;
-  perception_tiles_kernel<DIM, CH><<<grid_for(threads, 128), 128, 0, stream>>>(
-      g, p, s, total, padded, states, C, chunks, volume, tile_rows, tiles);
-}
-
 npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
-                                   const SortedGrid& s, uint32_t batch, const float* states,
+                                   const SortedGrid& s, const HitLists& hl, uint32_t batch, const float* states,
                                    int state_dims, const float* volume_sorted, int tile_rows,
                                    float* tiles, cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
   const uint32_t padded = (total + tile_rows - 1) / tile_rows * tile_rows;
-  const int ch = chunk_channels(state_dims);
   PerceptionParams pp = p;
   pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
-#define NPA_TILES(D, CHV)                                                                    \
-  launch_tiles_t<D, CHV>(g, pp, s, total, padded, states, state_dims, volume_sorted,         \
-                         tile_rows, tiles, stream)
+  const int ch = chunk_channels(state_dims);
+  const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
+  const unsigned blocks = grid_for(uint64_t(padded) * chunks, 128);
+#define NPA_TILES(D, CHV)                                                                     \
+  perception_tiles_kernel<D, CHV><<<blocks, 128, 0, stream>>>(                                \
+      g, pp, s, hl, total, padded, states, state_dims, chunks, volume_sorted, tile_rows, tiles)
   if (g.dim == 2) {
     if (ch == 4) NPA_TILES(2, 4); else if (ch == 8) NPA_TILES(2, 8); else NPA_TILES(2, 16);
   } else {

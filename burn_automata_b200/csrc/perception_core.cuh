@@ -34,95 +34,103 @@ __device__ __forceinline__ void log_normalize_n(float (&v)[DIM]) {
   for (int i = 0; i < DIM; ++i) v[i] = v[i] * scale;
 }
 
-// CH channels [c0, c0 + CH) of the particle in sorted slot q.  `states` is the
-// caller-order state matrix [B*N][C]; `volume` is recip_finite(density) per
-// sorted slot; `si` holds the particle's own channels.  Channels >= C stay 0.
+// Accumulators of one particle's chunk plus the moment matrix.
 template <int DIM, int CH>
-__device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
-                                               const SortedGrid& s, uint32_t batch, uint32_t q,
-                                               float4 pi, int3 center,
-                                               const float* __restrict__ states, int C, int c0,
-                                               const float* __restrict__ volume,
-                                               const float (&si)[CH],
-                                               PerceptionAcc<DIM, CH>& out) {
-  const bool both = p.state_grad && p.density_grad;
-  const uint32_t batch_base = batch * s.n;
+struct ChunkState {
+  PerceptionAcc<DIM, CH> acc;
   float moment[DIM][DIM];
+};
+
+template <int DIM, int CH>
+__device__ __forceinline__ void chunk_init(ChunkState<DIM, CH>& st) {
 #pragma unroll
   for (int r = 0; r < DIM; ++r)
 #pragma unroll
-    for (int c = 0; c < DIM; ++c) moment[r][c] = 0.0f;
+    for (int c = 0; c < DIM; ++c) st.moment[r][c] = 0.0f;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
-    out.blur[c] = 0.0f;
+    st.acc.blur[c] = 0.0f;
 #pragma unroll
-    for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = 0.0f;
+    for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = 0.0f;
   }
 #pragma unroll
-  for (int a = 0; a < DIM; ++a) out.dgrad[a] = 0.0f;
-  const bool full_chunk = c0 + CH <= C;
-  const bool vec4 = p.vec_states && ((C & 3) == 0) && ((c0 & 3) == 0) && (CH % 4 == 0) && full_chunk;
+  for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = 0.0f;
+}
 
-  for_each_neighbor(g, s, batch, pi, center, [&](uint32_t qj, float4 d, float r2) {
-    const float vol = __ldg(volume + qj);
-    const float smooth = poly6(g, r2);
-    const float* sj = states + size_t(batch_base + __ldg(s.permutation + qj)) * C + c0;
-    float sjv[CH];
-    if (vec4) {
+// Loads CH channels of state row `row` (float4 when aligned and whole).
+template <int CH>
+__device__ __forceinline__ void load_row(const float* __restrict__ states, size_t row, int C,
+                                         int c0, bool vec4, float (&out)[CH]) {
+  const float* sj = states + row * C + c0;
+  if (vec4) {
 #pragma unroll
-      for (int c = 0; c < CH; c += 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(sj + c));
-        sjv[c] = v.x;
-        sjv[c + 1] = v.y;
-        sjv[c + 2] = v.z;
-        sjv[c + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < CH; ++c) sjv[c] = (c0 + c < C) ? __ldg(sj + c) : 0.0f;
+    for (int c = 0; c < CH; c += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(sj + c));
+      out[c] = v.x;
+      out[c + 1] = v.y;
+      out[c + 2] = v.z;
+      out[c + 3] = v.w;
     }
-    if (both) {
+  } else {
 #pragma unroll
-      for (int c = 0; c < CH; ++c) out.blur[c] = out.blur[c] + sjv[c] * smooth * vol;
-    } else {
-      const float w = smooth * vol;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) out.blur[c] = out.blur[c] + sjv[c] * w;
-    }
-    if (qj == q) return;
-    const float dv[3] = {d.x, d.y, d.z};
-    if (p.density_grad) {
-      const float m1 = spiky_mag(g, r2, 1.0f);
-#pragma unroll
-      for (int a = 0; a < DIM; ++a) out.dgrad[a] = out.dgrad[a] + m1 * dv[a];
-    }
-    if (p.state_grad) {
-      const float mv = spiky_mag(g, r2, vol);
-      float gv[DIM];
-#pragma unroll
-      for (int a = 0; a < DIM; ++a) gv[a] = mv * dv[a];
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const float diff = sjv[c] - si[c];
-#pragma unroll
-        for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = out.sgrad[c][a] + diff * gv[a];
-      }
-      if (p.hybrid) {
-#pragma unroll
-        for (int r = 0; r < DIM; ++r)
-#pragma unroll
-          for (int col = 0; col < DIM; ++col) moment[r][col] = moment[r][col] + dv[r] * gv[col];
-      }
-    }
-  });
+    for (int c = 0; c < CH; ++c) out[c] = (c0 + c < C) ? __ldg(sj + c) : 0.0f;
+  }
+}
 
+// One neighbour's terms (second_pass_particle, forward.rs:249-295, or the
+// separate passes of the other branch), added in the reference's order.
+template <int DIM, int CH>
+__device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionParams& p,
+                                          bool self, float4 d, float r2, float vol,
+                                          const float (&sjv)[CH], const float (&si)[CH],
+                                          ChunkState<DIM, CH>& st) {
+  const float smooth = poly6(g, r2);
+  if (p.state_grad && p.density_grad) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) st.acc.blur[c] = st.acc.blur[c] + sjv[c] * smooth * vol;
+  } else {
+    const float w = smooth * vol;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) st.acc.blur[c] = st.acc.blur[c] + sjv[c] * w;
+  }
+  if (self) return;
+  const float dv[3] = {d.x, d.y, d.z};
+  if (p.density_grad) {
+    const float m1 = spiky_mag(g, r2, 1.0f);
+#pragma unroll
+    for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = st.acc.dgrad[a] + m1 * dv[a];
+  }
+  if (p.state_grad) {
+    const float mv = spiky_mag(g, r2, vol);
+    float gv[DIM];
+#pragma unroll
+    for (int a = 0; a < DIM; ++a) gv[a] = mv * dv[a];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const float diff = sjv[c] - si[c];
+#pragma unroll
+      for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = st.acc.sgrad[c][a] + diff * gv[a];
+    }
+    if (p.hybrid) {
+#pragma unroll
+      for (int r = 0; r < DIM; ++r)
+#pragma unroll
+        for (int col = 0; col < DIM; ++col)
+          st.moment[r][col] = st.moment[r][col] + dv[r] * gv[col];
+    }
+  }
+}
+
+// Moment correction (normalize.rs:93-118) and gradient normalisation (:5-58).
+template <int DIM, int CH>
+__device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkState<DIM, CH>& st) {
   if (p.state_grad) {
     if (p.hybrid) {
       float m9[9], inv[9];
 #pragma unroll
       for (int r = 0; r < DIM; ++r)
 #pragma unroll
-        for (int c = 0; c < DIM; ++c) m9[r * DIM + c] = moment[r][c];
+        for (int c = 0; c < DIM; ++c) m9[r * DIM + c] = st.moment[r][c];
       safe_inverse_symmetric(m9, DIM, inv);
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
@@ -132,24 +140,82 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
           corrected[oa] = 0.0f;
 #pragma unroll
           for (int ia = 0; ia < DIM; ++ia)
-            corrected[oa] = corrected[oa] + out.sgrad[c][ia] * inv[ia * DIM + oa];
+            corrected[oa] = corrected[oa] + st.acc.sgrad[c][ia] * inv[ia * DIM + oa];
         }
 #pragma unroll
-        for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = corrected[a];
+        for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = corrected[a];
       }
     }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
 #pragma unroll
-      for (int a = 0; a < DIM; ++a) out.sgrad[c][a] = out.sgrad[c][a] * p.state_scale;
-      if (p.log_norm_grad) log_normalize_n<DIM>(out.sgrad[c]);
+      for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = st.acc.sgrad[c][a] * p.state_scale;
+      if (p.log_norm_grad) log_normalize_n<DIM>(st.acc.sgrad[c]);
     }
   }
   if (p.density_grad) {
 #pragma unroll
-    for (int a = 0; a < DIM; ++a) out.dgrad[a] = out.dgrad[a] * p.density_scale;
-    if (p.log_norm_density_grad) log_normalize_n<DIM>(out.dgrad);
+    for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = st.acc.dgrad[a] * p.density_scale;
+    if (p.log_norm_density_grad) log_normalize_n<DIM>(st.acc.dgrad);
   }
+}
+
+// CH channels [c0, c0 + CH) of the particle in sorted slot q.  `states` is the
+// caller-order state matrix [B*N][C]; `volume` is recip_finite(density) per
+// sorted slot; `si` holds the particle's own channels.  Channels >= C stay 0.
+// The neighbours come from the density pass's hit list when it holds them all,
+// otherwise from a fresh hashgrid walk; both give the walk order.
+template <int DIM, int CH>
+__device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
+                                               const SortedGrid& s, const HitLists& hl,
+                                               uint32_t batch, uint32_t q, float4 pi,
+                                               int3 center, const float* __restrict__ states,
+                                               int C, int c0, const float* __restrict__ volume,
+                                               const float (&si)[CH],
+                                               PerceptionAcc<DIM, CH>& out) {
+  const uint32_t batch_base = batch * s.n;
+  const bool vec4 = p.vec_states && ((C & 3) == 0) && ((c0 & 3) == 0) && (CH % 4 == 0) &&
+                    (c0 + CH <= C);
+  ChunkState<DIM, CH> st;
+  chunk_init(st);
+  const uint32_t nh = hl.slots ? __ldg(hl.count + q) : uint32_t(hl.cap + 1);
+  if (nh <= uint32_t(hl.cap)) {
+    const uint32_t* list = hl.slots + q;
+    for (uint32_t e0 = 0; e0 < nh; e0 += 2) {
+      uint32_t qj[2];
+      float4 pj[2];
+      int3 cj[2];
+      float vol[2];
+      uint32_t prow[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        qj[u] = (e0 + u < nh) ? __ldg(list + size_t(e0 + u) * hl.stride) : q;
+        load_record<DIM>(s, qj[u], pj[u], cj[u]);
+        vol[u] = __ldg(volume + qj[u]);
+        prow[u] = batch_base + __ldg(s.permutation + qj[u]);
+      }
+      float sj[2][CH];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) load_row<CH>(states, prow[u], C, c0, vec4, sj[u]);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (e0 + u >= nh) break;
+        const float4 d = neighbor_delta(g, pi, pj[u]);
+        float r2 = d.x * d.x;
+        r2 = r2 + d.y * d.y;
+        if (DIM == 3) r2 = r2 + d.z * d.z;
+        chunk_add<DIM, CH>(g, p, qj[u] == q, d, r2, vol[u], sj[u], si, st);
+      }
+    }
+  } else {
+    for_each_neighbor<DIM>(g, s, batch, pi, center, [&](uint32_t qn, float4 d, float r2) {
+      float sjv[CH];
+      load_row<CH>(states, batch_base + __ldg(s.permutation + qn), C, c0, vec4, sjv);
+      chunk_add<DIM, CH>(g, p, qn == q, d, r2, __ldg(volume + qn), sjv, si, st);
+    });
+  }
+  chunk_finish<DIM, CH>(p, st);
+  out = st.acc;
 }
 
 // Visits the feature row [s | blur | grad (c*DIM+a) | dgrad? | pos?] of one

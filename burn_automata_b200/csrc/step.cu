@@ -377,7 +377,7 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
       norm = sqrtf(norm);
       float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int a = 0; a < D; ++a) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
-      const float4 pi = sg.spos[q];
+      const float4 pi = __ldg(sg.positions + row);
       float state_gate = 1.0f;
       if (sp.gates3d) {
         // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
