@@ -360,24 +360,33 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
     cp_async_wait<1>();
     __syncthreads();
     const float* ft = ftb[buf];
+    // The epilogue's global reads are issued before layer 1 so their latency
+    // is hidden behind it.
+    const int r = threadIdx.x / s.tpr;
+    const int part = threadIdx.x - r * s.tpr;
+    const uint32_t q = tile * s.M + r;
+    const bool live = q < total;
+    size_t row = 0;
+    float4 pi = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = 1.0f;
+    if (live) {
+      const uint32_t batch = q / sg.n;
+      row = size_t(batch) * sg.n + __ldg(sg.permutation + q);
+      pi = __ldg(sg.positions + row);
+      if (mask) m = __ldg(mask + row);
+    }
     mlp_layer1<HG>(s, w1t, b1, ft, w1s, hid);
     __syncthreads();
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
     // forward_from_features_with_eps + gates + euler_step, tpr threads per row
-    const int r = threadIdx.x / s.tpr;
-    const int part = threadIdx.x - r * s.tpr;
-    const uint32_t q = tile * s.M + r;
-    if (q < total) {
-      const uint32_t batch = q / sg.n;
-      const size_t row = size_t(batch) * sg.n + sg.permutation[q];
+    if (live) {
       const float* u = outs + r * s.out_stride;
       float norm = 0.0f;
       for (int a = 0; a < D; ++a) norm = norm + u[a] * u[a];
       norm = sqrtf(norm);
       float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int a = 0; a < D; ++a) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
-      const float4 pi = __ldg(sg.positions + row);
       float state_gate = 1.0f;
       if (sp.gates3d) {
         // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
@@ -388,7 +397,6 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
         if (!(pi.w >= 0.5f)) motion_gate = state_gate * clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
         for (int a = 0; a < D; ++a) dx[a] = dx[a] * motion_gate;
       }
-      const float m = mask ? __ldg(mask + row) : 1.0f;
       if (part == 0) {
         next_pos[row] = euler_position(g, ep, pi, dx, m);
         if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
