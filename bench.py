@@ -216,15 +216,14 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     import burn_automata_b200 as ba
-    from burn_automata_b200 import workloads
+    from burn_automata_b200 import multigpu, workloads
 
     torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
-                                device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank)
+    multigpu.init("nccl", multigpu.RankInfo(rank, world, local_rank), timeout_s=180, device=dev)
     lib = ba.load_library()
-    per_rank = args.rollouts or (BATCH_TOTAL // world if args.strong else BATCH_TOTAL)
-    first = rank * per_rank
+    total_rollouts = args.rollouts or BATCH_TOTAL
+    first, per_rank = multigpu.shard(total_rollouts, world, rank, args.strong)
     w = workloads.make(args.workload, batch=per_rank, first=first)
     model = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
                                                w.weights.b2), device=local_rank)
@@ -253,15 +252,15 @@ def run_ours(args, rank, world, local_rank):
     launches = lib.npa_kernel_launch_count() - launches0
     if world > 1:
         dist.barrier()
-    t = torch.tensor([total_ms, float(phase_ms[:, 3].mean())], dtype=torch.float64,
-                     device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms, fused_ms = float(t[0]), float(t[1])
+    max_ms, fused_ms = multigpu.max_over_ranks([total_ms, float(phase_ms[:, 3].mean())], dev)
     clocks = sampler.stop(visible_gpu_indices(world)) if sampler else None
 
     particles_rank = w.batch * w.n
-    particles_job = particles_rank * world
+    # all ranks' particles (strong scaling may give ranks unequal shares)
+    cnt = torch.tensor([float(particles_rank)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(cnt)
+    particles_job = int(cnt.item())
     value = particles_job * args.steps / (max_ms / 1000.0)
 
     # e2e through the public rollout API with host buffers (rank-local, then max).
@@ -281,16 +280,17 @@ def run_ours(args, rank, world, local_rank):
         out_pos.numpy()[:] = p_
         out_st.numpy()[:] = s_
         e2e_s = time.perf_counter() - t0
-        te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_s = float(te[0])
+        e2e_s = multigpu.max_over_ranks([e2e_s], dev)[0]
         h2d = w.positions.nbytes + w.states.nbytes
         e2e = {"value": particles_job * args.steps / e2e_s, "unit": "particle-steps/s",
                "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": h2d / args.steps,
                "api": "CudaAutomataExecutor create_state + step_state_many + read_state",
                "note": "one upload of the initial particles and one readback of the final "
                        "particles per K-step rollout (per-step bytes are amortised)"}
+
+    # one gather of per-shard checksums of the final states (validation only)
+    fp, fs = ex.read_state()
+    checksums = multigpu.gather_checksums(multigpu.shard_checksum(fp, fs), dev)
 
     if rank == 0:
         peak, peak_kind = load_peaks()
@@ -338,13 +338,14 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "final_state_checksums": checksums,
         }
         print(json.dumps(line), flush=True)
     ex.close()
     model.close()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+    multigpu.finish()
 
 
 def main():
