@@ -95,7 +95,8 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
 npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
                                    const SortedGrid& s, const HitLists& hl, uint32_t batch, const float* states,
                                    int state_dims, const float* volume_sorted, int tile_rows,
-                                   float* tiles, cudaStream_t stream);
+                                   float* tiles, cudaStream_t stream, uint32_t tile_begin = 0,
+                                   uint32_t tile_end = 0xffffffffu);
 
 // ---- model / step (step.cu) ----
 struct DeviceModel {
@@ -128,9 +129,11 @@ int hidden_padded_for(int hidden);
 int step_tile_rows(const DeviceModel& m);
 bool mlp_step_supported(const DeviceModel& m);
 // MLP + dx/ds (+3D gates) + Euler over feature tiles in sorted order.
+// Tiles [tile_begin, tile_end) of the step (default: all).
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& s,
                            uint32_t batch, const float* tiles, float dt, const float* mask,
-                           const StepOutputs& out, cudaStream_t stream);
+                           const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
+                           uint32_t tile_end = 0xffffffffu);
 
 // ---- decode (decode.cu) ----
 npa_status launch_decode(const npa_gaussian_decode_config& cfg, const float4* positions,

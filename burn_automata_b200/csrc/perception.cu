@@ -10,6 +10,8 @@
 //   perception_tiles_kernel step path: the feature rows of `tile_rows` sorted
 //                           slots stored feature-major ([tile][F][rows]), the
 //                           layout the MLP kernel stages into shared memory
+#include <algorithm>
+
 #include "perception_core.cuh"
 
 namespace npa {
@@ -86,13 +88,14 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
 template <int DIM, int CH>
 __global__ void __launch_bounds__(128)
 perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl,
-                        uint32_t total, uint32_t padded, const float* __restrict__ states, int C, int chunks,
+                        uint32_t total, uint32_t q_begin, uint32_t q_end,
+                        const float* __restrict__ states, int C, int chunks,
                         const float* __restrict__ volume, int tile_rows,
                         float* __restrict__ tiles) {
   const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= uint64_t(padded) * chunks) return;
-  const uint32_t q = static_cast<uint32_t>(t / chunks);
-  const int chunk = static_cast<int>(t - uint64_t(q) * chunks);
+  if (t >= uint64_t(q_end - q_begin) * chunks) return;
+  const uint32_t q = q_begin + static_cast<uint32_t>(t / chunks);
+  const int chunk = static_cast<int>(t - uint64_t(q - q_begin) * chunks);
   const int c0 = chunk * CH;
   const size_t F = p.feature_dims;
   float* tile = tiles + size_t(q / tile_rows) * F * tile_rows + (q % tile_rows);
@@ -199,18 +202,25 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
 npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& p,
                                    const SortedGrid& s, const HitLists& hl, uint32_t batch, const float* states,
                                    int state_dims, const float* volume_sorted, int tile_rows,
-                                   float* tiles, cudaStream_t stream) {
+                                   float* tiles, cudaStream_t stream, uint32_t tile_begin,
+                                   uint32_t tile_end) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
   const uint32_t padded = (total + tile_rows - 1) / tile_rows * tile_rows;
+  const uint32_t q_begin =
+      static_cast<uint32_t>(std::min<uint64_t>(padded, uint64_t(tile_begin) * tile_rows));
+  const uint32_t q_end =
+      static_cast<uint32_t>(std::min<uint64_t>(padded, uint64_t(tile_end) * tile_rows));
+  if (q_end <= q_begin) return NPA_OK;
   PerceptionParams pp = p;
   pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
-  const unsigned blocks = grid_for(uint64_t(padded) * chunks, 128);
+  const unsigned blocks = grid_for(uint64_t(q_end - q_begin) * chunks, 128);
 #define NPA_TILES(D, CHV)                                                                     \
   perception_tiles_kernel<D, CHV><<<blocks, 128, 0, stream>>>(                                \
-      g, pp, s, hl, total, padded, states, state_dims, chunks, volume_sorted, tile_rows, tiles)
+      g, pp, s, hl, total, q_begin, q_end, states, state_dims, chunks, volume_sorted,         \
+      tile_rows, tiles)
   if (g.dim == 2) {
     if (ch == 4) NPA_TILES(2, 4); else if (ch == 8) NPA_TILES(2, 8); else NPA_TILES(2, 16);
   } else {

@@ -9,12 +9,13 @@
 // the reference-order MLP stays at ~3.5e-4, so the MLP runs on the FP32
 // pipe as separate multiply and add (the library is built with --fmad=false).
 //
-// Work layout: 256 threads per block, HG x RG thread grid with HG = Hp / 8
-// hidden groups and RG = 256 / HG row groups; a tile holds M = 8 * RG rows.
-//   layer 1: each thread owns an 8 rows x 8 hidden-unit register tile and
+// Work layout: kThreads threads per block, HG x RG thread grid with
+// HG = Hp / kTH hidden groups and RG = kThreads / HG row groups; a tile holds
+// M = 8 * RG rows.
+//   layer 1: each thread owns an 8 rows x kTH hidden-unit register tile and
 //            walks k = 0..F-1 in order (features of the tile feature-major in
 //            shared memory, w1 transposed in shared memory);
-//   layer 2: 256 / M threads per row, each owning ceil(O / (256 / M))
+//   layer 2: kThreads / M threads per row, each owning ceil(O / (kThreads / M))
 //            outputs, sequential over h.
 // The rollout's MLP stage consumes the feature tiles written by
 // perception_tiles_kernel ([tile][F][M], sorted order), double-buffered with
@@ -29,7 +30,8 @@
 namespace npa {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;  // threads per block
+constexpr int kTH = 8;         // hidden units per thread in layer 1
 constexpr int kKC = 16;              // k slice when w1 is streamed
 constexpr int kMaxOut = 32;          // outputs per thread in layer 2
 constexpr size_t kSmemBudget = 220 * 1024;
@@ -99,39 +101,53 @@ __device__ __forceinline__ void load_weights(const MlpShape& s, const float* __r
 // 64 sums so no sum waits on the product issued just before it.  (The packed
 // mul.rn.f32x2 / add.rn.f32x2 pair was measured not to reproduce the scalar
 // results bit for bit, so the scalar form stays.)
-__device__ __forceinline__ void micro_tile(float (&acc)[8][8], float4 a0, float4 a1, float4 b0,
-                                           float4 b1) {
+__device__ __forceinline__ void micro_tile(float (&acc)[8][kTH], float4 a0, float4 a1,
+                                           const float4 (&bq)[kTH / 4]) {
   const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-  const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-  float p[8][8];
+  float bv[kTH];
+#pragma unroll
+  for (int j4 = 0; j4 < kTH / 4; ++j4) {
+    bv[4 * j4] = bq[j4].x;
+    bv[4 * j4 + 1] = bq[j4].y;
+    bv[4 * j4 + 2] = bq[j4].z;
+    bv[4 * j4 + 3] = bq[j4].w;
+  }
+  float p[8][kTH];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) p[i][j] = bv[j] * av[i];
+    for (int j = 0; j < kTH; ++j) p[i][j] = bv[j] * av[i];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = acc[i][j] + p[i][j];
+    for (int j = 0; j < kTH; ++j) acc[i][j] = acc[i][j] + p[i][j];
 }
 
 // Layer 1 for the tile in ft[F][M]: hid[r][h] = max(b1[h] + sum_k w1[h][k] f[r][k], 0).
+// The layer-1 biases of this thread's hidden units (constant over tiles).
+template <int HG>
+__device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __restrict__ b1,
+                                           float (&bias)[kTH]) {
+  const int h0 = (threadIdx.x % HG) * kTH;
+#pragma unroll
+  for (int j = 0; j < kTH; ++j) bias[j] = (h0 + j < s.H) ? __ldg(b1 + h0 + j) : 0.0f;
+}
+
 template <int HG>
 __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
-                                           const float* __restrict__ b1, const float* ft,
+                                           const float (&bias)[kTH], const float* ft,
                                            float* w1s, float* hid) {
   constexpr int RG = kThreads / HG;
   constexpr int M = RG * 8;
   const int t = threadIdx.x;
   const int rg = t / HG;
   const int hg = t - rg * HG;
-  const int h0 = hg * 8;
-  float acc[8][8];
+  const int h0 = hg * kTH;
+  float acc[8][kTH];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float bias = (h0 + j < s.H) ? __ldg(b1 + h0 + j) : 0.0f;
+  for (int j = 0; j < kTH; ++j)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i][j] = bias;
-  }
+    for (int i = 0; i < 8; ++i) acc[i][j] = bias[j];
   const float* arow = ft + rg * 8;
   if (s.w1_resident) {
     const float* wcol = w1s + h0;
@@ -139,9 +155,11 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
     for (int k = 0; k < s.F; ++k) {
       const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
       const float4 a1 = *reinterpret_cast<const float4*>(arow + k * M + 4);
-      const float4 b0 = *reinterpret_cast<const float4*>(wcol + k * s.Hp);
-      const float4 b1v = *reinterpret_cast<const float4*>(wcol + k * s.Hp + 4);
-      micro_tile(acc, a0, a1, b0, b1v);
+      float4 bq[kTH / 4];
+#pragma unroll
+      for (int j4 = 0; j4 < kTH / 4; ++j4)
+        bq[j4] = *reinterpret_cast<const float4*>(wcol + k * s.Hp + 4 * j4);
+      micro_tile(acc, a0, a1, bq);
     }
   } else {
     const int hp4 = s.Hp >> 2;
@@ -157,21 +175,22 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
         const int k = kc + kk;
         const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
         const float4 a1 = *reinterpret_cast<const float4*>(arow + k * M + 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(wcol + kk * s.Hp);
-        const float4 b1v = *reinterpret_cast<const float4*>(wcol + kk * s.Hp + 4);
-        micro_tile(acc, a0, a1, b0, b1v);
+        float4 bq[kTH / 4];
+#pragma unroll
+        for (int j4 = 0; j4 < kTH / 4; ++j4)
+          bq[j4] = *reinterpret_cast<const float4*>(wcol + kk * s.Hp + 4 * j4);
+        micro_tile(acc, a0, a1, bq);
       }
     }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float* row = hid + (rg * 8 + i) * s.hid_stride + h0;
-    *reinterpret_cast<float4*>(row) =
-        make_float4(fmaxf(acc[i][0], 0.0f), fmaxf(acc[i][1], 0.0f), fmaxf(acc[i][2], 0.0f),
-                    fmaxf(acc[i][3], 0.0f));
-    *reinterpret_cast<float4*>(row + 4) =
-        make_float4(fmaxf(acc[i][4], 0.0f), fmaxf(acc[i][5], 0.0f), fmaxf(acc[i][6], 0.0f),
-                    fmaxf(acc[i][7], 0.0f));
+#pragma unroll
+    for (int j4 = 0; j4 < kTH / 4; ++j4)
+      *reinterpret_cast<float4*>(row + 4 * j4) =
+          make_float4(fmaxf(acc[i][4 * j4], 0.0f), fmaxf(acc[i][4 * j4 + 1], 0.0f),
+                      fmaxf(acc[i][4 * j4 + 2], 0.0f), fmaxf(acc[i][4 * j4 + 3], 0.0f));
   }
 }
 
@@ -197,17 +216,21 @@ __device__ __forceinline__ void mlp_layer2(const MlpShape& s, const float* __res
   const int H4 = s.H & ~3;
   for (int h = 0; h < H4; h += 4) {
     const float4 hv = *reinterpret_cast<const float4*>(hrow + h);
+    float p[NOUT][4];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
       const float4 w = *reinterpret_cast<const float4*>(wrow[u] + h);
-      const float p0 = w.x * hv.x, p1 = w.y * hv.y, p2 = w.z * hv.z, p3 = w.w * hv.w;
-      float a = acc[u];
-      a = a + p0;
-      a = a + p1;
-      a = a + p2;
-      a = a + p3;
-      acc[u] = a;
+      p[u][0] = w.x * hv.x;
+      p[u][1] = w.y * hv.y;
+      p[u][2] = w.z * hv.z;
+      p[u][3] = w.w * hv.w;
     }
+    // each output still adds its four products in h order; the outputs'
+    // chains are interleaved so consecutive adds are independent
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int u = 0; u < NOUT; ++u) acc[u] = acc[u] + p[u][k];
   }
   for (int h = H4; h < s.H; ++h) {
     const float hv = hrow[h];
@@ -253,6 +276,8 @@ forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __
   float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
   load_weights(s, w1t, w2, w1s, w2s);
+  float bias1[kTH];
+  load_bias1<HG>(s, b1, bias1);
   const uint32_t tiles = (rows + s.M - 1) / s.M;
   for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     __syncthreads();
@@ -263,7 +288,7 @@ forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __
       ft[f * s.M + r] = row < rows ? __ldg(features + size_t(row) * s.F + f) : 0.0f;
     }
     __syncthreads();
-    mlp_layer1<HG>(s, w1t, b1, ft, w1s, hid);
+    mlp_layer1<HG>(s, w1t, bias1, ft, w1s, hid);
     __syncthreads();
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
@@ -326,8 +351,8 @@ struct StepParams {
 // The rollout step's MLP stage over feature tiles in sorted order.
 template <int HG>
 __global__ void __launch_bounds__(kThreads, 1)
-mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
-                const float* __restrict__ tiles_in, const float* __restrict__ w1t,
+mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_t tile_begin,
+                uint32_t tile_end, const float* __restrict__ tiles_in, const float* __restrict__ w1t,
                 const float* __restrict__ b1, const float* __restrict__ w2,
                 const float* __restrict__ b2, StepParams sp, EulerParams ep,
                 const float* __restrict__ mask, float4* __restrict__ next_pos,
@@ -342,16 +367,18 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
   float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
   const int C = sp.C, D = sp.D;
-  const uint32_t tiles = (total + s.M - 1) / s.M;
+  const uint32_t tiles = tile_end;
   const int chunks16 = s.F * s.M / 4;  // 16-byte chunks per feature tile
   auto issue = [&](uint32_t tile, float* dst) {
     const float* src = tiles_in + size_t(tile) * s.F * s.M;
     for (int e = threadIdx.x; e < chunks16; e += kThreads) cp_async16(dst + 4 * e, src + 4 * e);
   };
-  uint32_t tile = blockIdx.x;
+  uint32_t tile = tile_begin + blockIdx.x;
   if (tile < tiles) issue(tile, ftb[0]);
   cp_async_commit();
   load_weights(s, w1t, w2, w1s, w2s);
+  float bias1[kTH];
+  load_bias1<HG>(s, b1, bias1);
   int buf = 0;
   for (; tile < tiles; tile += gridDim.x, buf ^= 1) {
     const uint32_t next = tile + gridDim.x;
@@ -375,7 +402,7 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total,
       pi = __ldg(sg.positions + row);
       if (mask) m = __ldg(mask + row);
     }
-    mlp_layer1<HG>(s, w1t, b1, ft, w1s, hid);
+    mlp_layer1<HG>(s, w1t, bias1, ft, w1s, hid);
     __syncthreads();
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
@@ -421,7 +448,7 @@ MlpShape make_shape(const DeviceModel& m, bool double_buffer) {
   s.H = m.hidden_dims;
   s.Hp = m.hidden_padded;
   s.O = m.update_dims;
-  const int HG = s.Hp / 8;
+  const int HG = s.Hp / kTH;
   s.M = (kThreads / HG) * 8;
   s.tpr = kThreads / s.M;
   s.hid_stride = s.Hp + 4;
@@ -463,7 +490,7 @@ npa_status plan(K kernel, const MlpShape& s, bool double_buffer, uint64_t tiles,
 
 bool shape_ok(const DeviceModel& m) {
   if (m.hidden_padded != 64 && m.hidden_padded != 128 && m.hidden_padded != 256) return false;
-  const int M = (kThreads / (m.hidden_padded / 8)) * 8;
+  const int M = (kThreads / (m.hidden_padded / kTH)) * 8;
   const int tpr = kThreads / M;
   return (m.update_dims + tpr - 1) / tpr <= kMaxOut && m.feature_dims >= 1;
 }
@@ -472,7 +499,7 @@ bool shape_ok(const DeviceModel& m) {
 
 int hidden_padded_for(int hidden) { return hidden <= 64 ? 64 : (hidden <= 128 ? 128 : 256); }
 
-int step_tile_rows(const DeviceModel& m) { return (kThreads / (m.hidden_padded / 8)) * 8; }
+int step_tile_rows(const DeviceModel& m) { return (kThreads / (m.hidden_padded / kTH)) * 8; }
 
 bool mlp_step_supported(const DeviceModel& m) {
   return m.state_dims >= 0 && m.hidden_dims >= 1 && m.hidden_dims <= 256 && shape_ok(m);
@@ -493,9 +520,9 @@ npa_status launch_forward_update(const DeviceModel& m, const float* features, ui
                                                                        m.b2, features, rows,  \
                                                                        update);               \
   } while (0)
-  if (s.Hp == 64) NPA_FWD(8);
-  else if (s.Hp == 128) NPA_FWD(16);
-  else NPA_FWD(32);
+  if (s.Hp == 64) NPA_FWD(64 / kTH);
+  else if (s.Hp == 128) NPA_FWD(128 / kTH);
+  else NPA_FWD(256 / kTH);
 #undef NPA_FWD
   return after_launch("forward_update_kernel");
 }
@@ -514,7 +541,8 @@ npa_status launch_euler(const GridParams& g, const float4* positions, const floa
 
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
                            uint32_t batch, const float* tiles, float dt, const float* mask,
-                           const StepOutputs& out, cudaStream_t stream) {
+                           const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin,
+                           uint32_t tile_end) {
   const uint32_t total = batch * sgrid.n;
   if (total == 0) return NPA_OK;
   if (!mlp_step_supported(m))
@@ -527,18 +555,22 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
   sp.C = m.state_dims;
   sp.D = g.dim;
   EulerParams e{dt, g.dim == 3 ? 4 : 2, (g.dim == 3 && m.state_dims > 3) ? 1 : 0};
-  const uint64_t ntiles = (uint64_t(total) + s.M - 1) / s.M;
+  const uint32_t ntiles_all = static_cast<uint32_t>((uint64_t(total) + s.M - 1) / s.M);
+  tile_end = std::min(tile_end, ntiles_all);
+  if (tile_end <= tile_begin) return NPA_OK;
+  const uint64_t ntiles = tile_end - tile_begin;
   LaunchCfg lc;
 #define NPA_MLP(HGV)                                                                          \
   do {                                                                                        \
     NPA_TRY(plan(mlp_step_kernel<HGV>, s, true, ntiles, &lc));                                \
     mlp_step_kernel<HGV><<<lc.grid, kThreads, lc.smem, stream>>>(                             \
-        s, g, sgrid, total, tiles, m.w1t, m.b1, m.w2, m.b2, sp, e, mask, out.next_positions,  \
+        s, g, sgrid, total, tile_begin, tile_end, tiles, m.w1t, m.b1, m.w2, m.b2, sp, e, mask, \
+        out.next_positions,                                                                   \
         out.next_states, out.dx, out.ds, out.features);                                       \
   } while (0)
-  if (s.Hp == 64) NPA_MLP(8);
-  else if (s.Hp == 128) NPA_MLP(16);
-  else NPA_MLP(32);
+  if (s.Hp == 64) NPA_MLP(64 / kTH);
+  else if (s.Hp == 128) NPA_MLP(128 / kTH);
+  else NPA_MLP(256 / kTH);
 #undef NPA_MLP
   return after_launch("mlp_step_kernel");
 }
