@@ -1,27 +1,37 @@
 #!/usr/bin/env python3
-"""Benchmark of the NPA rollout step: particle-steps/s.
+"""Benchmark of the NPA rollout hot path: particle-steps/s.
 
-Workload (default "cfg2"): batched 2D rollouts, 4,096 particles each, the
-config-0 architecture (C=16, MLP 64->128->18, eps 0.05, grid 64x64 Particle
-hash), one shared seeded MLP.  Each GPU rank runs its own shard of 256
-rollouts (1,048,576 particles per step) with no collective on the step path
-("scaling": "weak"); --strong instead splits the 256 rollouts over the ranks.
+Workloads (--workload, default "cfg2"; seeded synthetic inputs from
+burn_automata_b200/workloads.py):
+  cfg0  one 2D rollout, 4,096 particles, C=16, MLP 64->128->18
+  cfg1  hashgrid build + perception alone, 1,048,576 2D particles, C=32, F=130
+  cfg2  256 independent cfg0-architecture rollouts of 4,096 particles per GPU
+  cfg3  one 3D torus rollout, 16,384 particles, C=32, MLP 160->256->35
+  cfg4  one clustered 2D rollout, 4,194,304 particles (64-component mixture)
+Each GPU rank runs its own shard with no collective on the step path
+("scaling": "weak"; --strong splits --rollouts over the ranks instead).
 
-A bench step is one rollout step (hashgrid -> density -> fused perception +
-MLP + Euler) over every particle of the shard.  The timed region is exactly K
-steps on resident device state, bracketed by barrier + synchronize, timed with
-CUDA events on the launching stream; the job time is the max over ranks.
+A bench step is one rollout step (hashgrid -> density -> perception ->
+MLP + Euler) over every particle of the shard; for cfg1 it is one hashgrid
+build + perception pass (features and density written).  The timed region is
+exactly K steps on resident device state, bracketed by barrier + synchronize,
+timed with CUDA events on the launching stream; the job time is the max over
+ranks.  The per-step working set exceeds the 126 MB L2 for cfg1, cfg2 and
+cfg4; cfg0 and cfg3 are small single rollouts that stay L2-resident (stated in
+the line's config).
 
 Extra keys:
-  roofline      dominant kernel (fused step) against measured HBM bandwidth,
-                from CUDA events around each of its launches in the timed region
-  compute_roof  the same kernel against the FP32 pipe (the MLP keeps the
-                reference's multiply-then-add order, so it runs as FP32 ops)
-  cpu_baseline  the CPU oracle (a port of the reference's CPU path) on a
-                bounded sample of the same workload, all host threads
-  e2e           the same metric through the public rollout API with host
-                buffers: H2D of the initial particles from pinned memory, K
-                steps, D2H of the final particles
+  roofline       dominant kernel (MLP step kernel; perception for cfg1)
+                 against measured HBM bandwidth, from CUDA events around each
+                 of its launches in the timed region
+  step_roofline  the whole step's algorithmic bytes against HBM bandwidth
+  compute_roof   the MLP step kernel against the FP32 pipe (the MLP keeps the
+                 reference's multiply-then-add order, so it runs as FP32 ops)
+  cpu_baseline   the CPU oracle (a port of the reference's CPU path) on a
+                 bounded sample of the same workload, all host threads
+  e2e            the same metric through the host-buffer call a drop-in user
+                 makes (step_cpu / perceive_with_options): per step, H2D of
+                 that step's inputs from pinned memory and D2H of its outputs
 --impl reference times the CPU port alone (the reference's own Rust/rayon
 path cannot be built here: no cargo / rustc).
 """
@@ -35,7 +45,6 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
 from pathlib import Path
 
 import numpy as np
@@ -43,16 +52,22 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-BATCH_TOTAL = 256
-PARTICLES = 4096
-# Algorithmic HBM bytes of the MLP step kernel per particle (C = 16, F = 64):
-# feature row read (4F = 256), position read + write (32), next state write
-# (4C = 64), permutation read (4).
-FUSED_BYTES_PER_PARTICLE = 356
-# Whole rollout step per particle-step (hashgrid keys / permutation and the
-# density round trip added): 184 + bin offsets (4 * 4097 / 4096).
-STEP_BYTES_PER_PARTICLE = 188
 METRIC = "particle-steps/s per rollout step at 1/2/4/8 B200; % of HBM roofline"
+DATA = "synthetic (seeded; see burn_automata_b200/workloads.py)"
+
+# rollouts per rank, kind of step, default timed steps
+WORKLOADS = {
+    "cfg0": {"rollouts": 1, "kind": "step", "steps": 200},
+    "cfg1": {"rollouts": 1, "kind": "perception", "steps": 50},
+    "cfg2": {"rollouts": 256, "kind": "step", "steps": 200},
+    "cfg3": {"rollouts": 1, "kind": "step", "steps": 100},
+    "cfg4": {"rollouts": 1, "kind": "step", "steps": 5},
+}
+
+# DRAM bytes (read + write) of one launch of the dominant kernel, from the
+# committed ncu captures, per particle of that launch:
+#   profiles/mlp_step_kernel_cfg2.txt: 289.7 MB + 65.7 MB for 1,048,576 rows.
+NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (289.698816e6 + 65.66272e6) / 1048576}
 
 
 def env_int(name, default):
@@ -70,6 +85,39 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
+def grid_cells(grid) -> int:
+    gs = list(grid.grid_size) + [1, 1, 1]
+    return int(np.prod(gs[:grid.dim]))
+
+
+def mlp_kernel_bytes(model) -> int:
+    """Algorithmic HBM bytes per particle of the MLP step kernel: feature row
+    read (4F), position read + write (32), next state write (4C), permutation
+    read (4)."""
+    return 4 * model.perception_dims() + 32 + 4 * model.state_dims + 4
+
+
+def step_bytes(w) -> float:
+    """Whole rollout step per particle-step: position read + write (32),
+    state read + write (8C), density write + read (8), hashgrid key /
+    permutation write + read (16), bin offsets 4 (B cells + 1) / (B N)."""
+    offsets = 4.0 * (grid_cells(w.grid) * w.batch + 1) / (w.batch * w.n)
+    return 32 + 8 * w.state_dims + 8 + 16 + offsets
+
+
+def perception_kernel_bytes(w, features) -> int:
+    """cfg1 perception kernel per particle: own position (16) and state (4C)
+    read, volume read (4), feature row write (4F)."""
+    return 16 + 4 * w.state_dims + 4 + 4 * features
+
+
+def perception_step_bytes(w, features) -> float:
+    """cfg1 pass per particle: position read (16), state read (4C), density
+    write + read (8), hashgrid (16), feature write (4F), offsets."""
+    offsets = 4.0 * (grid_cells(w.grid) * w.batch + 1) / (w.batch * w.n)
+    return 16 + 4 * w.state_dims + 8 + 16 + 4 * features + offsets
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
@@ -80,7 +128,6 @@ class ClockSampler:
     def __init__(self):
         self.proc = None
         self.path = None
-        self.t0 = self.t1 = None
 
     def start(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -91,12 +138,6 @@ class ClockSampler:
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-
-    def mark(self, which):
-        if which == "begin":
-            self.t0 = time.time()
-        else:
-            self.t1 = time.time()
 
     def stop(self, gpu_indices):
         if self.proc is None:
@@ -142,73 +183,133 @@ def visible_gpu_indices(world):
     return list(range(max(world, 1)))
 
 
-def cpu_baseline(workload_name, target_seconds=12.0):
-    """Times the CPU oracle (port of the reference CPU path) on a bounded sample."""
+# ---- CPU samples (the oracle: a port of the reference CPU path) ----
+
+class CpuSample:
+    """A bounded, per-particle-representative piece of a workload for the CPU
+    port: whole rollouts of a batched config, one mixture component of cfg4
+    (its particle density), a density-preserving sub-square of cfg1, or the
+    single rollout of cfg0 / cfg3."""
+
+    def __init__(self, name, size, seed=0):
+        from burn_automata_b200 import workloads
+
+        self.name = name
+        if name == "cfg4":
+            self.w = workloads.make("cfg4", seed, n=65536, components=1)
+            self.desc = "one 65,536-particle component of the cfg4 mixture (sigma 0.02)"
+        elif name == "cfg1":
+            full = 1 << 20
+            n = int(max(4096, min(full, size)))
+            half = float(np.sqrt(n / full))
+            self.w = workloads.make("cfg1", seed, n=n)
+            self.w.positions[:, :2] = workloads.uniform_positions_2d(n, seed, -half, half)[:, :2]
+            self.desc = (f"{n:,} cfg1 particles uniform in [-{half:.3f},{half:.3f}]^2 "
+                         "(cfg1's particle density)")
+        elif name == "cfg2":
+            b = int(max(1, min(256, size)))
+            self.w = workloads.make("cfg2", seed, batch=b)
+            self.desc = f"{b} of the 256 cfg2 rollouts"
+        else:
+            self.w = workloads.make(name, seed)
+            self.desc = f"the {name} rollout"
+        self.particles = self.w.batch * self.w.n
+
+    def run(self, pos=None, st=None):
+        """One step of the sample; returns (positions, states) after it."""
+        import oracle
+
+        w = self.w
+        pos = w.positions if pos is None else pos
+        st = w.states if st is None else st
+        if w.model is None:
+            oracle.perceive_with_options(pos, st, w.batch, w.n, w.state_dims, w.grid, w.options)
+            return pos, st
+        p, s, _ = oracle.rollout(w.model, w.weights, w.grid, pos, st, w.batch, w.n, 1, w.dt)
+        return p, s
+
+
+def calibrated_sample(name, seconds_per_step):
+    """The CpuSample whose one step takes about `seconds_per_step` here."""
+    probe_size = {"cfg1": 1 << 16, "cfg2": 2}.get(name, 1)
+    s = CpuSample(name, probe_size)
+    t = time.perf_counter()
+    s.run()
+    per_particle = (time.perf_counter() - t) / s.particles
+    if name == "cfg1":
+        return CpuSample(name, seconds_per_step / max(per_particle, 1e-12))
+    if name == "cfg2":
+        return CpuSample(name, seconds_per_step / max(per_particle * s.w.n, 1e-12))
+    return s
+
+
+def cpu_baseline(name, target_seconds=12.0):
+    """The CPU port timed on a bounded sample (about target_seconds)."""
     import oracle
-    from burn_automata_b200 import workloads
 
     oracle.build()
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    w = workloads.make(workload_name, batch=4, steps=1)
+    s = calibrated_sample(name, target_seconds / 4)
     t = time.perf_counter()
-    oracle.rollout(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, 1, w.dt)
-    per_ps = (time.perf_counter() - t) / (w.batch * w.n)
-    rollouts = int(min(64, max(4, target_seconds / 4 / (per_ps * w.n))))
-    steps = int(min(16, max(1, target_seconds / (per_ps * w.n * rollouts))))
-    w = workloads.make(workload_name, batch=rollouts, steps=steps)
+    pos, st = s.run()
+    one = time.perf_counter() - t
+    if one >= target_seconds / 2:  # one step is already a long enough sample
+        return {"value": s.particles / one, "unit": "particle-steps/s", "cores": threads,
+                "kind": "port", "sample": f"1 step of {s.desc}"}
+    steps = int(min(16, max(1, target_seconds / max(one, 1e-6))))
     t = time.perf_counter()
-    oracle.rollout(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, steps, w.dt)
+    for _ in range(steps):
+        pos, st = s.run(pos, st)
     dt = time.perf_counter() - t
-    return {"value": w.batch * w.n * steps / dt, "unit": "particle-steps/s", "cores": threads,
-            "kind": "port",
-            "sample": f"{rollouts} rollouts x {w.n} particles x {steps} steps of {workload_name}"}
+    return {"value": s.particles * steps / dt, "unit": "particle-steps/s", "cores": threads,
+            "kind": "port", "sample": f"{steps} step(s) of {s.desc}"}
 
 
 def run_reference(args, rank, world):
+    """CPU port of the reference path on the host cores (rank 0 only)."""
     if rank != 0:
         return
     import oracle
-    from burn_automata_b200 import workloads
 
     oracle.build()
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    per_rank = BATCH_TOTAL // world if args.strong else BATCH_TOTAL
-    # Calibrate a per-step sample of rollouts that takes ~1 s on the host.
-    probe = workloads.make(args.workload, batch=4, steps=1)
-    t = time.perf_counter()
-    oracle.rollout(probe.model, probe.weights, probe.grid, probe.positions, probe.states,
-                   probe.batch, probe.n, 1, probe.dt)
-    per_rollout = (time.perf_counter() - t) / probe.batch
-    sample = int(min(per_rank, max(1, 1.0 / max(per_rollout, 1e-6))))
-    w = workloads.make(args.workload, batch=sample, steps=1)
-    pos, st = w.positions.copy(), w.states.copy()
+    budget = min(1.0, 150.0 / max(args.steps + args.warmup, 1))
+    s = calibrated_sample(args.workload, budget)
+    pos = st = None
     for _ in range(args.warmup):
-        pos, st, _ = oracle.rollout(w.model, w.weights, w.grid, pos, st, w.batch, w.n, 1, w.dt)
+        pos, st = s.run(pos, st)
     times = []
     for _ in range(args.steps):
         t = time.perf_counter()
-        pos, st, _ = oracle.rollout(w.model, w.weights, w.grid, pos, st, w.batch, w.n, 1, w.dt)
+        pos, st = s.run(pos, st)
         times.append(time.perf_counter() - t)
     total = float(np.sum(times))
-    value = sample * w.n * args.steps / total
+    value = s.particles * args.steps / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "particle-steps/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
         "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; see burn_automata_b200/workloads.py)",
-        "config": {"workload": args.workload, "rollouts_per_step_sample": sample,
-                   "particles_per_rollout": w.n, "note": "CPU port of the reference path "
-                   "(oracle/npa_oracle.c); the Rust reference cannot be built without cargo"},
+        "data": DATA,
+        "config": {"workload": args.workload, "sample": s.desc,
+                   "note": "CPU port of the reference path (oracle/npa_oracle.c); the Rust "
+                           "reference cannot be built without cargo"},
         "cpu_baseline": {"value": value, "unit": "particle-steps/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"{sample} rollouts x {w.n} particles per step"},
+                         "kind": "port", "sample": f"per step: {s.desc}"},
         "e2e": {"value": value, "unit": "particle-steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ---- GPU arm ----
+
+def pinned(shape):
+    import torch
+
+    return torch.empty(shape, dtype=torch.float32).pin_memory().numpy()
 
 
 def run_ours(args, rank, world, local_rank):
@@ -222,16 +323,29 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     multigpu.init("nccl", multigpu.RankInfo(rank, world, local_rank), timeout_s=180, device=dev)
     lib = ba.load_library()
-    total_rollouts = args.rollouts or BATCH_TOTAL
+    spec = WORKLOADS[args.workload]
+    total_rollouts = args.rollouts or spec["rollouts"]
     first, per_rank = multigpu.shard(total_rollouts, world, rank, args.strong)
     w = workloads.make(args.workload, batch=per_rank, first=first)
-    model = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
-                                               w.weights.b2), device=local_rank)
-    ex = ba.CudaAutomataExecutor(model, w.grid, w.batch, w.n)
-    ex.create_state(w.positions, w.states)
-    stream = torch.cuda.Stream()
+    particles_rank = w.batch * w.n
+    stream = torch.cuda.Stream(dev)
     sptr = stream.cuda_stream
-    ex.step_state_many(args.warmup, w.dt, use_graph=True, stream=sptr)
+    perception_only = spec["kind"] == "perception"
+
+    if perception_only:
+        runner = ba.DevicePerception(w.grid, w.options, w.batch, w.n, w.state_dims, local_rank)
+        d_pos = torch.from_numpy(w.positions).to(dev)
+        d_st = torch.from_numpy(w.states).to(dev)
+        for _ in range(args.warmup):
+            runner(d_pos, d_st, stream=sptr)
+        features = runner.feature_dims
+    else:
+        model = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
+                                                   w.weights.b2), device=local_rank)
+        ex = ba.CudaAutomataExecutor(model, w.grid, w.batch, w.n)
+        ex.create_state(w.positions, w.states)
+        ex.step_state_many(args.warmup, w.dt, use_graph=True, stream=sptr)
+        features = w.model.perception_dims()
     torch.cuda.synchronize()
 
     sampler = ClockSampler() if rank == 0 else None
@@ -242,20 +356,20 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     launches0 = lib.npa_kernel_launch_count()
-    if sampler:
-        sampler.mark("begin")
-    phase_ms, total_ms = ex.step_state_many_profiled(args.steps, w.dt, use_graph=True,
-                                                     stream=sptr)
-    if sampler:
-        sampler.mark("end")
+    if perception_only:
+        phase_ms, total_ms = runner.run_profiled(d_pos, d_st, args.steps, stream=sptr)
+        dominant = phase_ms[:, 2]
+    else:
+        phase_ms, total_ms = ex.step_state_many_profiled(args.steps, w.dt, use_graph=True,
+                                                         stream=sptr)
+        dominant = phase_ms[:, 3]
     torch.cuda.synchronize()
     launches = lib.npa_kernel_launch_count() - launches0
     if world > 1:
         dist.barrier()
-    max_ms, fused_ms = multigpu.max_over_ranks([total_ms, float(phase_ms[:, 3].mean())], dev)
+    max_ms, dom_ms = multigpu.max_over_ranks([total_ms, float(dominant.mean())], dev)
     clocks = sampler.stop(visible_gpu_indices(world)) if sampler else None
 
-    particles_rank = w.batch * w.n
     # all ranks' particles (strong scaling may give ranks unequal shares)
     cnt = torch.tensor([float(particles_rank)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -263,86 +377,113 @@ def run_ours(args, rank, world, local_rank):
     particles_job = int(cnt.item())
     value = particles_job * args.steps / (max_ms / 1000.0)
 
-    # e2e through the public rollout API with host buffers (rank-local, then max).
+    # e2e through the host-buffer call of a drop-in user, one call per step
     e2e = None
     if not args.no_e2e:
-        pin_pos = torch.from_numpy(w.positions).pin_memory()
-        pin_st = torch.from_numpy(w.states).pin_memory()
-        out_pos = torch.empty_like(pin_pos).pin_memory()
-        out_st = torch.empty_like(pin_st).pin_memory()
+        if perception_only:
+            inp = (pinned((particles_rank, 4)), pinned(particles_rank * w.state_dims))
+            inp[0][:] = w.positions
+            inp[1][:] = w.states
+            out = (pinned(particles_rank * features), pinned(particles_rank))
+
+            def one(k):
+                ba.perceive_with_options(inp[0], inp[1], w.batch, w.n, w.state_dims, w.grid,
+                                         w.options, outputs=(), out=out)
+            h2d = inp[0].nbytes + inp[1].nbytes
+            d2h = out[0].nbytes + out[1].nbytes
+            api = ("perceive_with_options (C ABI npa_perceive_with_options) with pinned host "
+                   "buffers, features + density copied back, one call per step")
+        else:
+            bufs = [(pinned((particles_rank, 4)), pinned(particles_rank * w.state_dims))
+                    for _ in range(2)]
+            bufs[0][0][:] = w.positions
+            bufs[0][1][:] = w.states
+
+            def one(k):
+                src, dst = bufs[k % 2], bufs[(k + 1) % 2]
+                model.step(src[0], src[1], w.batch, w.n, w.grid, w.dt, outputs=(), out=dst)
+            h2d = d2h = bufs[0][0].nbytes + bufs[0][1].nbytes
+            api = ("NpaModel.step (C ABI npa_model_step, the step_cpu drop-in) with pinned "
+                   "host buffers, next positions + states copied back, one call per step")
+        for k in range(args.warmup):
+            one(k)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        ex.create_state(pin_pos.numpy(), pin_st.numpy())
-        ex.step_state_many(args.steps, w.dt, use_graph=True, stream=sptr)
-        p_, s_ = ex.read_state()
-        out_pos.numpy()[:] = p_
-        out_st.numpy()[:] = s_
-        e2e_s = time.perf_counter() - t0
-        e2e_s = multigpu.max_over_ranks([e2e_s], dev)[0]
-        h2d = w.positions.nbytes + w.states.nbytes
+        for k in range(args.steps):
+            one(k)
+        e2e_s = multigpu.max_over_ranks([time.perf_counter() - t0], dev)[0]
         e2e = {"value": particles_job * args.steps / e2e_s, "unit": "particle-steps/s",
-               "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": h2d / args.steps,
-               "api": "CudaAutomataExecutor create_state + step_state_many + read_state",
-               "note": "one upload of the initial particles and one readback of the final "
-                       "particles per K-step rollout (per-step bytes are amortised)"}
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
 
     # one gather of per-shard checksums of the final states (validation only)
-    fp, fs = ex.read_state()
+    if perception_only:
+        fp, fs = runner.features.cpu().numpy(), runner.density.cpu().numpy()
+    else:
+        fp, fs = ex.read_state()
     checksums = multigpu.gather_checksums(multigpu.shard_checksum(fp, fs), dev)
 
     if rank == 0:
         peak, peak_kind = load_peaks()
-        fused_achieved = FUSED_BYTES_PER_PARTICLE * particles_rank / (fused_ms / 1000.0) / 1e9
-        sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-        mlp_ops = 2 * (w.model.perception_dims() * w.model.hidden_dims
-                       + w.model.hidden_dims * w.model.update_dims())
-        fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12
-        fp32_achieved = mlp_ops * particles_rank / (fused_ms / 1000.0) / 1e12
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(args.workload)
+        if perception_only:
+            kernel, kbytes = "perception_kernel", perception_kernel_bytes(w, features)
+            sbytes = perception_step_bytes(w, features)
+            names = ["hashgrid", "density", "perception"]
+        else:
+            kernel, kbytes = "mlp_step_kernel", mlp_kernel_bytes(w.model)
+            sbytes = step_bytes(w)
+            names = ["hashgrid", "density", "perception", "mlp_step"]
+        achieved = kbytes * particles_rank / (dom_ms / 1000.0) / 1e9
+        tr = NCU_TRAFFIC_PER_PARTICLE.get((args.workload, kernel))
         line = {
             "metric": METRIC, "value": value, "unit": "particle-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": max_ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded; see burn_automata_b200/workloads.py)",
+            "dtype": "f32", "data": DATA,
             "config": {"workload": args.workload, "rollouts_per_gpu": per_rank,
                        "particles_per_rollout": w.n, "particles_per_gpu": particles_rank,
-                       "state_dims": w.model.state_dims, "mlp": [w.model.perception_dims(),
-                                                                 w.model.hidden_dims,
-                                                                 w.model.update_dims()],
-                       "eps": w.grid.eps, "grid": list(w.grid.grid_size[:2]),
+                       "state_dims": w.state_dims, "features": features,
+                       "eps": w.grid.eps, "grid": list(w.grid.grid_size[:w.grid.dim]),
                        "parallelism": f"{world} independent shards (no step-path collective)",
-                       "l2": "no flush: per-step working set (~220 MB) exceeds the 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": "mlp_step_kernel",
-                         "achieved": fused_achieved, "peak": peak, "unit": "GB/s",
-                         "frac": fused_achieved / peak, "peak_source": peak_kind,
-                         "traffic": None,
-                         "bytes_per_particle": FUSED_BYTES_PER_PARTICLE,
-                         "avg_launch_ms": fused_ms},
-            "step_roofline": {"bound": "hbm", "achieved":
-                              STEP_BYTES_PER_PARTICLE * value / world / 1e9, "peak": peak,
-                              "unit": "GB/s",
-                              "frac": STEP_BYTES_PER_PARTICLE * value / world / 1e9 / peak},
-            "compute_roof": {"bound": "fp32", "achieved": fp32_achieved, "peak": fp32_peak,
-                             "unit": "TFLOP/s (FP32 mul + add, reference order)",
-                             "frac": fp32_achieved / fp32_peak},
-            "phase_ms": {"hashgrid": float(phase_ms[:, 0].mean()),
-                         "density": float(phase_ms[:, 1].mean()),
-                         "perception": float(phase_ms[:, 2].mean()),
-                         "mlp_step": float(phase_ms[:, 3].mean())},
+                       "l2": ("no flush: per-step working set exceeds the 126 MB L2"
+                              if particles_rank >= (1 << 20) else
+                              "no flush: small single rollout, L2-resident by nature")},
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                         "traffic": tr * particles_rank if tr else None,
+                         "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                            "profiles/mlp_step_kernel_cfg2.txt") if tr else None,
+                         "bytes_per_particle": kbytes, "avg_launch_ms": dom_ms},
+            "step_roofline": {"bound": "hbm", "achieved": sbytes * value / world / 1e9,
+                              "peak": peak, "unit": "GB/s",
+                              "frac": sbytes * value / world / 1e9 / peak,
+                              "bytes_per_particle": sbytes},
+            "phase_ms": {k: float(phase_ms[:, i].mean()) for i, k in enumerate(names)},
             "gpu_launches": int(launches),
             "clocks": clocks,
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "final_state_checksums": checksums,
         }
+        if not perception_only:
+            sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+            mlp_ops = 2 * (features * w.model.hidden_dims
+                           + w.model.hidden_dims * w.model.update_dims())
+            fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12
+            fp32_achieved = mlp_ops * particles_rank / (dom_ms / 1000.0) / 1e12
+            line["compute_roof"] = {"bound": "fp32", "kernel": kernel, "achieved": fp32_achieved,
+                                    "peak": fp32_peak, "frac": fp32_achieved / fp32_peak,
+                                    "unit": "TFLOP/s (FP32 mul + add, reference order; peak = "
+                                            "148 SM x 128 lanes x median SM clock)"}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(args.workload)
+        line["cpu_baseline"] = cpu
+        line["e2e"] = e2e
+        line["final_state_checksums"] = checksums
         print(json.dumps(line), flush=True)
-    ex.close()
-    model.close()
+    if not perception_only:
+        ex.close()
+        model.close()
     if world > 1:
         dist.barrier()
     multigpu.finish()
@@ -351,19 +492,24 @@ def run_ours(args, rank, world, local_rank):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default per workload: cfg0/cfg2 200, cfg1 50, cfg3 100, "
+                         "cfg4 5)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2"])
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
     ap.add_argument("--strong", action="store_true",
-                    help="split the 256 rollouts over the ranks instead of 256 per rank")
+                    help="split --rollouts over the ranks instead of running them on every rank")
     ap.add_argument("--rollouts", type=int, default=None,
-                    help="rollouts per rank (default: 256, or 256 / ranks with --strong)")
+                    help="rollouts per rank (default: 256 for cfg2, 1 otherwise), or in total "
+                         "with --strong")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.steps is None:
+        args.steps = WORKLOADS[args.workload]["steps"]
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
     local_rank = env_int("LOCAL_RANK", 0)

@@ -8,7 +8,7 @@ this package is the Python mirror of the reference's operator surface
 from .config import (Boundary, EquivarianceMode, GaussianDecodeConfig, GaussianDecodeMode,
                      HashGridConfig, HashGridMode, KernelError, NpaConfig, PerceptionOptions,
                      feature_dims)
-from .kernels import (Gaussian3d, HashGridSnapshot, PerceptionOutput, build_hashgrid,
+from .kernels import (DevicePerception, Gaussian3d, HashGridSnapshot, PerceptionOutput, build_hashgrid,
                       decode_gaussians_3d, decode_gaussians_3d_records, euler_step, perceive,
                       perceive_with_options)
 from .model import (CudaAutomataExecutor, NpaModel, NpaWeights, RolloutConfig, RolloutTrace,

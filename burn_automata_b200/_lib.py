@@ -94,6 +94,9 @@ SIGNATURES = [
     ("npa_dev_perceive_with_options", c_i32,
      [P(GridConfigC), P(PerceptionOptionsC), vp, vp, c_i64, c_i64, c_i64, vp, vp, vp, vp, vp, vp,
       ctypes.c_size_t, vp]),
+    ("npa_dev_perceive_many_profiled", c_i32,
+     [P(GridConfigC), P(PerceptionOptionsC), vp, vp, c_i64, c_i64, c_i64, vp, vp, vp,
+      ctypes.c_size_t, c_i64, vp, f32p, f32p]),
     ("npa_dev_model_forward_update", c_i32, [vp, vp, c_i64, vp, vp]),
     ("npa_dev_euler_step", c_i32,
      [P(GridConfigC), vp, vp, vp, vp, c_i64, c_i64, c_i64, c_f32, vp, vp, vp, vp]),

@@ -12,6 +12,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -193,29 +194,103 @@ npa_status current_device(int* device) {
 // exhausting a device.
 std::atomic<uint64_t> g_alloc_cap{0};
 
-// Device scratch of one host-buffer call, freed on scope exit.
+// Device blocks released by host-buffer calls, kept per device (up to
+// kCacheBytes) and handed to later calls of a similar size, so a loop of
+// host-buffer calls does not pay cudaMalloc / cudaFree every time.
+struct BlockCache {
+  std::mutex mu;
+  std::multimap<size_t, std::pair<int, void*>> blocks;  // size -> (device, pointer)
+  size_t bytes = 0;
+};
+constexpr size_t kCacheBytes = size_t(8) << 30;
+
+BlockCache& block_cache() {
+  static BlockCache* c = new BlockCache();  // never destroyed: no frees after the driver unloads
+  return *c;
+}
+
+// A cached block of at least `bytes` (and at most twice that) on `dev`.
+void* cache_take(int dev, size_t bytes, size_t* got) {
+  BlockCache& c = block_cache();
+  std::lock_guard<std::mutex> lock(c.mu);
+  for (auto it = c.blocks.lower_bound(bytes); it != c.blocks.end() && it->first <= 2 * bytes; ++it) {
+    if (it->second.first != dev) continue;
+    void* p = it->second.second;
+    *got = it->first;
+    c.bytes -= it->first;
+    c.blocks.erase(it);
+    return p;
+  }
+  return nullptr;
+}
+
+// Frees every cached block of `dev` (before retrying an allocation that failed).
+void cache_release(int dev) {
+  BlockCache& c = block_cache();
+  std::lock_guard<std::mutex> lock(c.mu);
+  for (auto it = c.blocks.begin(); it != c.blocks.end();) {
+    if (it->second.first == dev) {
+      cudaFree(it->second.second);
+      c.bytes -= it->first;
+      it = c.blocks.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
+// cudaMalloc that drops the cached blocks of the device and retries once
+// when the device is out of memory.
+cudaError_t malloc_or_release(void** p, size_t bytes, int dev) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    cache_release(dev);
+    e = cudaMalloc(p, bytes);
+  }
+  return e;
+}
+
+void cache_give(int dev, void* p, size_t bytes) {
+  BlockCache& c = block_cache();
+  {
+    std::lock_guard<std::mutex> lock(c.mu);
+    if (c.bytes + bytes <= kCacheBytes) {
+      c.blocks.emplace(bytes, std::make_pair(dev, p));
+      c.bytes += bytes;
+      return;
+    }
+  }
+  cudaFree(p);
+}
+
+// Device scratch of one host-buffer call, returned to the block cache on
+// scope exit (after the call's stream has drained).
 struct Scratch {
-  std::vector<void*> ptrs;
+  std::vector<std::pair<void*, size_t>> ptrs;
   uint64_t bytes = 0;
+  int device = 0;
   cudaStream_t stream = nullptr;
   ~Scratch() {
     if (stream) cudaStreamSynchronize(stream);
-    for (void* p : ptrs) cudaFree(p);
+    for (auto& b : ptrs) cache_give(device, b.first, b.second);
     if (stream) cudaStreamDestroy(stream);
   }
   npa_status init() {
+    NPA_CUDA(cudaGetDevice(&device), "cudaGetDevice");
     NPA_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
     return NPA_OK;
   }
   template <class T>
   npa_status alloc(T** out, size_t count) {
     *out = nullptr;
-    const size_t b = std::max<size_t>(count * sizeof(T), 256);
+    const size_t b = (std::max<size_t>(count * sizeof(T), 256) + 255) & ~size_t(255);
     const uint64_t cap = g_alloc_cap.load();
     if (cap && bytes + b > cap) return fail(NPA_ERR_OUT_OF_MEMORY, "allocation cap reached");
-    void* p = nullptr;
-    NPA_CUDA(cudaMalloc(&p, b), "cudaMalloc");
-    ptrs.push_back(p);
+    size_t got = b;
+    void* p = cache_take(device, b, &got);
+    if (!p) NPA_CUDA(malloc_or_release(&p, b, device), "cudaMalloc");
+    ptrs.emplace_back(p, got);
     bytes += b;
     *out = static_cast<T*>(p);
     return NPA_OK;
@@ -338,10 +413,20 @@ int64_t record_floats(const npa_gaussian_decode_config* cfg) {
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
+// Device buffers and the stream behind a model's host-buffer step calls:
+// kept between calls (grown on demand, freed with the model), so a loop of
+// host-buffer steps pays for its copies and kernels, not for allocations.
+struct HostArena {
+  void* base = nullptr;
+  size_t cap = 0;
+  cudaStream_t stream = nullptr;
+};
+
 struct npa_model {
   DeviceModel dm{};
   npa_model_config cfg{};
   std::mutex mu;
+  HostArena arena;
 };
 
 namespace {
@@ -675,6 +760,9 @@ void npa_model_destroy(npa_model* m) {
   cudaFree(m->dm.b1);
   cudaFree(m->dm.w2);
   cudaFree(m->dm.b2);
+  if (m->arena.stream) cudaStreamSynchronize(m->arena.stream);
+  cudaFree(m->arena.base);
+  if (m->arena.stream) cudaStreamDestroy(m->arena.stream);
   cudaSetDevice(prev);
   delete m;
 }
@@ -702,6 +790,25 @@ npa_status npa_model_forward_update_from_features(npa_model* m, const float* fea
   return s.finish();
 }
 
+// Reserves `bytes` of the model's host-call arena (caller holds m->mu).
+npa_status arena_reserve(npa_model* m, size_t bytes) {
+  HostArena& a = m->arena;
+  if (!a.stream)
+    NPA_CUDA(cudaStreamCreateWithFlags(&a.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (bytes <= a.cap) return NPA_OK;
+  const uint64_t cap = g_alloc_cap.load();
+  if (cap && bytes > cap) return fail(NPA_ERR_OUT_OF_MEMORY, "allocation cap reached");
+  NPA_CUDA(cudaStreamSynchronize(a.stream), "cudaStreamSynchronize");
+  cudaFree(a.base);
+  a.base = nullptr;
+  a.cap = 0;
+  int dev = 0;
+  NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  NPA_CUDA(malloc_or_release(&a.base, bytes, dev), "cudaMalloc");
+  a.cap = bytes;
+  return NPA_OK;
+}
+
 npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float* positions,
                           int64_t positions_len, const float* states, int64_t states_len,
                           int64_t batch, int64_t n, float dt, const float* update_mask,
@@ -717,36 +824,54 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
   if (total > 0 && (!positions || (C > 0 && (!states || !next_states)) || !next_positions))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
   NPA_TRY(ensure_device(m->dm.device));
-  const GridParams g = make_grid_params(*grid);
-  Scratch s;
-  NPA_TRY(s.init());
-  float4* dpos;
-  float *dst, *dmask = nullptr;
-  NPA_TRY(s.upload(&dpos, positions, total));
-  NPA_TRY(s.upload(&dst, states, size_t(total) * C));
-  if (update_mask) NPA_TRY(s.upload(&dmask, update_mask, total));
-  float4 *dnp, *ddx = nullptr;
-  float *dns, *dds = nullptr, *dfeat = nullptr, *ddens = nullptr;
-  NPA_TRY(s.alloc(&dnp, total));
-  NPA_TRY(s.alloc(&dns, size_t(total) * C));
-  if (dx) NPA_TRY(s.alloc(&ddx, total));
-  if (ds) NPA_TRY(s.alloc(&dds, size_t(total) * C));
-  if (features) NPA_TRY(s.alloc(&dfeat, size_t(total) * m->dm.feature_dims));
-  if (density) NPA_TRY(s.alloc(&ddens, total));
   size_t wsb = 0;
   NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
-  char* ws;
-  NPA_TRY(s.alloc(&ws, wsb));
-  NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(dpos), dst, batch, n, dt, dmask,
-                             reinterpret_cast<float*>(dnp), dns, reinterpret_cast<float*>(ddx),
-                             dds, dfeat, ddens, ws, wsb, s.stream));
-  NPA_TRY(s.download(next_positions, dnp, size_t(total) * 16));
-  NPA_TRY(s.download(next_states, dns, size_t(total) * C * 4));
-  if (dx) NPA_TRY(s.download(dx, ddx, size_t(total) * 16));
-  if (ds) NPA_TRY(s.download(ds, dds, size_t(total) * C * 4));
-  if (features) NPA_TRY(s.download(features, dfeat, size_t(total) * m->dm.feature_dims * 4));
-  if (density) NPA_TRY(s.download(density, ddens, size_t(total) * 4));
-  return s.finish();
+  std::lock_guard<std::mutex> lock(m->mu);
+  struct Bufs {
+    float4 *pos, *np, *dx;
+    float *st, *mask, *ns, *ds, *feat, *dens;
+    char* ws;
+  } b{};
+  const size_t F = size_t(m->dm.feature_dims);
+  auto layout = [&](void* base) {
+    Carve c(base, ~size_t(0));
+    b.pos = c.take<float4>(total);
+    b.st = c.take<float>(size_t(total) * C);
+    b.mask = update_mask ? c.take<float>(total) : nullptr;
+    b.np = c.take<float4>(total);
+    b.ns = c.take<float>(size_t(total) * C);
+    b.dx = dx ? c.take<float4>(total) : nullptr;
+    b.ds = ds ? c.take<float>(size_t(total) * C) : nullptr;
+    b.feat = features ? c.take<float>(size_t(total) * F) : nullptr;
+    b.dens = density ? c.take<float>(total) : nullptr;
+    b.ws = c.take<char>(wsb);
+    return c.used + 256;
+  };
+  NPA_TRY(arena_reserve(m, layout(nullptr)));
+  layout(m->arena.base);
+  cudaStream_t st = m->arena.stream;
+  auto h2d = [&](void* d, const void* h, size_t bytes) -> npa_status {
+    if (bytes) NPA_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st), "cudaMemcpyAsync H2D");
+    return NPA_OK;
+  };
+  auto d2h = [&](void* h, const void* d, size_t bytes) -> npa_status {
+    if (bytes && h) NPA_CUDA(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync D2H");
+    return NPA_OK;
+  };
+  NPA_TRY(h2d(b.pos, positions, size_t(total) * 16));
+  NPA_TRY(h2d(b.st, states, size_t(total) * C * 4));
+  if (update_mask) NPA_TRY(h2d(b.mask, update_mask, size_t(total) * 4));
+  NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(b.pos), b.st, batch, n, dt, b.mask,
+                             reinterpret_cast<float*>(b.np), b.ns, reinterpret_cast<float*>(b.dx),
+                             b.ds, b.feat, b.dens, b.ws, wsb, st));
+  NPA_TRY(d2h(next_positions, b.np, size_t(total) * 16));
+  NPA_TRY(d2h(next_states, b.ns, size_t(total) * C * 4));
+  if (dx) NPA_TRY(d2h(dx, b.dx, size_t(total) * 16));
+  if (ds) NPA_TRY(d2h(ds, b.ds, size_t(total) * C * 4));
+  if (features) NPA_TRY(d2h(features, b.feat, size_t(total) * F * 4));
+  if (density) NPA_TRY(d2h(density, b.dens, size_t(total) * 4));
+  NPA_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  return NPA_OK;
 }
 
 // ---- device operators ----
@@ -799,14 +924,16 @@ npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t b
   return NPA_OK;
 }
 
-npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
-                                         const npa_perception_options* o,
-                                         const float* d_positions, const float* d_states,
-                                         int64_t batch, int64_t n, int64_t state_dims,
-                                         float* d_features, float* d_density,
-                                         float* d_blurred_state, float* d_state_gradient,
-                                         float* d_density_gradient, void* d_workspace,
-                                         size_t workspace_bytes, void* stream) {
+namespace {
+
+// The phases of npa_dev_perceive_with_options; `ev` (4 events or null) are
+// recorded before the hashgrid, density and perception launches and after.
+npa_status perceive_phases(const npa_grid_config* cfg, const npa_perception_options* o,
+                           const float* d_positions, const float* d_states, int64_t batch,
+                           int64_t n, int64_t state_dims, float* d_features, float* d_density,
+                           float* d_blurred_state, float* d_state_gradient,
+                           float* d_density_gradient, void* d_workspace, size_t workspace_bytes,
+                           cudaStream_t st, cudaEvent_t* ev) {
   if (!o) return fail(NPA_ERR_INVALID_ARGUMENT, "options are null");
   size_t need = 0;
   NPA_TRY(npa_dev_perceive_workspace_size(cfg, batch, n, state_dims, &need));
@@ -819,14 +946,69 @@ npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
   PerceiveWorkspace w;
   if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w))
     return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ev) NPA_CUDA(cudaEventRecord(ev[0], st), "cudaEventRecord");
   NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
                           w.sort_scratch, w.sort_scratch_bytes, st));
+  if (ev) NPA_CUDA(cudaEventRecord(ev[1], st), "cudaEventRecord");
   const SortedGrid sv = sorted_view(w, N, B, d_positions);
   NPA_TRY(launch_density(g, sv, B, w.volume, d_density, w.hits, st));
-  return launch_perception(g, p, sv, w.hits, B, d_states, int(state_dims), w.volume, d_features,
-                           d_blurred_state, p.state_grad ? d_state_gradient : nullptr,
-                           p.density_grad ? d_density_gradient : nullptr, st);
+  if (ev) NPA_CUDA(cudaEventRecord(ev[2], st), "cudaEventRecord");
+  NPA_TRY(launch_perception(g, p, sv, w.hits, B, d_states, int(state_dims), w.volume, d_features,
+                            d_blurred_state, p.state_grad ? d_state_gradient : nullptr,
+                            p.density_grad ? d_density_gradient : nullptr, st));
+  if (ev) NPA_CUDA(cudaEventRecord(ev[3], st), "cudaEventRecord");
+  return NPA_OK;
+}
+
+}  // namespace
+
+npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
+                                         const npa_perception_options* o,
+                                         const float* d_positions, const float* d_states,
+                                         int64_t batch, int64_t n, int64_t state_dims,
+                                         float* d_features, float* d_density,
+                                         float* d_blurred_state, float* d_state_gradient,
+                                         float* d_density_gradient, void* d_workspace,
+                                         size_t workspace_bytes, void* stream) {
+  return perceive_phases(cfg, o, d_positions, d_states, batch, n, state_dims, d_features,
+                         d_density, d_blurred_state, d_state_gradient, d_density_gradient,
+                         d_workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+npa_status npa_dev_perceive_many_profiled(const npa_grid_config* cfg,
+                                          const npa_perception_options* o,
+                                          const float* d_positions, const float* d_states,
+                                          int64_t batch, int64_t n, int64_t state_dims,
+                                          float* d_features, float* d_density,
+                                          void* d_workspace, size_t workspace_bytes,
+                                          int64_t repeats, void* stream, float* phase_ms,
+                                          float* total_ms) {
+  if (repeats < 0 || (repeats > 0 && (!phase_ms || !total_ms)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "bad repeat count or null timing output");
+  if (repeats == 0) return NPA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<cudaEvent_t> ev(size_t(repeats) * 4, nullptr);
+  npa_status rc = NPA_OK;
+  for (auto& e : ev) {
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      e = nullptr;
+      rc = fail(NPA_ERR_CUDA, "cudaEventCreate");
+      break;
+    }
+  }
+  for (int64_t r = 0; rc == NPA_OK && r < repeats; ++r)
+    rc = perceive_phases(cfg, o, d_positions, d_states, batch, n, state_dims, d_features,
+                         d_density, nullptr, nullptr, nullptr, d_workspace, workspace_bytes, st,
+                         &ev[size_t(r) * 4]);
+  if (rc == NPA_OK && cudaStreamSynchronize(st) != cudaSuccess)
+    rc = fail(NPA_ERR_CUDA, "cudaStreamSynchronize");
+  for (int64_t r = 0; rc == NPA_OK && r < repeats; ++r)
+    for (int k = 0; k < 3; ++k)
+      cudaEventElapsedTime(&phase_ms[r * 3 + k], ev[r * 4 + k], ev[r * 4 + k + 1]);
+  if (rc == NPA_OK) cudaEventElapsedTime(total_ms, ev[0], ev[size_t(repeats) * 4 - 1]);
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  return rc;
 }
 
 npa_status npa_dev_model_forward_update(npa_model* m, const float* d_features, int64_t rows,

@@ -21,7 +21,7 @@ from typing import List, Optional
 import numpy as np
 
 from . import _lib
-from .config import (GaussianDecodeConfig, GaussianDecodeMode, HashGridConfig,
+from .config import (GaussianDecodeConfig, GaussianDecodeMode, HashGridConfig, InvalidArgument,
                      PerceptionOptions, feature_dims)
 
 
@@ -91,8 +91,13 @@ def build_hashgrid(positions, batch_size: int, particle_count: int,
 
 
 def perceive_with_options(positions, states, batch_size: int, particle_count: int,
-                          state_dims: int, cfg: HashGridConfig,
-                          options: PerceptionOptions) -> PerceptionOutput:
+                          state_dims: int, cfg: HashGridConfig, options: PerceptionOptions,
+                          outputs=("blurred_state", "state_gradient", "density_gradient"),
+                          out=None) -> PerceptionOutput:
+    """perceive_with_options (forward.rs:26-143).  Host arrays are copied to
+    the GPU and back; torch CUDA tensors stay on the device.  Host calls may
+    skip the intermediate outputs (`outputs`) and reuse caller-owned float32
+    arrays for (features, density) via `out`."""
     if _is_torch(positions):
         return _perceive_device(positions, states, batch_size, particle_count, state_dims, cfg,
                                 options)
@@ -100,11 +105,21 @@ def perceive_with_options(positions, states, batch_size: int, particle_count: in
     st = _f32(states).reshape(-1)
     total = batch_size * particle_count
     fd = feature_dims(cfg, options, state_dims) if cfg.dim in (2, 3) else 0
-    feats = np.zeros(max(total * fd, 0), np.float32)
-    dens = np.zeros(max(total, 0), np.float32)
-    blur = np.zeros(max(total * state_dims, 0), np.float32)
-    sgrad = np.zeros(max(total * state_dims * cfg.dim, 0) if options.state_grad else 0, np.float32)
-    dgrad = np.zeros(max(total * cfg.dim, 0) if options.density_grad else 0, np.float32)
+    if out is not None:
+        feats, dens = out
+        if (feats.dtype != np.float32 or dens.dtype != np.float32
+                or not feats.flags.c_contiguous or not dens.flags.c_contiguous
+                or feats.size != max(total * fd, 0) or dens.size != max(total, 0)):
+            raise InvalidArgument("out buffers must be contiguous float32 of the output's size")
+    else:
+        feats = np.zeros(max(total * fd, 0), np.float32)
+        dens = np.zeros(max(total, 0), np.float32)
+    want = set(outputs or ())
+    blur = np.zeros(max(total * state_dims, 0), np.float32) if "blurred_state" in want else None
+    sgrad = (np.zeros(max(total * state_dims * cfg.dim, 0) if options.state_grad else 0,
+                      np.float32) if "state_gradient" in want else None)
+    dgrad = (np.zeros(max(total * cfg.dim, 0) if options.density_grad else 0, np.float32)
+             if "density_gradient" in want else None)
     L = _lib.lib()
     g, o = _lib.grid_c(cfg), _lib.options_c(options)
     _lib.check(L.npa_perceive_with_options(
@@ -113,6 +128,60 @@ def perceive_with_options(positions, states, batch_size: int, particle_count: in
         _fp(blur), _fp(sgrad) if options.state_grad else None,
         _fp(dgrad) if options.density_grad else None), "perceive_with_options")
     return PerceptionOutput(feats, dens, blur, sgrad, dgrad, fd)
+
+
+class DevicePerception:
+    """Repeated perceive_with_options over one particle set's shape on the
+    device: the workspace and the feature / density outputs are allocated
+    once and reused (the hashgrid + perception pass of a caller that keeps
+    its particles in GPU memory)."""
+
+    def __init__(self, cfg: HashGridConfig, options: PerceptionOptions, batch: int, n: int,
+                 state_dims: int, device=None):
+        import torch
+
+        self.cfg, self.options = cfg, options
+        self.batch, self.n, self.state_dims = batch, n, state_dims
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None
+                                   else device)
+        self.feature_dims = feature_dims(cfg, options, state_dims)
+        self._g, self._o = _lib.grid_c(cfg), _lib.options_c(options)
+        ws = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().npa_dev_perceive_workspace_size(
+            ctypes.byref(self._g), batch, n, state_dims, ctypes.byref(ws)), "perceive")
+        self._ws_bytes = ws.value
+        total = batch * n
+        self.workspace = torch.empty(max(ws.value, 1), dtype=torch.uint8, device=self.device)
+        self.features = torch.empty(max(total * self.feature_dims, 1), dtype=torch.float32,
+                                    device=self.device)
+        self.density = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
+
+    def _stream(self, stream):
+        import torch
+
+        return stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+
+    def __call__(self, positions, states, stream=None):
+        """Features and density of device tensors positions [B*N, 4], states [B*N*C]."""
+        _lib.check(_lib.lib().npa_dev_perceive_with_options(
+            ctypes.byref(self._g), ctypes.byref(self._o), positions.data_ptr(),
+            states.data_ptr(), self.batch, self.n, self.state_dims, self.features.data_ptr(),
+            self.density.data_ptr(), None, None, None, self.workspace.data_ptr(),
+            self._ws_bytes, self._stream(stream)), "perceive")
+        return self.features, self.density
+
+    def run_profiled(self, positions, states, repeats: int, stream=None):
+        """`repeats` back-to-back passes with CUDA events between phases:
+        (phase_ms [repeats, 3] = hashgrid, density, perception; total_ms)."""
+        phase = np.zeros(max(repeats, 1) * 3, np.float32)
+        total = ctypes.c_float(0.0)
+        _lib.check(_lib.lib().npa_dev_perceive_many_profiled(
+            ctypes.byref(self._g), ctypes.byref(self._o), positions.data_ptr(),
+            states.data_ptr(), self.batch, self.n, self.state_dims, self.features.data_ptr(),
+            self.density.data_ptr(), self.workspace.data_ptr(), self._ws_bytes, repeats,
+            self._stream(stream), phase.ctypes.data_as(_lib.f32p), ctypes.byref(total)),
+            "perceive_many_profiled")
+        return phase[:repeats * 3].reshape(repeats, 3), float(total.value)
 
 
 def perceive(positions, states, batch_size, particle_count, state_dims, cfg, state_grad: bool,

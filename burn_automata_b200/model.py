@@ -121,20 +121,34 @@ class NpaModel:
         return dx, ds.reshape(-1)
 
     def step(self, positions, states, batch_size: int, particle_count: int,
-             grid: HashGridConfig, dt: float, update_mask=None) -> StepOutput:
-        """NpaModel::step_cpu (model.rs:768-858), executed on the GPU."""
+             grid: HashGridConfig, dt: float, update_mask=None,
+             outputs=("dx", "ds", "features", "density"), out=None) -> StepOutput:
+        """NpaModel::step_cpu (model.rs:768-858), executed on the GPU.
+
+        `outputs` selects which of the StepOutput extras are copied back (the
+        reference always builds all of them); `out` = (next_positions,
+        next_states) reuses caller-owned float32 host arrays (pinned ones make
+        the copies asynchronous DMA)."""
         pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
         st = _f32(states).reshape(-1)
         total = batch_size * particle_count
         C = self.config.state_dims
-        mask = _f32(update_mask).reshape(-1) if update_mask is not None else None
-        npos = np.zeros((max(total, 0), 4), np.float32)
-        nst = np.zeros(max(total * C, 0), np.float32)
-        dx = np.zeros((max(total, 0), 4), np.float32)
-        ds = np.zeros(max(total * C, 0), np.float32)
         F = self.config.perception_dims()
-        feats = np.zeros(max(total * F, 0), np.float32)
-        dens = np.zeros(max(total, 0), np.float32)
+        mask = _f32(update_mask).reshape(-1) if update_mask is not None else None
+        if out is not None:
+            npos, nst = out
+            if (npos.dtype != np.float32 or nst.dtype != np.float32 or not npos.flags.c_contiguous
+                    or not nst.flags.c_contiguous or npos.size != max(total, 0) * 4
+                    or nst.size != max(total * C, 0)):
+                raise InvalidArgument("out buffers must be contiguous float32 of the step's size")
+        else:
+            npos = np.zeros((max(total, 0), 4), np.float32)
+            nst = np.zeros(max(total * C, 0), np.float32)
+        want = set(outputs or ())
+        dx = np.zeros((max(total, 0), 4), np.float32) if "dx" in want else None
+        ds = np.zeros(max(total * C, 0), np.float32) if "ds" in want else None
+        feats = np.zeros(max(total * F, 0), np.float32) if "features" in want else None
+        dens = np.zeros(max(total, 0), np.float32) if "density" in want else None
         g = _lib.grid_c(grid)
         _lib.check(_lib.lib().npa_model_step(
             self._handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],

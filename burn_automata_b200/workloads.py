@@ -122,11 +122,14 @@ def learned_scale_decode() -> GaussianDecodeConfig:
 
 
 def make(name: str, seed: int = 0, *, batch: Optional[int] = None, n: Optional[int] = None,
-         steps: Optional[int] = None, first: int = 0) -> Workload:
+         steps: Optional[int] = None, first: int = 0,
+         components: Optional[int] = None) -> Workload:
     """Build one configuration.  batch / n / steps override the sizes for
     reduced parity cases; everything else stays as the configuration names it.
     `first` is the global index of the first rollout, so a shard of a batched
-    configuration draws exactly the rollouts the full batch would."""
+    configuration draws exactly the rollouts the full batch would.
+    `components` (cfg4 only) sets the number of mixture components; 1 with
+    n = 65,536 is one component of the full draw at its particle density."""
     if name == "cfg0":
         b = batch or 1
         n_ = n or 4096
@@ -169,7 +172,9 @@ def make(name: str, seed: int = 0, *, batch: Optional[int] = None, n: Optional[i
         n_ = n or (1 << 22)
         model = cfg0_model()
         grid = cfg0_grid()
-        pos = np.concatenate([mixture_positions_2d(n_, seed + 1000 * (first + k)) for k in range(b)])
+        comp = components or 64
+        pos = np.concatenate([mixture_positions_2d(n_, seed + 1000 * (first + k), comp)
+                              for k in range(b)])
         st = np.concatenate([normal_states(n_, 16, 0.1, seed + 1 + 1000 * (first + k)) for k in range(b)])
         return Workload("cfg4", b, n_, steps or 32, 0.1, grid, model, model.perception_options(),
                         learned_scale_decode(), pos, st, kaiming_weights(model, seed + 2), 16)

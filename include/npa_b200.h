@@ -276,6 +276,20 @@ npa_status npa_dev_perceive_with_options(const npa_grid_config* cfg,
                                          float* d_density_gradient, void* d_workspace,
                                          size_t workspace_bytes, void* stream);
 
+/* Benchmark aid, no reference counterpart: `repeats` back-to-back
+ * npa_dev_perceive_with_options calls (features and density written) with
+ * CUDA events recorded on `stream` between their phases.  phase_ms receives
+ * repeats*3 durations (hashgrid build, density, perception) and total_ms the
+ * span from the first launch to the last.  Synchronises `stream`. */
+npa_status npa_dev_perceive_many_profiled(const npa_grid_config* cfg,
+                                          const npa_perception_options* options,
+                                          const float* d_positions, const float* d_states,
+                                          int64_t batch, int64_t n, int64_t state_dims,
+                                          float* d_features, float* d_density,
+                                          void* d_workspace, size_t workspace_bytes,
+                                          int64_t repeats, void* stream, float* phase_ms,
+                                          float* total_ms);
+
 /* forward_update_from_features on device buffers (model.rs:900-940). */
 npa_status npa_dev_model_forward_update(npa_model* model, const float* d_features, int64_t rows,
                                         float* d_update, void* stream);

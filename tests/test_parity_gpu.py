@@ -301,3 +301,69 @@ def test_device_tensor_perception_matches_host():
                                    w.options)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(dev.features.cpu().numpy(), host.features)
+
+
+def test_device_perception_runner_and_profiled_repeats():
+    import torch
+
+    w = workloads.make("cfg1", n=1 << 15, steps=1)
+    host = ba.perceive_with_options(w.positions, w.states, 1, w.n, 32, w.grid, w.options)
+    run = ba.DevicePerception(w.grid, w.options, 1, w.n, 32)
+    d_pos = torch.from_numpy(w.positions).cuda()
+    d_st = torch.from_numpy(w.states).cuda()
+    feats, dens = run(d_pos, d_st)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(feats.cpu().numpy(), host.features)
+    np.testing.assert_array_equal(dens.cpu().numpy(), host.density)
+    run.features.zero_()
+    phase, total = run.run_profiled(d_pos, d_st, 3)
+    assert phase.shape == (3, 3) and np.all(phase > 0) and total >= phase.sum() * 0.5
+    np.testing.assert_array_equal(run.features.cpu().numpy(), host.features)
+
+
+def test_host_perception_output_selection_and_out_buffers():
+    w = workloads.make("cfg1", n=1 << 14, steps=1)
+    full = ba.perceive_with_options(w.positions, w.states, 1, w.n, 32, w.grid, w.options)
+    out = (np.full(full.features.size, np.nan, np.float32),
+           np.full(full.density.size, np.nan, np.float32))
+    part = ba.perceive_with_options(w.positions, w.states, 1, w.n, 32, w.grid, w.options,
+                                    outputs=(), out=out)
+    assert part.features is out[0] and part.blurred_state is None
+    np.testing.assert_array_equal(out[0], full.features)
+    np.testing.assert_array_equal(out[1], full.density)
+
+
+def test_host_step_reuses_buffers_across_sizes(oracle_mod):
+    """Repeated host-buffer steps (growing and shrinking sizes) through the
+    model's reusable device buffers match the oracle each time."""
+    w = workloads.make("cfg2", batch=4, steps=1)
+    m = make_model(w)
+    for b in (1, 4, 2):
+        sub = workloads.make("cfg2", batch=b, steps=1)
+        out = (np.empty((b * sub.n, 4), np.float32), np.empty(b * sub.n * 16, np.float32))
+        r = m.step(sub.positions, sub.states, b, sub.n, sub.grid, sub.dt, outputs=(), out=out)
+        assert r.dx is None and r.features is None and r.next_positions is out[0]
+        ref = oracle_mod.step(sub.model, sub.weights, sub.grid, sub.positions, sub.states, b,
+                              sub.n, sub.dt)
+        np.testing.assert_allclose(out[1], ref["next_states"], rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(out[0], ref["next_positions"], rtol=RTOL, atol=ATOL)
+
+
+def test_host_calls_report_out_of_memory_under_an_allocation_cap():
+    """The host-buffer entry points return OutOfMemory (not a crash) when their
+    device allocations are refused; the cap is a test hook, lifted after."""
+    from burn_automata_b200.config import OutOfMemory
+
+    L = ba.load_library()
+    w = workloads.make("cfg0", n=1024, steps=1)
+    m = make_model(w)
+    L.npa_debug_set_allocation_cap(4096)
+    try:
+        with pytest.raises(OutOfMemory):
+            m.step(w.positions, w.states, 1, w.n, w.grid, w.dt)
+        with pytest.raises(OutOfMemory):
+            ba.perceive_with_options(w.positions, w.states, 1, w.n, 16, w.grid, w.options)
+    finally:
+        L.npa_debug_set_allocation_cap(0)
+    r = m.step(w.positions, w.states, 1, w.n, w.grid, w.dt)
+    assert np.isfinite(r.next_states).all()
