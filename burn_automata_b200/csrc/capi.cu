@@ -1055,7 +1055,7 @@ npa_status npa_dev_step_workspace_size(npa_model* m, const npa_grid_config* grid
   const GridParams g = make_grid_params(*grid);
   *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n),
                                     tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims,
-                                                 step_tile_rows(m->dm)));
+                                                 step_tile_rows(m->dm, uint64_t(batch) * n)));
   return NPA_OK;
 }
 
@@ -1076,7 +1076,7 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   if (!mlp_step_supported(m->dm))
     return fail(NPA_ERR_UNSUPPORTED, "step shape outside the supported range");
   PerceiveWorkspace w;
-  const int tile_rows = step_tile_rows(m->dm);
+  const int tile_rows = step_tile_rows(m->dm, total);
   if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w,
                       tiles_floats(B, N, m->dm.feature_dims, tile_rows)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
@@ -1094,7 +1094,7 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   out.dx = reinterpret_cast<float4*>(d_dx);
   out.ds = d_ds;
   out.features = d_features;
-  return launch_mlp_step(m->dm, g, sv, B, w.tiles, dt, d_update_mask, out, st);
+  return launch_mlp_step(m->dm, g, sv, B, w.tiles, d_states, dt, d_update_mask, out, st);
 }
 
 }  // extern "C"
@@ -1148,7 +1148,8 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
       out.dx = nullptr;
       out.ds = nullptr;
       out.features = nullptr;
-      return launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, dt, nullptr, out, s);
+      return launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr, out,
+                             s);
     }
   }
 }
@@ -1220,7 +1221,7 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   e->n = n;
   const size_t total = size_t(batch) * n;
   const size_t C = size_t(m->dm.state_dims);
-  e->tile_rows = step_tile_rows(m->dm);
+  e->tile_rows = step_tile_rows(m->dm, total);
   const size_t tf = tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims, e->tile_rows);
   e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n), tf);
   npa_status st = NPA_OK;

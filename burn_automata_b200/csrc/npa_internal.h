@@ -125,13 +125,15 @@ struct StepOutputs {
   float* features;   // optional
 };
 int hidden_padded_for(int hidden);
-// Rows per feature tile of the MLP stage (depends on the padded hidden width).
-int step_tile_rows(const DeviceModel& m);
+// Rows per feature tile of the MLP stage for a step over `rows` particles
+// (depends on the padded hidden width, the feature width and the row count).
+int step_tile_rows(const DeviceModel& m, uint64_t rows);
 bool mlp_step_supported(const DeviceModel& m);
 // MLP + dx/ds (+3D gates) + Euler over feature tiles in sorted order.
 // Tiles [tile_begin, tile_end) of the step (default: all).
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& s,
-                           uint32_t batch, const float* tiles, float dt, const float* mask,
+                           uint32_t batch, const float* tiles, const float* states, float dt,
+                           const float* mask,
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 

@@ -9,17 +9,21 @@
 // the reference-order MLP stays at ~3.5e-4, so the MLP runs on the FP32
 // pipe as separate multiply and add (the library is built with --fmad=false).
 //
-// Work layout: kThreads threads per block, HG x RG thread grid with
-// HG = Hp / kTH hidden groups and RG = kThreads / HG row groups; a tile holds
+// Work layout: NT threads per block (384, or 256 when a 384-thread tile does
+// not fit in shared memory), HG x RG thread grid with
+// HG = Hp / kTH hidden groups and RG = NT / HG row groups; a tile holds
 // M = 8 * RG rows.
 //   layer 1: each thread owns an 8 rows x kTH hidden-unit register tile and
 //            walks k = 0..F-1 in order (features of the tile feature-major in
 //            shared memory, w1 transposed in shared memory);
-//   layer 2: kThreads / M threads per row, each owning ceil(O / (kThreads / M))
+//   layer 2: NT / M threads per row, each owning ceil(O / (NT / M))
 //            outputs, sequential over h.
 // The rollout's MLP stage consumes the feature tiles written by
-// perception_tiles_kernel ([tile][F][M], sorted order), double-buffered with
-// cp.async, and finishes each row with forward_from_features_with_eps
+// perception_tiles_kernel ([tile][F][M], sorted order) through one shared
+// buffer: the next tile is fetched with cp.async once layer 1 has consumed
+// the current one, behind layer 2 and the epilogue (one buffer instead of two
+// is what lets 12 warps per SM fit; measured 1.017 vs 1.067 ms at 8 warps
+// double-buffered on cfg2).  Each row finishes with forward_from_features_with_eps
 // (model.rs:867-898), the 3D position gates (model.rs:806-837) and euler_step
 // (crates/burn_automata_kernels/src/reference/step.rs:4-55), writing the next
 // position / state in the caller's particle order.
@@ -30,16 +34,18 @@
 namespace npa {
 namespace {
 
-constexpr int kThreads = 256;  // threads per block
+constexpr int kThreadsWide = 384;    // 12 warps per SM: 3 per scheduler
+constexpr int kThreadsNarrow = 256;  // when the wide tile does not fit in shared memory
 constexpr int kTH = 8;         // hidden units per thread in layer 1
 constexpr int kKC = 16;              // k slice when w1 is streamed
-constexpr int kMaxOut = 32;          // outputs per thread in layer 2
+constexpr int kMaxOut = 64;          // outputs per thread in layer 2 (passes of kL2Chunk)
 constexpr size_t kSmemBudget = 220 * 1024;
 
 struct MlpShape {
+  int NT;          // threads per block
   int F, H, Hp, O;
   int M;           // rows per tile
-  int tpr;         // layer-2 threads per row (256 / M)
+  int tpr;         // layer-2 threads per row (NT / M)
   int hid_stride;  // Hp + 4
   int w2_stride;   // Hp + 4
   int out_stride;  // O + 1
@@ -47,10 +53,10 @@ struct MlpShape {
 };
 
 struct SmemLayout {
-  size_t ft0, ft1, hid, w1, w2, outs, total;  // offsets in floats
+  size_t ft0, hid, w1, w2, outs, total;  // offsets in floats
 };
 
-__host__ __device__ inline SmemLayout smem_layout(const MlpShape& s, bool double_buffer) {
+__host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
   SmemLayout l;
   size_t off = 0;
   auto take = [&](size_t floats) {
@@ -59,7 +65,6 @@ __host__ __device__ inline SmemLayout smem_layout(const MlpShape& s, bool double
     return o;
   };
   l.ft0 = take(size_t(s.F) * s.M);
-  l.ft1 = double_buffer ? take(size_t(s.F) * s.M) : l.ft0;
   l.hid = take(size_t(s.M) * s.hid_stride);
   l.w1 = take(size_t(s.w1_resident ? s.F : kKC) * s.Hp);
   l.w2 = take(size_t(s.O) * s.w2_stride);
@@ -84,7 +89,7 @@ __device__ __forceinline__ void cp_async_wait() {
 __device__ __forceinline__ void load_weights(const MlpShape& s, const float* __restrict__ w1t,
                                              const float* __restrict__ w2, float* w1s,
                                              float* w2s) {
-  for (int e = threadIdx.x; e < s.O * s.H; e += kThreads) {
+  for (int e = threadIdx.x; e < s.O * s.H; e += blockDim.x) {
     const int o = e / s.H, h = e - o * s.H;
     w2s[o * s.w2_stride + h] = __ldg(w2 + e);
   }
@@ -92,7 +97,7 @@ __device__ __forceinline__ void load_weights(const MlpShape& s, const float* __r
     const float4* src = reinterpret_cast<const float4*>(w1t);
     float4* dst = reinterpret_cast<float4*>(w1s);
     const int n4 = s.F * s.Hp / 4;
-    for (int e = threadIdx.x; e < n4; e += kThreads) dst[e] = __ldg(src + e);
+    for (int e = threadIdx.x; e < n4; e += blockDim.x) dst[e] = __ldg(src + e);
   }
 }
 
@@ -133,11 +138,11 @@ __device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __res
   for (int j = 0; j < kTH; ++j) bias[j] = (h0 + j < s.H) ? __ldg(b1 + h0 + j) : 0.0f;
 }
 
-template <int HG>
+template <int HG, int NT>
 __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
                                            const float (&bias)[kTH], const float* ft,
                                            float* w1s, float* hid) {
-  constexpr int RG = kThreads / HG;
+  constexpr int RG = NT / HG;
   constexpr int M = RG * 8;
   const int t = threadIdx.x;
   const int rg = t / HG;
@@ -168,7 +173,7 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
       __syncthreads();  // previous slice consumed
       const float4* src = reinterpret_cast<const float4*>(w1t + size_t(kc) * s.Hp);
       float4* dst = reinterpret_cast<float4*>(w1s);
-      for (int e = t; e < kn * hp4; e += kThreads) dst[e] = __ldg(src + e);
+      for (int e = t; e < kn * hp4; e += NT) dst[e] = __ldg(src + e);
       __syncthreads();
       const float* wcol = w1s + h0;
       for (int kk = 0; kk < kn; ++kk) {
@@ -195,22 +200,24 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
 }
 
 // Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
-// tpr threads per row; thread j owns outputs o = j + tpr * u, u < NOUT
-// (NOUT = ceil(O / tpr), the last one masked for threads past O).
+// tpr threads per row; thread j owns outputs o = j + tpr * u.  One call
+// handles u in [u0, u0 + NOUT) (outputs past O are computed on a valid row
+// and not stored).
 template <int NOUT>
 __device__ __forceinline__ void mlp_layer2(const MlpShape& s, const float* __restrict__ b2,
-                                           const float* hid, const float* w2s, float* outs) {
+                                           const float* hid, const float* w2s, float* outs,
+                                           int u0) {
   const int t = threadIdx.x;
   const int r = t / s.tpr;
   const int j = t - r * s.tpr;
-  const bool last_ok = j + s.tpr * (NOUT - 1) < s.O;
   float acc[NOUT];
   const float* wrow[NOUT];
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
-    const int o = (u == NOUT - 1 && !last_ok) ? j : j + s.tpr * u;
-    acc[u] = __ldg(b2 + o);
-    wrow[u] = w2s + o * s.w2_stride;
+    const int o = j + s.tpr * (u0 + u);
+    const int oo = o < s.O ? o : j;
+    acc[u] = __ldg(b2 + oo);
+    wrow[u] = w2s + oo * s.w2_stride;
   }
   const float* hrow = hid + r * s.hid_stride;
   const int H4 = s.H & ~3;
@@ -238,38 +245,43 @@ __device__ __forceinline__ void mlp_layer2(const MlpShape& s, const float* __res
     for (int u = 0; u < NOUT; ++u) acc[u] = acc[u] + wrow[u][h] * hv;
   }
 #pragma unroll
-  for (int u = 0; u < NOUT; ++u)
-    if (u < NOUT - 1 || last_ok) outs[r * s.out_stride + j + s.tpr * u] = acc[u];
+  for (int u = 0; u < NOUT; ++u) {
+    const int o = j + s.tpr * (u0 + u);
+    if (o < s.O) outs[r * s.out_stride + o] = acc[u];
+  }
 }
 
-// Dispatches layer 2 on the per-thread output count.
+// Layer 2 over all of a thread's outputs, at most kL2Chunk per pass over the
+// hidden row (bounds the registers of the accumulators).
+constexpr int kL2Chunk = 16;
 __device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
                                                const float* hid, const float* w2s, float* outs) {
-  switch ((s.O + s.tpr - 1) / s.tpr) {
+  const int per_thread = (s.O + s.tpr - 1) / s.tpr;
+  for (int u0 = 0; u0 < per_thread; u0 += kL2Chunk) {
+    switch (min(kL2Chunk, per_thread - u0)) {
 #define NPA_L2(N) \
   case N:         \
-    mlp_layer2<N>(s, b2, hid, w2s, outs); \
+    mlp_layer2<N>(s, b2, hid, w2s, outs, u0); \
     break;
-    NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
-    NPA_L2(9) NPA_L2(10) NPA_L2(11) NPA_L2(12) NPA_L2(13) NPA_L2(14) NPA_L2(15) NPA_L2(16)
-    NPA_L2(17) NPA_L2(18) NPA_L2(19) NPA_L2(20) NPA_L2(21) NPA_L2(22) NPA_L2(23) NPA_L2(24)
-    NPA_L2(25) NPA_L2(26) NPA_L2(27) NPA_L2(28) NPA_L2(29) NPA_L2(30) NPA_L2(31) NPA_L2(32)
+      NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
+      NPA_L2(9) NPA_L2(10) NPA_L2(11) NPA_L2(12) NPA_L2(13) NPA_L2(14) NPA_L2(15) NPA_L2(16)
 #undef NPA_L2
-    default:
-      break;
+      default:
+        break;
+    }
   }
 }
 
 // API MLP: rows of the caller's row-major feature matrix.
-template <int HG>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int HG, int NT>
+__global__ void __launch_bounds__(NT, 1)
 forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __restrict__ b1,
                       const float* __restrict__ w2, const float* __restrict__ b2,
                       const float* __restrict__ features, uint32_t rows,
                       float* __restrict__ update) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
-  const SmemLayout L = smem_layout(s, false);
+  const SmemLayout L = smem_layout(s);
   float* ft = smem + L.ft0;
   float* hid = smem + L.hid;
   float* w1s = smem + L.w1;
@@ -282,17 +294,17 @@ forward_update_kernel(MlpShape s, const float* __restrict__ w1t, const float* __
   for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     __syncthreads();
     const uint32_t row0 = tile * s.M;
-    for (int e = threadIdx.x; e < s.M * s.F; e += kThreads) {
+    for (int e = threadIdx.x; e < s.M * s.F; e += NT) {
       const int r = e / s.F, f = e - r * s.F;
       const uint32_t row = row0 + r;
       ft[f * s.M + r] = row < rows ? __ldg(features + size_t(row) * s.F + f) : 0.0f;
     }
     __syncthreads();
-    mlp_layer1<HG>(s, w1t, bias1, ft, w1s, hid);
+    mlp_layer1<HG, NT>(s, w1t, bias1, ft, w1s, hid);
     __syncthreads();
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
-    for (int e = threadIdx.x; e < s.M * s.O; e += kThreads) {
+    for (int e = threadIdx.x; e < s.M * s.O; e += NT) {
       const int r = e / s.O, o = e - r * s.O;
       const uint32_t row = row0 + r;
       if (row < rows) update[size_t(row) * s.O + o] = outs[r * s.out_stride + o];
@@ -346,11 +358,16 @@ struct StepParams {
   int gates3d;       // dim == 3 && position_features && C > 3 (model.rs:806-809)
   int C;
   int D;
+  const float* states;  // the step's input states [B*N][C] (caller order)
 };
 
+// Own-state channels a thread keeps in registers between layer 1 and the
+// epilogue (the rest, C > kStateRegs * threads per row, are read there).
+constexpr int kStateRegs = 8;
+
 // The rollout step's MLP stage over feature tiles in sorted order.
-template <int HG>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int HG, int NT>
+__global__ void __launch_bounds__(NT, 1)
 mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_t tile_begin,
                 uint32_t tile_end, const float* __restrict__ tiles_in, const float* __restrict__ w1t,
                 const float* __restrict__ b1, const float* __restrict__ w2,
@@ -360,37 +377,35 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
                 float* __restrict__ ds_out, float* __restrict__ features_out) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
-  const SmemLayout L = smem_layout(s, true);
-  float* ftb[2] = {smem + L.ft0, smem + L.ft1};
+  // One feature-tile buffer: the next tile is fetched while layer 2 and the
+  // epilogue of this one run (the tile is dead once layer 1 has read it).
+  const SmemLayout L = smem_layout(s);
+  float* ft = smem + L.ft0;
   float* hid = smem + L.hid;
   float* w1s = smem + L.w1;
   float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
+  constexpr int TPR = HG / 8;  // layer-2 / epilogue threads per row (NT / M)
   const int C = sp.C, D = sp.D;
   const uint32_t tiles = tile_end;
   const int chunks16 = s.F * s.M / 4;  // 16-byte chunks per feature tile
-  auto issue = [&](uint32_t tile, float* dst) {
-    const float* src = tiles_in + size_t(tile) * s.F * s.M;
-    for (int e = threadIdx.x; e < chunks16; e += kThreads) cp_async16(dst + 4 * e, src + 4 * e);
+  auto issue = [&](uint32_t t) {
+    const float* src = tiles_in + size_t(t) * s.F * s.M;
+    for (int e = threadIdx.x; e < chunks16; e += NT) cp_async16(ft + 4 * e, src + 4 * e);
+    cp_async_commit();
   };
   uint32_t tile = tile_begin + blockIdx.x;
-  if (tile < tiles) issue(tile, ftb[0]);
-  cp_async_commit();
+  if (tile < tiles) issue(tile);
   load_weights(s, w1t, w2, w1s, w2s);
   float bias1[kTH];
   load_bias1<HG>(s, b1, bias1);
-  int buf = 0;
-  for (; tile < tiles; tile += gridDim.x, buf ^= 1) {
-    const uint32_t next = tile + gridDim.x;
-    if (next < tiles) issue(next, ftb[buf ^ 1]);
-    cp_async_commit();
-    cp_async_wait<1>();
+  const int r = threadIdx.x / TPR;
+  const int part = threadIdx.x - r * TPR;
+  for (; tile < tiles; tile += gridDim.x) {
+    cp_async_wait<0>();
     __syncthreads();
-    const float* ft = ftb[buf];
-    // The epilogue's global reads are issued before layer 1 so their latency
-    // is hidden behind it.
-    const int r = threadIdx.x / s.tpr;
-    const int part = threadIdx.x - r * s.tpr;
+    // The epilogue's position / mask reads are issued before layer 1 so
+    // their latency is hidden behind it.
     const uint32_t q = tile * s.M + r;
     const bool live = q < total;
     size_t row = 0;
@@ -402,61 +417,98 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
       pi = __ldg(sg.positions + row);
       if (mask) m = __ldg(mask + row);
     }
-    mlp_layer1<HG>(s, w1t, bias1, ft, w1s, hid);
+    mlp_layer1<HG, NT>(s, w1t, bias1, ft, w1s, hid);
+    if (features_out && live)
+      for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
     __syncthreads();
+    const uint32_t next = tile + gridDim.x;
+    if (next < tiles) issue(next);
+    // own state for the Euler update, hidden behind layer 2
+    float sv[kStateRegs];
+#pragma unroll
+    for (int j = 0; j < kStateRegs; ++j) {
+      const int ch = part + j * TPR;
+      sv[j] = (live && ch < C) ? __ldg(sp.states + row * C + ch) : 0.0f;
+    }
+    float liveness = 0.0f, sd = 0.0f;
+    if (sp.gates3d && live) {
+      liveness = __ldg(sp.states + row * C + 3);
+      sd = __ldg(sp.states + row * C + 7);
+    }
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
-    // forward_from_features_with_eps + gates + euler_step, tpr threads per row
+    // forward_from_features_with_eps + gates + euler_step, TPR threads per row
     if (live) {
       const float* u = outs + r * s.out_stride;
       float norm = 0.0f;
-      for (int a = 0; a < D; ++a) norm = norm + u[a] * u[a];
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+        if (a < D) norm = norm + u[a] * u[a];
       norm = sqrtf(norm);
       float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int a = 0; a < D; ++a) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+        if (a < D) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
       float state_gate = 1.0f;
       if (sp.gates3d) {
         // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
-        const float liveness = ft[3 * s.M + r];
-        const float sd = ft[7 * s.M + r];
         state_gate = clamp_rs((4.0f - liveness) * 2.0f, 0.0f, 1.0f);
         float motion_gate = 0.0f;
         if (!(pi.w >= 0.5f)) motion_gate = state_gate * clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
-        for (int a = 0; a < D; ++a) dx[a] = dx[a] * motion_gate;
+#pragma unroll
+        for (int a = 0; a < 4; ++a) dx[a] = dx[a] * motion_gate;
       }
       if (part == 0) {
         next_pos[row] = euler_position(g, ep, pi, dx, m);
         if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
       }
-      for (int ch = part; ch < C; ch += s.tpr) {
+#pragma unroll
+      for (int j = 0; j < kStateRegs; ++j) {
+        const int ch = part + j * TPR;
+        if (ch < C) {
+          float dsv = u[D + ch];
+          if (sp.gates3d) dsv = dsv * state_gate;
+          next_states[row * C + ch] = euler_state(ep, C, ch, sv[j], dsv, m);
+          if (ds_out) ds_out[row * C + ch] = dsv;
+        }
+      }
+      for (int ch = part + kStateRegs * TPR; ch < C; ch += TPR) {
         float dsv = u[D + ch];
         if (sp.gates3d) dsv = dsv * state_gate;
-        next_states[row * C + ch] = euler_state(ep, C, ch, ft[ch * s.M + r], dsv, m);
+        next_states[row * C + ch] = euler_state(ep, C, ch, __ldg(sp.states + row * C + ch), dsv, m);
         if (ds_out) ds_out[row * C + ch] = dsv;
       }
-      if (features_out)
-        for (int f = part; f < s.F; f += s.tpr) features_out[row * s.F + f] = ft[f * s.M + r];
     }
-    __syncthreads();
   }
   cp_async_wait<0>();
 }
 
-MlpShape make_shape(const DeviceModel& m, bool double_buffer) {
+MlpShape shape_with(const DeviceModel& m, int nt) {
   MlpShape s;
+  s.NT = nt;
   s.F = m.feature_dims;
   s.H = m.hidden_dims;
   s.Hp = m.hidden_padded;
   s.O = m.update_dims;
   const int HG = s.Hp / kTH;
-  s.M = (kThreads / HG) * 8;
-  s.tpr = kThreads / s.M;
+  s.M = (nt / HG) * 8;
+  s.tpr = nt / s.M;
   s.hid_stride = s.Hp + 4;
   s.w2_stride = s.Hp + 4;
   s.out_stride = s.O + 1;
   s.w1_resident = 1;
-  if (smem_layout(s, double_buffer).total * sizeof(float) > kSmemBudget) s.w1_resident = 0;
+  if (smem_layout(s).total * sizeof(float) > kSmemBudget) s.w1_resident = 0;
   return s;
+}
+
+// The 384-thread shape for `rows` rows when its tile fits in shared memory
+// and there are enough rows for a wide tile per SM (148 on B200); else 256
+// threads (smaller tiles, so small rollouts spread over more SMs).
+MlpShape make_shape(const DeviceModel& m, uint64_t rows) {
+  const MlpShape wide = shape_with(m, kThreadsWide);
+  if (smem_layout(wide).total * sizeof(float) <= kSmemBudget && rows >= uint64_t(148) * wide.M)
+    return wide;
+  return shape_with(m, kThreadsNarrow);
 }
 
 struct LaunchCfg {
@@ -465,8 +517,8 @@ struct LaunchCfg {
 };
 
 template <class K>
-npa_status plan(K kernel, const MlpShape& s, bool double_buffer, uint64_t tiles, LaunchCfg* out) {
-  const size_t smem = smem_layout(s, double_buffer).total * sizeof(float);
+npa_status plan(K kernel, const MlpShape& s, uint64_t tiles, LaunchCfg* out) {
+  const size_t smem = smem_layout(s).total * sizeof(float);
   int dev = 0;
   NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   int max_optin = 0, sms = 0;
@@ -479,7 +531,7 @@ npa_status plan(K kernel, const MlpShape& s, bool double_buffer, uint64_t tiles,
   NPA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
            "cudaFuncSetAttribute");
   int per_sm = 0;
-  NPA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem),
+  NPA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, s.NT, smem),
            "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   if (per_sm < 1) return fail(NPA_ERR_UNSUPPORTED, "MLP kernel cannot be resident");
   const uint64_t slots = uint64_t(per_sm) * sms;
@@ -490,16 +542,16 @@ npa_status plan(K kernel, const MlpShape& s, bool double_buffer, uint64_t tiles,
 
 bool shape_ok(const DeviceModel& m) {
   if (m.hidden_padded != 64 && m.hidden_padded != 128 && m.hidden_padded != 256) return false;
-  const int M = (kThreads / (m.hidden_padded / kTH)) * 8;
-  const int tpr = kThreads / M;
-  return (m.update_dims + tpr - 1) / tpr <= kMaxOut && m.feature_dims >= 1;
+  const MlpShape s = make_shape(m, 0);  // the narrow shape: it fits whenever any does
+  return (m.update_dims + s.tpr - 1) / s.tpr <= kMaxOut && m.feature_dims >= 1 &&
+         smem_layout(s).total * sizeof(float) <= kSmemBudget;
 }
 
 }  // namespace
 
 int hidden_padded_for(int hidden) { return hidden <= 64 ? 64 : (hidden <= 128 ? 128 : 256); }
 
-int step_tile_rows(const DeviceModel& m) { return (kThreads / (m.hidden_padded / kTH)) * 8; }
+int step_tile_rows(const DeviceModel& m, uint64_t rows) { return make_shape(m, rows).M; }
 
 bool mlp_step_supported(const DeviceModel& m) {
   return m.state_dims >= 0 && m.hidden_dims >= 1 && m.hidden_dims <= 256 && shape_ok(m);
@@ -510,19 +562,25 @@ npa_status launch_forward_update(const DeviceModel& m, const float* features, ui
   if (rows == 0) return NPA_OK;
   if (!mlp_step_supported(m))
     return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range");
-  const MlpShape s = make_shape(m, false);
+  const MlpShape s = make_shape(m, rows);
   const uint64_t tiles = (uint64_t(rows) + s.M - 1) / s.M;
   LaunchCfg lc;
-#define NPA_FWD(HGV)                                                                          \
+#define NPA_FWD(HGV, NTV)                                                                     \
   do {                                                                                        \
-    NPA_TRY(plan(forward_update_kernel<HGV>, s, false, tiles, &lc));                          \
-    forward_update_kernel<HGV><<<lc.grid, kThreads, lc.smem, stream>>>(s, m.w1t, m.b1, m.w2,  \
+    NPA_TRY(plan(forward_update_kernel<HGV, NTV>, s, tiles, &lc));                            \
+    forward_update_kernel<HGV, NTV><<<lc.grid, NTV, lc.smem, stream>>>(s, m.w1t, m.b1, m.w2,  \
                                                                        m.b2, features, rows,  \
                                                                        update);               \
   } while (0)
-  if (s.Hp == 64) NPA_FWD(64 / kTH);
-  else if (s.Hp == 128) NPA_FWD(128 / kTH);
-  else NPA_FWD(256 / kTH);
+#define NPA_FWD_NT(NTV)                          \
+  do {                                           \
+    if (s.Hp == 64) NPA_FWD(64 / kTH, NTV);      \
+    else if (s.Hp == 128) NPA_FWD(128 / kTH, NTV); \
+    else NPA_FWD(256 / kTH, NTV);                \
+  } while (0)
+  if (s.NT == kThreadsWide) NPA_FWD_NT(kThreadsWide);
+  else NPA_FWD_NT(kThreadsNarrow);
+#undef NPA_FWD_NT
 #undef NPA_FWD
   return after_launch("forward_update_kernel");
 }
@@ -540,15 +598,17 @@ npa_status launch_euler(const GridParams& g, const float4* positions, const floa
 }
 
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
-                           uint32_t batch, const float* tiles, float dt, const float* mask,
+                           uint32_t batch, const float* tiles, const float* states, float dt,
+                           const float* mask,
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin,
                            uint32_t tile_end) {
   const uint32_t total = batch * sgrid.n;
   if (total == 0) return NPA_OK;
   if (!mlp_step_supported(m))
     return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range");
-  const MlpShape s = make_shape(m, true);
+  const MlpShape s = make_shape(m, total);
   StepParams sp;
+  sp.states = states;
   sp.alpha = m.alpha;
   sp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
   sp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;
@@ -560,17 +620,22 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
   if (tile_end <= tile_begin) return NPA_OK;
   const uint64_t ntiles = tile_end - tile_begin;
   LaunchCfg lc;
-#define NPA_MLP(HGV)                                                                          \
+#define NPA_MLP(HGV, NTV)                                                                     \
   do {                                                                                        \
-    NPA_TRY(plan(mlp_step_kernel<HGV>, s, true, ntiles, &lc));                                \
-    mlp_step_kernel<HGV><<<lc.grid, kThreads, lc.smem, stream>>>(                             \
+    NPA_TRY(plan(mlp_step_kernel<HGV, NTV>, s, ntiles, &lc));                                 \
+    mlp_step_kernel<HGV, NTV><<<lc.grid, NTV, lc.smem, stream>>>(                             \
         s, g, sgrid, total, tile_begin, tile_end, tiles, m.w1t, m.b1, m.w2, m.b2, sp, e, mask, \
-        out.next_positions,                                                                   \
-        out.next_states, out.dx, out.ds, out.features);                                       \
+        out.next_positions, out.next_states, out.dx, out.ds, out.features);                   \
   } while (0)
-  if (s.Hp == 64) NPA_MLP(64 / kTH);
-  else if (s.Hp == 128) NPA_MLP(128 / kTH);
-  else NPA_MLP(256 / kTH);
+#define NPA_MLP_NT(NTV)                          \
+  do {                                           \
+    if (s.Hp == 64) NPA_MLP(64 / kTH, NTV);      \
+    else if (s.Hp == 128) NPA_MLP(128 / kTH, NTV); \
+    else NPA_MLP(256 / kTH, NTV);                \
+  } while (0)
+  if (s.NT == kThreadsWide) NPA_MLP_NT(kThreadsWide);
+  else NPA_MLP_NT(kThreadsNarrow);
+#undef NPA_MLP_NT
 #undef NPA_MLP
   return after_launch("mlp_step_kernel");
 }

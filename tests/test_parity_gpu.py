@@ -203,7 +203,9 @@ def make_model(w):
     return NpaModel(w.model, NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2, w.weights.b2))
 
 
-@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg3", 1, 4096)])
+# cfg2 x 8 (32,768 rows) runs the 384-thread MLP tiles, the others the 256-thread ones.
+@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg2", 8, 4096),
+                                          ("cfg3", 1, 4096)])
 def test_step_parity(oracle_mod, name, batch, n):
     w = workloads.make(name, batch=batch, n=n, steps=1)
     m = make_model(w)
@@ -217,14 +219,17 @@ def test_step_parity(oracle_mod, name, batch, n):
     np.testing.assert_allclose(gpu.next_positions, ref["next_positions"], rtol=RTOL, atol=ATOL)
 
 
-def test_step_bit_exact_without_log_norm(oracle_mod):
-    w = workloads.make("cfg0", steps=1)
+@pytest.mark.parametrize("batch", [1, 8])
+def test_step_bit_exact_without_log_norm(oracle_mod, batch):
+    w = workloads.make("cfg2", batch=batch, steps=1)
     w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
     m = make_model(w)
     rng = np.random.default_rng(0)
-    mask = (rng.uniform(size=w.n) < 0.7).astype(np.float32)
-    gpu = m.step(w.positions, w.states, 1, w.n, w.grid, w.dt, mask)
-    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, 1, w.n, w.dt, mask)
+    total = w.batch * w.n
+    mask = (rng.uniform(size=total) < 0.7).astype(np.float32)
+    gpu = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt, mask)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, w.dt,
+                          mask)
     for key in ("features", "ds", "dx", "next_states", "next_positions", "density"):
         np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
 
