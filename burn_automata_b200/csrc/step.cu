@@ -16,12 +16,12 @@
 //   layer 1: each thread owns an 8 rows x kTH hidden-unit register tile and
 //            walks k = 0..F-1 in order (features of the tile feature-major in
 //            shared memory, w1 transposed in shared memory);
-//   layer 2: NT / M threads per row, each owning ceil(O / (NT / M))
-//            outputs, sequential over h.
+//   layer 2: 2 NT / M threads per pair of rows, each owning
+//            ceil(O / (2 NT / M)) outputs of both rows, sequential over h.
 // The rollout's MLP stage consumes the feature tiles written by
 // perception_tiles_kernel ([tile][F][M], sorted order) through one shared
-// buffer: the next tile is fetched with cp.async once layer 1 has consumed
-// the current one, behind layer 2 and the epilogue (one buffer instead of two
+// buffer: the next tile is fetched with cp.async once layer 2 is done, behind
+// the epilogue and the wait at the top of the loop (one buffer instead of two
 // is what lets 12 warps per SM fit; measured 1.017 vs 1.067 ms at 8 warps
 // double-buffered on cfg2).  Each row finishes with forward_from_features_with_eps
 // (model.rs:867-898), the 3D position gates (model.rs:806-837) and euler_step
@@ -38,7 +38,7 @@ constexpr int kThreadsWide = 384;    // 12 warps per SM: 3 per scheduler
 constexpr int kThreadsNarrow = 256;  // when the wide tile does not fit in shared memory
 constexpr int kTH = 8;         // hidden units per thread in layer 1
 constexpr int kKC = 16;              // k slice when w1 is streamed
-constexpr int kMaxOut = 64;          // outputs per thread in layer 2 (passes of kL2Chunk)
+constexpr int kMaxOut = 64;          // outputs per row-owning thread (layer 2 runs in passes of kL2Chunk)
 constexpr size_t kSmemBudget = 220 * 1024;
 
 struct MlpShape {
@@ -156,7 +156,7 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
   const float* arow = ft + rg * 8;
   if (s.w1_resident) {
     const float* wcol = w1s + h0;
-#pragma unroll 2
+#pragma unroll 1
     for (int k = 0; k < s.F; ++k) {
       const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
       const float4 a1 = *reinterpret_cast<const float4*>(arow + k * M + 4);
@@ -199,72 +199,85 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
   }
 }
 
-// Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
-// tpr threads per row; thread j owns outputs o = j + tpr * u.  One call
-// handles u in [u0, u0 + NOUT) (outputs past O are computed on a valid row
-// and not stored).
+// Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h,
+// two rows per thread: 2 * tpr threads per row pair, thread j owning outputs
+// o = j + 2 tpr u (u in [u0, u0 + NOUT)) of both rows; each weight load
+// serves both rows.  Outputs past O are computed on a valid row, not stored.
 template <int NOUT>
-__device__ __forceinline__ void mlp_layer2(const MlpShape& s, const float* __restrict__ b2,
-                                           const float* hid, const float* w2s, float* outs,
-                                           int u0) {
+__device__ __forceinline__ void mlp_layer2_pair(const MlpShape& s, const float* __restrict__ b2,
+                                                const float* hid, const float* w2s, float* outs,
+                                                int u0) {
+  const int tpp = 2 * s.tpr;
   const int t = threadIdx.x;
-  const int r = t / s.tpr;
-  const int j = t - r * s.tpr;
-  float acc[NOUT];
+  const int rp = t / tpp;
+  const int j = t - rp * tpp;
+  float acc0[NOUT], acc1[NOUT];
   const float* wrow[NOUT];
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
-    const int o = j + s.tpr * (u0 + u);
-    const int oo = o < s.O ? o : j;
-    acc[u] = __ldg(b2 + oo);
+    const int o = j + tpp * (u0 + u);
+    const int oo = o < s.O ? o : 0;
+    acc0[u] = __ldg(b2 + oo);
+    acc1[u] = acc0[u];
     wrow[u] = w2s + oo * s.w2_stride;
   }
-  const float* hrow = hid + r * s.hid_stride;
+  const float* h0row = hid + (2 * rp) * s.hid_stride;
+  const float* h1row = h0row + s.hid_stride;
   const int H4 = s.H & ~3;
   for (int h = 0; h < H4; h += 4) {
-    const float4 hv = *reinterpret_cast<const float4*>(hrow + h);
-    float p[NOUT][4];
+    const float4 hv0 = *reinterpret_cast<const float4*>(h0row + h);
+    const float4 hv1 = *reinterpret_cast<const float4*>(h1row + h);
+    float p0[NOUT][4], p1[NOUT][4];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
       const float4 w = *reinterpret_cast<const float4*>(wrow[u] + h);
-      p[u][0] = w.x * hv.x;
-      p[u][1] = w.y * hv.y;
-      p[u][2] = w.z * hv.z;
-      p[u][3] = w.w * hv.w;
+      p0[u][0] = w.x * hv0.x;
+      p0[u][1] = w.y * hv0.y;
+      p0[u][2] = w.z * hv0.z;
+      p0[u][3] = w.w * hv0.w;
+      p1[u][0] = w.x * hv1.x;
+      p1[u][1] = w.y * hv1.y;
+      p1[u][2] = w.z * hv1.z;
+      p1[u][3] = w.w * hv1.w;
     }
-    // each output still adds its four products in h order; the outputs'
-    // chains are interleaved so consecutive adds are independent
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int u = 0; u < NOUT; ++u) acc[u] = acc[u] + p[u][k];
+      for (int u = 0; u < NOUT; ++u) {
+        acc0[u] = acc0[u] + p0[u][k];
+        acc1[u] = acc1[u] + p1[u][k];
+      }
   }
   for (int h = H4; h < s.H; ++h) {
-    const float hv = hrow[h];
+    const float hv0 = h0row[h], hv1 = h1row[h];
 #pragma unroll
-    for (int u = 0; u < NOUT; ++u) acc[u] = acc[u] + wrow[u][h] * hv;
+    for (int u = 0; u < NOUT; ++u) {
+      acc0[u] = acc0[u] + wrow[u][h] * hv0;
+      acc1[u] = acc1[u] + wrow[u][h] * hv1;
+    }
   }
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
-    const int o = j + s.tpr * (u0 + u);
-    if (o < s.O) outs[r * s.out_stride + o] = acc[u];
+    const int o = j + tpp * (u0 + u);
+    if (o < s.O) {
+      outs[(2 * rp) * s.out_stride + o] = acc0[u];
+      outs[(2 * rp + 1) * s.out_stride + o] = acc1[u];
+    }
   }
 }
 
-// Layer 2 over all of a thread's outputs, at most kL2Chunk per pass over the
-// hidden row (bounds the registers of the accumulators).
-constexpr int kL2Chunk = 16;
+// Outputs per thread per pass over the hidden rows (bounds the accumulators' registers).
+constexpr int kL2Chunk = 8;
 __device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
                                                const float* hid, const float* w2s, float* outs) {
-  const int per_thread = (s.O + s.tpr - 1) / s.tpr;
+  const int per_thread = (s.O + 2 * s.tpr - 1) / (2 * s.tpr);
   for (int u0 = 0; u0 < per_thread; u0 += kL2Chunk) {
     switch (min(kL2Chunk, per_thread - u0)) {
 #define NPA_L2(N) \
   case N:         \
-    mlp_layer2<N>(s, b2, hid, w2s, outs, u0); \
+    mlp_layer2_pair<N>(s, b2, hid, w2s, outs, u0); \
     break;
       NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
-      NPA_L2(9) NPA_L2(10) NPA_L2(11) NPA_L2(12) NPA_L2(13) NPA_L2(14) NPA_L2(15) NPA_L2(16)
 #undef NPA_L2
       default:
         break;
@@ -421,8 +434,6 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
     if (features_out && live)
       for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
     __syncthreads();
-    const uint32_t next = tile + gridDim.x;
-    if (next < tiles) issue(next);
     // own state for the Euler update, hidden behind layer 2
     float sv[kStateRegs];
 #pragma unroll
@@ -437,6 +448,8 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
     }
     mlp_layer2_any(s, b2, hid, w2s, outs);
     __syncthreads();
+    const uint32_t next = tile + gridDim.x;
+    if (next < tiles) issue(next);
     // forward_from_features_with_eps + gates + euler_step, TPR threads per row
     if (live) {
       const float* u = outs + r * s.out_stride;
