@@ -99,6 +99,7 @@ GridParams make_grid_params(const npa_grid_config& cfg) {
     if (a < cfg.dim) cells *= static_cast<uint64_t>(cfg.grid_size[a]);
   }
   g.cells = static_cast<uint32_t>(cells);
+  g.cells_mask = (g.cells & (g.cells - 1)) == 0 ? g.cells - 1 : 0u;
   g.eps = cfg.eps;
   g.eps2 = cfg.eps * cfg.eps;
   for (int a = 0; a < 3; ++a) {

@@ -24,6 +24,7 @@ struct GridParams {
   int mode;
   int grid_size[3];
   uint32_t cells;      // HashGridConfig::cell_count (config.rs:86-88)
+  uint32_t cells_mask; // cells - 1 when cells is a power of two (always in Particle mode), else 0
   float eps;
   float eps2;          // eps * eps (neighbor.rs:25)
   float extent[3];     // grid_size[axis] as f32 * eps (hashgrid.rs:170 / :80)
@@ -62,7 +63,9 @@ __device__ __forceinline__ uint32_t mix_coord(int value_low32, uint32_t salt) {
 __device__ __forceinline__ uint32_t particle_cell_hash(const GridParams& g, int cx, int cy, int cz) {
   uint32_t h = mix_coord(cx, 0x9e3779b9u) ^ mix_coord(cy, 0x85ebca6bu);
   if (g.dim == 3) h ^= mix_coord(cz, 0xc2b2ae35u);
-  return h % g.cells;
+  // h % cells; for a power-of-two cell count (Particle mode validates one)
+  // the mask gives the same value without an integer division.
+  return g.cells_mask ? (h & g.cells_mask) : (h % g.cells);
 }
 
 // Grid-mode axis cell (hashgrid.rs:80-90 / :106-116).
