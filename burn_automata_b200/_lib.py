@@ -111,6 +111,9 @@ SIGNATURES = [
     ("npa_executor_set_state_device", c_i32, [vp, vp, vp, vp]),
     ("npa_executor_step_many", c_i32, [vp, c_i64, c_f32, c_i32, vp]),
     ("npa_executor_step_many_profiled", c_i32, [vp, c_i64, c_f32, c_i32, vp, f32p, f32p]),
+    ("npa_executor_set_update_prob", c_i32, [vp, c_f32, c_u64, P(c_u64)]),
+    ("npa_executor_set_step_index", c_i32, [vp, ctypes.c_uint32]),
+    ("npa_executor_step_index", c_i32, [vp, P(ctypes.c_uint32)]),
     ("npa_executor_read_state", c_i32, [vp, f32p, f32p]),
     ("npa_executor_state_device", c_i32, [vp, P(vp), P(vp)]),
     ("npa_executor_launches_per_step", c_i32, [vp, P(c_i64)]),

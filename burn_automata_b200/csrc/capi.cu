@@ -1095,7 +1095,8 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   out.dx = reinterpret_cast<float4*>(d_dx);
   out.ds = d_ds;
   out.features = d_features;
-  return launch_mlp_step(m->dm, g, sv, B, w.tiles, d_states, dt, d_update_mask, out, st);
+  return launch_mlp_step(m->dm, g, sv, B, w.tiles, d_states, dt, d_update_mask, StochasticMask{},
+                         out, st);
 }
 
 }  // extern "C"
@@ -1126,6 +1127,13 @@ struct npa_executor {
   cudaStream_t graph_stream = nullptr;
   int64_t launches[kPhases] = {0, 0, 0, 0};
   int tile_rows = 0;
+  // Stochastic update mask (create_state_with_update_prob): active when
+  // update_prob < 1; step_index mirrors the device counter d_step.
+  int stochastic = 0;
+  float update_prob = 1.0f;
+  uint32_t* d_lane_seeds = nullptr;  // [batch]
+  uint32_t* d_step = nullptr;
+  uint32_t step_index = 0;
 };
 
 namespace {
@@ -1149,8 +1157,16 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
       out.dx = nullptr;
       out.ds = nullptr;
       out.features = nullptr;
-      return launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr, out,
-                             s);
+      StochasticMask sm;
+      if (e->stochastic) {
+        sm.update_prob = e->update_prob;
+        sm.lane_seeds = e->d_lane_seeds;
+        sm.step_counter = e->d_step;
+      }
+      NPA_TRY(launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr, sm,
+                              out, s));
+      if (e->stochastic) NPA_TRY(launch_advance_step(e->d_step, s));
+      return NPA_OK;
     }
   }
 }
@@ -1235,6 +1251,10 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
     if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->st[i]), total * C * 4);
   }
   if (st == NPA_OK) st = alloc(&e->ws, e->ws_bytes);
+  if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->d_lane_seeds), size_t(batch) * 4);
+  if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->d_step), 4);
+  if (st == NPA_OK && cudaMemset(e->d_step, 0, 4) != cudaSuccess)
+    st = fail(NPA_ERR_CUDA, "cudaMemset step counter");
   if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w, tf))
     st = fail(NPA_ERR_INVALID_ARGUMENT, "executor workspace layout");
   if (st != NPA_OK) {
@@ -1256,6 +1276,8 @@ void npa_executor_destroy(npa_executor* e) {
     cudaFree(e->st[i]);
   }
   cudaFree(e->ws);
+  cudaFree(e->d_lane_seeds);
+  cudaFree(e->d_step);
   cudaSetDevice(prev);
   delete e;
 }
@@ -1291,6 +1313,9 @@ static npa_status exec_prepare(npa_executor* e, int64_t steps, float dt, int32_t
   if (use_graph && s == nullptr) return fail(NPA_ERR_INVALID_ARGUMENT, "graph replay needs a non-default stream");
   if (use_graph && (!e->graph[0][0] || e->graph_dt != dt || e->graph_stream != s))
     NPA_TRY(exec_capture(e, dt, s));
+  if (e->stochastic && steps > 0)  // the device counter starts from the host's step index
+    NPA_CUDA(cudaMemcpyAsync(e->d_step, &e->step_index, 4, cudaMemcpyHostToDevice, s),
+             "upload step index");
   return NPA_OK;
 }
 
@@ -1301,7 +1326,49 @@ npa_status npa_executor_step_many(npa_executor* e, int64_t steps, float dt, int3
   for (int64_t k = 0; k < steps; ++k) {
     for (int phase = 0; phase < kPhases; ++phase) NPA_TRY(exec_run_phase(e, phase, dt, use_graph, s));
     e->cur = 1 - e->cur;
+    e->step_index += 1u;
   }
+  return NPA_OK;
+}
+
+npa_status npa_executor_set_update_prob(npa_executor* e, float update_prob, uint64_t seed,
+                                        const uint64_t* lane_seeds) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  NPA_TRY(ensure_device(e->model->dm.device));
+  // gpu_random_seed (gpu/helpers/params.rs:186-188) and gpu_lane_seeds
+  // (gpu/executor/state.rs:1282-1312): lane l of a shared seed draws with
+  // seed ^ (l * particle_count); independent lanes fold their own seeds.
+  auto fold = [](uint64_t v) { return uint32_t(v) ^ uint32_t(v >> 32); };
+  std::vector<uint32_t> seeds(size_t(e->batch));
+  for (int64_t lane = 0; lane < e->batch; ++lane) {
+    if (lane_seeds) {
+      seeds[size_t(lane)] = fold(lane_seeds[lane]);
+    } else {
+      const uint64_t offset = uint64_t(lane) * uint64_t(e->n);
+      if (offset > 0xffffffffull) return fail(NPA_ERR_INVALID_ARGUMENT, "lane particle offset overflow");
+      seeds[size_t(lane)] = fold(seed) ^ uint32_t(offset);
+    }
+  }
+  if (!seeds.empty())
+    NPA_CUDA(cudaMemcpy(e->d_lane_seeds, seeds.data(), seeds.size() * 4, cudaMemcpyHostToDevice),
+             "upload lane seeds");
+  const int stochastic = update_prob >= 1.0f ? 0 : 1;
+  if (stochastic != e->stochastic) exec_drop_graphs(e);  // the MLP phase changes shape
+  e->stochastic = stochastic;
+  e->update_prob = update_prob;
+  if (stochastic) exec_drop_graphs(e);  // update_prob is a kernel argument
+  return NPA_OK;
+}
+
+npa_status npa_executor_set_step_index(npa_executor* e, uint32_t step_index) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  e->step_index = step_index;
+  return NPA_OK;
+}
+
+npa_status npa_executor_step_index(npa_executor* e, uint32_t* step_index) {
+  if (!e || !step_index) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *step_index = e->step_index;
   return NPA_OK;
 }
 
@@ -1323,6 +1390,7 @@ npa_status npa_executor_step_many_profiled(npa_executor* e, int64_t steps, float
         cudaEventRecord(ev[size_t(k) * (kPhases + 1) + phase + 1], s);
       }
       e->cur = 1 - e->cur;
+      e->step_index += 1u;
     }
     if (st == NPA_OK && cudaStreamSynchronize(s) != cudaSuccess) st = fail(NPA_ERR_CUDA, "sync");
     if (st == NPA_OK) {

@@ -256,6 +256,32 @@ __device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
   return v;
 }
 
+// The GPU executor's counter-based stochastic update mask
+// (crates/burn_automata/src/gpu_step.wgsl:1019-1056; host twin
+// crates/burn_automata/tests/gpu_wgpu/common.rs:115-137): a particle updates
+// in a step when random01(local index, step index, lane seed) < update_prob.
+__host__ __device__ inline uint32_t mask_hash_u32(uint32_t x) {
+  x = (x ^ 61u) ^ (x >> 16);
+  x = x + (x << 3);
+  x = x ^ (x >> 4);
+  x = x * 0x27d4eb2du;
+  x = x ^ (x >> 15);
+  return x;
+}
+
+__host__ __device__ inline float mask_random01(uint32_t particle, uint32_t step, uint32_t seed) {
+  const uint32_t mixed = mask_hash_u32(particle ^ mask_hash_u32(step + 0x9e3779b9u) ^ seed);
+  return static_cast<float>(mixed >> 8) * (1.0f / 16777216.0f);
+}
+
+// update_mask without the reference's material / coarse-material extensions.
+__host__ __device__ inline float stochastic_update_mask(float prob, uint32_t particle,
+                                                        uint32_t step, uint32_t seed) {
+  if (prob >= 1.0f) return 1.0f;
+  if (prob <= 0.0f) return 0.0f;
+  return mask_random01(particle, step, seed) < prob ? 1.0f : 0.0f;
+}
+
 // Sorted-slot view of the hashgrid used by every neighbour walk.
 struct SortedGrid {
   const uint32_t* bin_offsets;  // [B*cells + 1], global sorted slots

@@ -129,11 +129,19 @@ int hidden_padded_for(int hidden);
 // (depends on the padded hidden width, the feature width and the row count).
 int step_tile_rows(const DeviceModel& m, uint64_t rows);
 bool mlp_step_supported(const DeviceModel& m);
+// The GPU executor's stochastic update mask (inactive when lane_seeds is null).
+struct StochasticMask {
+  float update_prob = 1.0f;
+  const uint32_t* lane_seeds = nullptr;    // [B] device
+  const uint32_t* step_counter = nullptr;  // device step index
+};
+// step_counter[0] += 1 (after a step that used the stochastic mask).
+npa_status launch_advance_step(uint32_t* counter, cudaStream_t stream);
 // MLP + dx/ds (+3D gates) + Euler over feature tiles in sorted order.
 // Tiles [tile_begin, tile_end) of the step (default: all).
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& s,
                            uint32_t batch, const float* tiles, const float* states, float dt,
-                           const float* mask,
+                           const float* mask, const StochasticMask& sm,
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 

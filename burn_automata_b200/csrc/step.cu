@@ -372,6 +372,12 @@ struct StepParams {
   int C;
   int D;
   const float* states;  // the step's input states [B*N][C] (caller order)
+  // Stochastic update mask of the GPU executor (when lane_seeds is set):
+  // mask = stochastic_update_mask(update_prob, local index, *step_counter,
+  // lane_seeds[batch]).
+  float update_prob;
+  const uint32_t* lane_seeds;    // [B] or null
+  const uint32_t* step_counter;  // device step index (read once per launch)
 };
 
 // Own-state channels a thread keeps in registers between layer 1 and the
@@ -414,6 +420,7 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   load_bias1<HG>(s, b1, bias1);
   const int r = threadIdx.x / TPR;
   const int part = threadIdx.x - r * TPR;
+  const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
   for (; tile < tiles; tile += gridDim.x) {
     cp_async_wait<0>();
     __syncthreads();
@@ -426,9 +433,13 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
     float m = 1.0f;
     if (live) {
       const uint32_t batch = q / sg.n;
-      row = size_t(batch) * sg.n + __ldg(sg.permutation + q);
+      const uint32_t local = __ldg(sg.permutation + q);
+      row = size_t(batch) * sg.n + local;
       pi = __ldg(sg.positions + row);
-      if (mask) m = __ldg(mask + row);
+      if (sp.lane_seeds)
+        m = stochastic_update_mask(sp.update_prob, local, step_index, __ldg(sp.lane_seeds + batch));
+      else if (mask)
+        m = __ldg(mask + row);
     }
     mlp_layer1<HG, NT>(s, w1t, bias1, ft, w1s, hid);
     if (features_out && live)
@@ -598,6 +609,13 @@ npa_status launch_forward_update(const DeviceModel& m, const float* features, ui
   return after_launch("forward_update_kernel");
 }
 
+__global__ void advance_step_kernel(uint32_t* counter) { counter[0] += 1u; }
+
+npa_status launch_advance_step(uint32_t* counter, cudaStream_t stream) {
+  advance_step_kernel<<<1, 1, 0, stream>>>(counter);
+  return after_launch("advance_step_kernel");
+}
+
 npa_status launch_euler(const GridParams& g, const float4* positions, const float* states,
                         const float4* dx, const float* ds, uint32_t total, int state_dims,
                         float dt, const float* mask, float4* next_positions, float* next_states,
@@ -612,7 +630,7 @@ npa_status launch_euler(const GridParams& g, const float4* positions, const floa
 
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
                            uint32_t batch, const float* tiles, const float* states, float dt,
-                           const float* mask,
+                           const float* mask, const StochasticMask& sm,
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin,
                            uint32_t tile_end) {
   const uint32_t total = batch * sgrid.n;
@@ -622,6 +640,9 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
   const MlpShape s = make_shape(m, total);
   StepParams sp;
   sp.states = states;
+  sp.update_prob = sm.update_prob;
+  sp.lane_seeds = sm.lane_seeds;
+  sp.step_counter = sm.step_counter;
   sp.alpha = m.alpha;
   sp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
   sp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;

@@ -228,11 +228,44 @@ class CudaAutomataExecutor:
         except Exception:
             pass
 
-    def create_state(self, positions, states) -> None:
+    def create_state(self, positions, states, update_prob: float = 1.0, seed: int = 0,
+                     lane_seeds=None) -> None:
+        """create_state / create_state_with_update_prob (gpu/executor/state.rs:6-55):
+        uploads the particles and restarts the step index at 0.  update_prob < 1
+        applies the executor's counter-based stochastic update mask (see
+        set_update_prob)."""
         pos = _f32(positions).reshape(-1, 4)
         st = _f32(states).reshape(-1)
         _lib.check(_lib.lib().npa_executor_upload_state(self._handle, _fp(pos), _fp(st)),
                    "create_state")
+        self.set_step_index(0)
+        self.set_update_prob(update_prob, seed, lane_seeds)
+
+    def set_update_prob(self, update_prob: float, seed: int = 0, lane_seeds=None) -> None:
+        """Stochastic update mask of later steps: particle i of lane l updates
+        when random01(i, step_index, lane seed) < update_prob; lane seeds are
+        fold(seed) ^ (l * particle_count), or fold(lane_seeds[l]) when given."""
+        ls = None
+        if lane_seeds is not None:
+            arr = np.ascontiguousarray(np.asarray(lane_seeds, dtype=np.uint64))
+            if arr.size != self.batch_size:
+                raise InvalidArgument(f"lane seed count {arr.size} does not match batch size "
+                                      f"{self.batch_size}")
+            ls = arr.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
+        _lib.check(_lib.lib().npa_executor_set_update_prob(
+            self._handle, float(update_prob), int(seed) & 0xFFFFFFFFFFFFFFFF, ls),
+            "set_update_prob")
+
+    @property
+    def step_index(self) -> int:
+        v = ctypes.c_uint32(0)
+        _lib.check(_lib.lib().npa_executor_step_index(self._handle, ctypes.byref(v)), "step_index")
+        return v.value
+
+    def set_step_index(self, step_index: int) -> None:
+        _lib.check(_lib.lib().npa_executor_set_step_index(self._handle,
+                                                          int(step_index) & 0xFFFFFFFF),
+                   "set_step_index")
 
     def set_state_device(self, d_positions, d_states, stream=None) -> None:
         _lib.check(_lib.lib().npa_executor_set_state_device(

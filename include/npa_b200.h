@@ -350,6 +350,24 @@ npa_status npa_executor_step_many(npa_executor* exec, int64_t steps, float dt, i
 npa_status npa_executor_step_many_profiled(npa_executor* exec, int64_t steps, float dt,
                                            int32_t use_graph, void* stream, float* phase_ms,
                                            float* total_ms);
+/* Stochastic update mask of the resident executor
+ * (create_state_with_update_prob, crates/burn_automata/src/gpu/executor/state.rs:29-55,
+ * the mask itself crates/burn_automata/src/gpu_step.wgsl:1019-1056).  With
+ * update_prob < 1 every later step updates particle i of lane l only when
+ * random01(i, step_index, lane_seed[l]) < update_prob (a counter hash of the
+ * particle, the step index and the lane seed; update_prob <= 0 freezes all).
+ * The 64-bit seed folds to 32 bits as (seed ^ seed >> 32); lane l's seed is
+ * that ^ (l * n) (gpu/executor/state.rs:1282-1312), or, when lane_seeds is
+ * given (batch entries), the fold of lane_seeds[l].  update_prob >= 1 turns
+ * the mask off.  The material / coarse-material extensions of the reference
+ * mask are not part of this path. */
+npa_status npa_executor_set_update_prob(npa_executor* exec, float update_prob, uint64_t seed,
+                                        const uint64_t* lane_seeds);
+/* The step index the next step's mask uses (0 after create); each step
+ * advances it by one, with or without the mask, as the reference's
+ * WgpuAutomataState::step_index. */
+npa_status npa_executor_set_step_index(npa_executor* exec, uint32_t step_index);
+npa_status npa_executor_step_index(npa_executor* exec, uint32_t* step_index);
 /* read_state (executor/readback.rs:85): synchronises and copies to host. */
 npa_status npa_executor_read_state(npa_executor* exec, float* positions, float* states);
 /* Current resident device buffers ([f32;4] positions, states). */

@@ -150,6 +150,8 @@ def lib():
         L.ora_gaussian_record_floats.argtypes = [P(_Decode)]
         L.ora_gaussian_record_floats.restype = i64
         L.ora_decode_gaussians.argtypes = [P(_Decode), f32p, f32p, i64, i64, f32p]
+        L.ora_gpu_update_mask.argtypes = [i64, i64, ctypes.c_float, ctypes.c_uint32,
+                                          P(ctypes.c_uint32), f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
@@ -337,6 +339,28 @@ def rollout(model_cfg, weights, grid, positions, states, batch, n, steps, dt, ma
                              ctypes.byref(g), _ptr(pos), _ptr(st), batch, n, steps, float(dt),
                              _ptr(mk), _ptr(mean_dx)), "rollout")
     return pos, st, mean_dx
+
+
+def gpu_lane_seeds(batch: int, n: int, seed: int, lane_seeds=None) -> np.ndarray:
+    """gpu_random_seed / gpu_lane_seeds (gpu/helpers/params.rs:186-188,
+    gpu/executor/state.rs:1282-1312)."""
+    fold = lambda v: (int(v) & 0xFFFFFFFF) ^ ((int(v) >> 32) & 0xFFFFFFFF)
+    if lane_seeds is not None:
+        return np.array([fold(v) for v in lane_seeds], np.uint32)
+    return np.array([fold(seed) ^ ((lane * n) & 0xFFFFFFFF) for lane in range(batch)], np.uint32)
+
+
+def gpu_update_masks(batch: int, n: int, update_prob: float, steps: int, seed: int = 0,
+                     first_step: int = 0, lane_seeds=None) -> np.ndarray:
+    """The executor's masks for `steps` consecutive steps: [steps, batch * n]."""
+    seeds = gpu_lane_seeds(batch, n, seed, lane_seeds)
+    out = np.zeros((steps, batch * n), np.float32)
+    for k in range(steps):
+        _check(lib().ora_gpu_update_mask(batch, n, float(update_prob),
+                                         (first_step + k) & 0xFFFFFFFF,
+                                         seeds.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+                                         _ptr(out[k])), "gpu_update_mask")
+    return out
 
 
 def decode_gaussians(positions, states, c: int, cfg):

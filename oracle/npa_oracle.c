@@ -903,3 +903,38 @@ int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
   }
   return ORA_OK;
 }
+
+/* ---- GPU executor stochastic update mask ----
+ * Host twin of the reference's WGSL update_mask (crates/burn_automata/src/
+ * gpu_step.wgsl:1019-1056) as restated by its test helper gpu_update_mask /
+ * gpu_random01 / hash_u32 (crates/burn_automata/tests/gpu_wgpu/common.rs:
+ * 115-137), extended to batches with the executor's lane seeds
+ * (crates/burn_automata/src/gpu/executor/state.rs:1282-1312). */
+static uint32_t ora_mask_hash(uint32_t value) {
+  uint32_t x = value;
+  x = (x ^ 61u) ^ (x >> 16);
+  x = x + (x << 3);
+  x ^= x >> 4;
+  x = x * 0x27d4eb2du;
+  return x ^ (x >> 15);
+}
+
+static float ora_mask_random01(uint32_t particle, uint32_t step, uint32_t seed) {
+  uint32_t mixed = ora_mask_hash(particle ^ ora_mask_hash(step + 0x9e3779b9u) ^ seed);
+  return (float)(mixed >> 8) * (1.0f / 16777216.0f);
+}
+
+int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t step,
+                        const uint32_t* lane_seeds, float* out) {
+  if (batch < 0 || n < 0) return ORA_ERR_INVALID_ARGUMENT;
+  for (int64_t lane = 0; lane < batch; ++lane) {
+    for (int64_t i = 0; i < n; ++i) {
+      float m;
+      if (update_prob >= 1.0f) m = 1.0f;
+      else if (update_prob <= 0.0f) m = 0.0f;
+      else m = ora_mask_random01((uint32_t)i, step, lane_seeds[lane]) < update_prob ? 1.0f : 0.0f;
+      out[lane * n + i] = m;
+    }
+  }
+  return ORA_OK;
+}

@@ -158,6 +158,10 @@ int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
                          float* out);
 
 /* Threads used by the OpenMP loops (0 = OpenMP default). */
+/* The GPU executor's stochastic update mask for one step: out[lane * n + i]
+ * (gpu_step.wgsl:1019-1056; tests/gpu_wgpu/common.rs:115-137). */
+int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t step,
+                        const uint32_t* lane_seeds, float* out);
 void ora_set_threads(int threads);
 int ora_get_threads(void);
 
