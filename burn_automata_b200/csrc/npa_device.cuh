@@ -396,6 +396,131 @@ __device__ __forceinline__ void for_each_neighbor(const GridParams& g, const Sor
   }
 }
 
+// Per-warp staging of the cooperative walk: one 32-candidate window.
+struct WarpWindow {
+  float4 rec[32];     // candidate position; w = 1 when its cell is the visited cell
+  uint32_t slot[32];  // candidate sorted slot
+  float vol[32];      // payload of the perception walk
+  uint32_t row[32];
+};
+
+// Lanes of this (converged, fully populated) warp with the same batch and
+// cell as this lane; their neighbour candidate sequences are identical.
+__device__ __forceinline__ uint32_t warp_cell_peers(uint32_t batch, int3 c) {
+  return __match_any_sync(0xffffffffu, c.x) & __match_any_sync(0xffffffffu, c.y) &
+         __match_any_sync(0xffffffffu, c.z) & __match_any_sync(0xffffffffu, batch);
+}
+
+// Number of distinct (batch, cell) groups among the warp's lanes.
+__device__ __forceinline__ int warp_cell_groups(uint32_t peers) {
+  const uint32_t lane = threadIdx.x & 31u;
+  return __popc(__ballot_sync(0xffffffffu, lane == static_cast<uint32_t>(__ffs(peers) - 1)));
+}
+
+// for_each_neighbor, done by a whole warp for the lanes `peers` of one
+// (batch, cell) group (the calling lanes' own group when mine is set): the
+// candidate sequence of that cell is the same for every member, so lane L
+// fetches candidate v0 + L of each 32-candidate window (record, exact-cell
+// test, and stage(L, q) for a caller payload) into shared memory, and each
+// member then tests the window's candidates in order from there.  The per-lane
+// bin bookkeeping and record loads of for_each_neighbor are done once per
+// candidate per warp instead of once per lane.  Same visits in the same
+// order; visit(j, q, delta, r2) also receives the window index j.
+template <int DIM, class Stage, class Visit>
+__device__ __forceinline__ void walk_cell_warp(const GridParams& g, const SortedGrid& s,
+                                               uint32_t batch, int3 center, bool mine, float4 pi,
+                                               WarpWindow& win, Stage& stage, Visit& visit) {
+  constexpr int NB = DIM == 3 ? 27 : 9;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t bin_base = batch * g.cells;
+  uint32_t beg[NB], cum[NB];
+  uint32_t ncand = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int3 nc = add_wrapping(center, bin_delta<DIM>(b));
+    const long long cell = cell_index(g, nc.x, nc.y, nc.z);
+    uint32_t lo = 0, cnt = 0;
+    if (cell >= 0) {
+      const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
+      lo = __ldg(s.bin_offsets + bin);
+      const uint32_t hi = min(__ldg(s.bin_offsets + bin + 1), s.total);
+      cnt = hi > lo ? hi - lo : 0u;
+    }
+    beg[b] = lo;
+    ncand += cnt;
+    cum[b] = ncand;
+  }
+  int b = 0;
+  uint32_t cur_beg = beg[0], cur_lo = 0, cur_hi = cum[0];
+  for (uint32_t v0 = 0; v0 < ncand; v0 += 32) {
+    const uint32_t v = v0 + lane;
+    if (v < ncand) {
+      while (v >= cur_hi) {  // advance to the bin holding candidate v
+        ++b;
+        cur_lo = cur_hi;
+#pragma unroll
+        for (int k = 1; k < NB; ++k)
+          if (k == b) {
+            cur_beg = beg[k];
+            cur_hi = cum[k];
+          }
+      }
+      const uint32_t q = cur_beg + (v - cur_lo);
+      float4 pj;
+      int3 cj;
+      load_record<DIM>(s, q, pj, cj);
+      bool match = true;
+      if (g.mode == kModeParticle) {
+        const int3 want = add_wrapping(center, bin_delta<DIM>(b));
+        match = cj.x == want.x && cj.y == want.y && cj.z == want.z;
+      }
+      pj.w = match ? 1.0f : 0.0f;
+      win.rec[lane] = pj;
+      win.slot[lane] = q;
+      if (match) stage(lane, q);
+    }
+    __syncwarp();
+    if (mine) {
+      const uint32_t nv = min(32u, ncand - v0);
+      for (uint32_t j = 0; j < nv; ++j) {
+        const float4 pj = win.rec[j];
+        if (pj.w == 0.0f) continue;
+        const float4 d = neighbor_delta(g, pi, pj);
+        float r2 = d.x * d.x;
+        r2 = r2 + d.y * d.y;
+        if (DIM == 3) r2 = r2 + d.z * d.z;
+        if (r2 < g.eps2) visit(j, win.slot[j], d, r2);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Every (batch, cell) group of the warp in turn (peers from warp_cell_peers):
+// each lane visits exactly its own cell's neighbours, in walk order.
+template <int DIM, class Stage, class Visit>
+__device__ __forceinline__ void for_each_neighbor_warp(const GridParams& g, const SortedGrid& s,
+                                                       uint32_t batch, float4 pi, int3 center,
+                                                       uint32_t peers, WarpWindow& win,
+                                                       Stage&& stage, Visit&& visit) {
+  const uint32_t lane = threadIdx.x & 31u;
+  uint32_t pending = 0xffffffffu;
+  while (pending) {
+    const int leader = __ffs(pending) - 1;
+    const uint32_t members = __shfl_sync(0xffffffffu, peers, leader);
+    pending &= ~members;
+    const uint32_t gb = __shfl_sync(0xffffffffu, batch, leader);
+    const int3 gc = make_int3(__shfl_sync(0xffffffffu, center.x, leader),
+                              __shfl_sync(0xffffffffu, center.y, leader),
+                              __shfl_sync(0xffffffffu, center.z, leader));
+    walk_cell_warp<DIM>(g, s, gb, gc, ((members >> lane) & 1u) != 0, pi, win, stage, visit);
+  }
+}
+
+// At most this many cell groups per warp take the cooperative walk (each
+// group costs the warp one full walk); more diverse warps walk per lane.
+constexpr int kMaxWarpCellGroups = 4;
+
 // Neighbour lists recorded by the density pass: the sorted slots of a
 // particle's hits in walk order, at most `cap` per particle; a particle with
 // more hits stores count = cap + 1 and is walked again from the hashgrid.

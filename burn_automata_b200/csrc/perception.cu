@@ -22,11 +22,14 @@ namespace {
 // registers (cfg2 perception 0.446 vs 0.538 ms; 5 blocks 0.485, 8 blocks 0.512).
 constexpr int kPerceptionBlocksPerSm = 6;
 
-template <int DIM>
+template <int DIM, bool COOP>
 __global__ void __launch_bounds__(256)
 density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ volume,
                float* __restrict__ density_out, HitLists hl) {
+  __shared__ WarpWindow windows[COOP ? 256 / 32 : 1];
   const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  // Whole warp in range (warp-uniform), so warp collectives below are safe.
+  const bool full_warp = (q | 31u) < total;
   if (q >= total) return;
   const uint32_t batch = q / s.n;
   float4 pi;
@@ -35,11 +38,21 @@ density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ v
   float rho = 0.0f;
   uint32_t hits = 0;
   uint32_t* list = hl.slots ? hl.slots + q : nullptr;
-  for_each_neighbor<DIM, 4>(g, s, batch, pi, c, [&](uint32_t qj, float4, float r2) {
+  auto visit = [&](uint32_t qj, float r2) {
     rho = rho + poly6(g, r2);
     if (list && hits < uint32_t(hl.cap)) list[size_t(hits) * hl.stride] = qj;
     ++hits;
-  });
+  };
+  uint32_t peers = 0;
+  if (COOP && full_warp) peers = warp_cell_peers(batch, c);
+  if (COOP && full_warp && warp_cell_groups(peers) <= kMaxWarpCellGroups) {
+    for_each_neighbor_warp<DIM>(g, s, batch, pi, c, peers, windows[threadIdx.x >> 5],
+                                [](uint32_t, uint32_t) {},
+                                [&](uint32_t, uint32_t qj, float4, float r2) { visit(qj, r2); });
+  } else {
+    for_each_neighbor<DIM, 4>(g, s, batch, pi, c,
+                              [&](uint32_t qj, float4, float r2) { visit(qj, r2); });
+  }
   if (list) hl.count[q] = min(hits, uint32_t(hl.cap + 1));
   volume[q] = recip_finite(rho);
   if (density_out) density_out[size_t(batch) * s.n + s.permutation[q]] = rho;
@@ -52,14 +65,16 @@ __device__ __forceinline__ void load_own(const float* __restrict__ states, size_
   for (int c = 0; c < CH; ++c) si[c] = (c0 + c < C) ? __ldg(states + row * C + c0 + c) : 0.0f;
 }
 
-template <int DIM, int CH>
+template <int DIM, int CH, bool COOP>
 __global__ void __launch_bounds__(128, kPerceptionBlocksPerSm)
 perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, uint32_t total,
                   const float* __restrict__ states, int C, int chunks,
                   const float* __restrict__ volume, float* __restrict__ features,
                   float* __restrict__ blurred, float* __restrict__ state_gradient,
                   float* __restrict__ density_gradient) {
+  __shared__ WarpWindow windows[COOP ? 128 / 32 : 1];
   const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool full_warp = (t | 31u) < uint64_t(total) * chunks;  // warp-uniform
   if (t >= uint64_t(total) * chunks) return;
   const uint32_t q = static_cast<uint32_t>(t / chunks);
   const int chunk = static_cast<int>(t - uint64_t(q) * chunks);
@@ -68,10 +83,17 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
   const size_t row = size_t(batch) * s.n + s.permutation[q];
   const float4 pi = __ldg(s.positions + row);
   const int3 c = slot_cell<DIM>(s, q);
+  WarpWindow* win = nullptr;
+  uint32_t peers = 0;
+  if (COOP && full_warp) {
+    peers = warp_cell_peers(batch, c);
+    if (warp_cell_groups(peers) <= kMaxWarpCellGroups) win = &windows[threadIdx.x >> 5];
+  }
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a);
+  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
+                          peers);
   const size_t F = p.feature_dims;
   float* f = features + row * F;
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi, [&](int k, float v) { f[k] = v; });
@@ -90,14 +112,18 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
     for (int d = 0; d < DIM; ++d) density_gradient[row * DIM + d] = a.dgrad[d];
 }
 
-template <int DIM, int CH>
+template <int DIM, int CH, bool COOP>
 __global__ void __launch_bounds__(128, kPerceptionBlocksPerSm)
 perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl,
                         uint32_t total, uint32_t q_begin, uint32_t q_end,
                         const float* __restrict__ states, int C, int chunks,
                         const float* __restrict__ volume, int tile_rows,
                         float* __restrict__ tiles) {
+  __shared__ WarpWindow windows[COOP ? 128 / 32 : 1];
   const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  // warp-uniform: every lane in range and on a real particle
+  const bool full_warp = (t | 31u) < uint64_t(q_end - q_begin) * chunks &&
+                         q_begin + static_cast<uint32_t>((t | 31u) / chunks) < total;
   if (t >= uint64_t(q_end - q_begin) * chunks) return;
   const uint32_t q = q_begin + static_cast<uint32_t>(t / chunks);
   const int chunk = static_cast<int>(t - uint64_t(q - q_begin) * chunks);
@@ -112,10 +138,17 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists
   const size_t row = size_t(batch) * s.n + s.permutation[q];
   const float4 pi = __ldg(s.positions + row);
   const int3 c = slot_cell<DIM>(s, q);
+  WarpWindow* win = nullptr;
+  uint32_t peers = 0;
+  if (COOP && full_warp) {
+    peers = warp_cell_peers(batch, c);
+    if (warp_cell_groups(peers) <= kMaxWarpCellGroups) win = &windows[threadIdx.x >> 5];
+  }
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a);
+  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
+                          peers);
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
                          [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
 }
@@ -134,6 +167,15 @@ float powi_f32(float x, int n) {
     if (n) square = square * square;
   }
   return have ? result : 1.0f;
+}
+
+// The warp-cooperative walk pays off when cells hold whole warps of
+// particles; its kernels are only launched when the mean occupancy of the
+// bins is at least 8 (cfg4's clusters: ~1000 per bin; cfg1: 4; cfg2: 1),
+// since the extra code costs the sparse kernels registers (cfg2 perception
+// 0.477 vs 0.437 ms).  Both variants give identical results.
+bool dense_cells(const GridParams& g, uint32_t batch, uint32_t total) {
+  return uint64_t(total) >= uint64_t(8) * batch * g.cells;
 }
 
 // Channels per thread: 8 (measured on cfg2: two threads of 8 channels per
@@ -169,12 +211,16 @@ npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t bat
                           cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
-  if (g.dim == 2)
-    density_kernel<2><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted,
-                                                                density_out, hl);
-  else
-    density_kernel<3><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted,
-                                                                density_out, hl);
+#define NPA_DENS(D, CO)                                                                   \
+  density_kernel<D, CO><<<grid_for(total, 256), 256, 0, stream>>>(g, s, total, volume_sorted, \
+                                                                  density_out, hl)
+  const bool coop = dense_cells(g, batch, total);
+  if (g.dim == 2) {
+    if (coop) NPA_DENS(2, true); else NPA_DENS(2, false);
+  } else {
+    if (coop) NPA_DENS(3, true); else NPA_DENS(3, false);
+  }
+#undef NPA_DENS
   return after_launch("density_kernel");
 }
 
@@ -190,16 +236,21 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(total) * chunks, 128);
-#define NPA_PERC(D, CHV)                                                                      \
-  perception_kernel<D, CHV><<<blocks, 128, 0, stream>>>(g, pp, s, hl, total, states, state_dims, \
-                                                        chunks, volume_sorted, features,      \
-                                                        blurred, state_gradient,              \
-                                                        density_gradient)
+#define NPA_PERC(D, CHV, CO)                                                                  \
+  perception_kernel<D, CHV, CO><<<blocks, 128, 0, stream>>>(                                  \
+      g, pp, s, hl, total, states, state_dims, chunks, volume_sorted, features, blurred,      \
+      state_gradient, density_gradient)
+#define NPA_PERC_CH(D, CO)                                   \
+  do {                                                       \
+    if (ch == 4) NPA_PERC(D, 4, CO); else NPA_PERC(D, 8, CO); \
+  } while (0)
+  const bool coop = dense_cells(g, batch, total);
   if (g.dim == 2) {
-    if (ch == 4) NPA_PERC(2, 4); else if (ch == 8) NPA_PERC(2, 8); else NPA_PERC(2, 16);
+    if (coop) NPA_PERC_CH(2, true); else NPA_PERC_CH(2, false);
   } else {
-    if (ch == 4) NPA_PERC(3, 4); else if (ch == 8) NPA_PERC(3, 8); else NPA_PERC(3, 16);
+    if (coop) NPA_PERC_CH(3, true); else NPA_PERC_CH(3, false);
   }
+#undef NPA_PERC_CH
 #undef NPA_PERC
   return after_launch("perception_kernel");
 }
@@ -222,15 +273,21 @@ npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& 
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(q_end - q_begin) * chunks, 128);
-#define NPA_TILES(D, CHV)                                                                     \
-  perception_tiles_kernel<D, CHV><<<blocks, 128, 0, stream>>>(                                \
+#define NPA_TILES(D, CHV, CO)                                                                 \
+  perception_tiles_kernel<D, CHV, CO><<<blocks, 128, 0, stream>>>(                            \
       g, pp, s, hl, total, q_begin, q_end, states, state_dims, chunks, volume_sorted,         \
       tile_rows, tiles)
+#define NPA_TILES_CH(D, CO)                                    \
+  do {                                                         \
+    if (ch == 4) NPA_TILES(D, 4, CO); else NPA_TILES(D, 8, CO); \
+  } while (0)
+  const bool coop = dense_cells(g, batch, total);
   if (g.dim == 2) {
-    if (ch == 4) NPA_TILES(2, 4); else if (ch == 8) NPA_TILES(2, 8); else NPA_TILES(2, 16);
+    if (coop) NPA_TILES_CH(2, true); else NPA_TILES_CH(2, false);
   } else {
-    if (ch == 4) NPA_TILES(3, 4); else if (ch == 8) NPA_TILES(3, 8); else NPA_TILES(3, 16);
+    if (coop) NPA_TILES_CH(3, true); else NPA_TILES_CH(3, false);
   }
+#undef NPA_TILES_CH
 #undef NPA_TILES
   return after_launch("perception_tiles_kernel");
 }

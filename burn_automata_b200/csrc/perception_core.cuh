@@ -164,7 +164,10 @@ __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkSta
 // caller-order state matrix [B*N][C]; `volume` is recip_finite(density) per
 // sorted slot; `si` holds the particle's own channels.  Channels >= C stay 0.
 // The neighbours come from the density pass's hit list when it holds them all,
-// otherwise from a fresh hashgrid walk; both give the walk order.
+// otherwise from a fresh hashgrid walk; both give the walk order.  `win` is
+// set (warp-uniformly) when the warp's lanes fall into few (batch, cell)
+// groups (`peers`: this lane's group): then a walk, if any lane needs one, is
+// the warp-cooperative walk of each group.
 template <int DIM, int CH>
 __device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
                                                const SortedGrid& s, const HitLists& hl,
@@ -172,14 +175,27 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
                                                int3 center, const float* __restrict__ states,
                                                int C, int c0, const float* __restrict__ volume,
                                                const float (&si)[CH],
-                                               PerceptionAcc<DIM, CH>& out) {
+                                               PerceptionAcc<DIM, CH>& out,
+                                               WarpWindow* win = nullptr, uint32_t peers = 0) {
   const uint32_t batch_base = batch * s.n;
   const bool vec4 = p.vec_states && ((C & 3) == 0) && ((c0 & 3) == 0) && (CH % 4 == 0) &&
                     (c0 + CH <= C);
   ChunkState<DIM, CH> st;
   chunk_init(st);
   const uint32_t nh = hl.slots ? __ldg(hl.count + q) : uint32_t(hl.cap + 1);
-  if (nh <= uint32_t(hl.cap)) {
+  if (win && __any_sync(0xffffffffu, nh > uint32_t(hl.cap))) {
+    for_each_neighbor_warp<DIM>(
+        g, s, batch, pi, center, peers, *win,
+        [&](uint32_t lane, uint32_t qn) {
+          win->vol[lane] = __ldg(volume + qn);
+          win->row[lane] = batch_base + __ldg(s.permutation + qn);
+        },
+        [&](uint32_t j, uint32_t qn, float4 d, float r2) {
+          float sjv[CH];
+          load_row<CH>(states, win->row[j], C, c0, vec4, sjv);
+          chunk_add<DIM, CH>(g, p, qn == q, d, r2, win->vol[j], sjv, si, st);
+        });
+  } else if (nh <= uint32_t(hl.cap)) {
     const uint32_t* list = hl.slots + q;
     for (uint32_t e0 = 0; e0 < nh; e0 += 2) {
       uint32_t qj[2];

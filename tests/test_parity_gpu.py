@@ -372,3 +372,32 @@ def test_host_calls_report_out_of_memory_under_an_allocation_cap():
         L.npa_debug_set_allocation_cap(0)
     r = m.step(w.positions, w.states, 1, w.n, w.grid, w.dt)
     assert np.isfinite(r.next_states).all()
+
+
+@pytest.mark.parametrize("n", [8192])
+def test_dense_cluster_step_bit_exact_without_log_norm(oracle_mod, n):
+    """One tight cluster (thousands of particles per cell): density and
+    perception take the warp-cooperative neighbour walk."""
+    w = workloads.make("cfg4", n=n, components=1, steps=1)
+    # 16 x 16 bins: mean occupancy >= 8 selects the cooperative kernels
+    w.grid = w.grid.with_(grid_size=(16, 16, 1))
+    w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
+    m = make_model(w)
+    gpu = m.step(w.positions, w.states, 1, w.n, w.grid, w.dt)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, 1, w.n, w.dt)
+    for key in ("density", "features", "ds", "dx", "next_states", "next_positions"):
+        np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
+
+
+def test_dense_cluster_perception_full_options(oracle_mod):
+    """Dense cluster through the API perception (all outputs, density and state
+    gradients, 2 and 4 channel chunks), cooperative kernels."""
+    w = workloads.make("cfg4", n=4096, components=1, steps=1)
+    w.grid = w.grid.with_(grid_size=(16, 16, 1))
+    for c in (16, 32):
+        st = workloads.normal_states(w.n, c, 0.5, 3)
+        opt = NpaConfig.growing_2d().perception_options()
+        gpu = ba.perceive_with_options(w.positions, st, 1, w.n, c, w.grid, opt)
+        ref = oracle_mod.perceive_with_options(w.positions, st, 1, w.n, c, w.grid, opt)
+        np.testing.assert_array_equal(gpu.density, ref["density"])
+        np.testing.assert_allclose(gpu.features, ref["features"], rtol=RTOL, atol=ATOL)
