@@ -13,6 +13,7 @@ from .kernels import (DevicePerception, Gaussian3d, HashGridSnapshot, Perception
                       perceive_with_options)
 from .model import (CudaAutomataExecutor, NpaModel, NpaWeights, RolloutConfig, RolloutTrace,
                     StepOutput, run_rollout_from_particles)
+from . import bpk
 from ._lib import build as build_library, lib as load_library
 
 __all__ = [

@@ -1457,4 +1457,55 @@ npa_status npa_model_run_rollout(npa_model* m, const npa_grid_config* grid, floa
   return st;
 }
 
+npa_status npa_model_run_rollout_trace(npa_model* m, const npa_grid_config* grid,
+                                       float* positions, int64_t positions_len, float* states,
+                                       int64_t states_len, int64_t batch, int64_t n,
+                                       int64_t steps, float dt, float* mean_dx) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_step(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, m->dm.state_dims));
+  NPA_TRY(check_bins(grid, batch));
+  if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
+  if (steps > 0 && !mean_dx) return fail(NPA_ERR_INVALID_ARGUMENT, "null mean_dx");
+  const uint32_t total = uint32_t(batch * n);
+  const int C = m->dm.state_dims;
+  if (total > 0 && (!positions || (C > 0 && !states)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_device(m->dm.device));
+  if (total == 0) {
+    for (int64_t k = 0; k < steps; ++k) mean_dx[k] = 0.0f;  // 0 / max(len, 1)
+    return NPA_OK;
+  }
+  size_t wsb = 0;
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float4 *pos[2], *ddx;
+  float *st[2], *dmean;
+  double* partials;
+  char* ws;
+  NPA_TRY(sc.upload(&pos[0], positions, total));
+  NPA_TRY(sc.upload(&st[0], states, size_t(total) * C));
+  NPA_TRY(sc.alloc(&pos[1], total));
+  NPA_TRY(sc.alloc(&st[1], size_t(total) * C));
+  NPA_TRY(sc.alloc(&ddx, total));
+  NPA_TRY(sc.alloc(&dmean, size_t(std::max<int64_t>(steps, 1))));
+  NPA_TRY(sc.alloc(&partials, mean_norm_scratch_bytes() / sizeof(double)));
+  NPA_TRY(sc.alloc(&ws, wsb));
+  int cur = 0;
+  for (int64_t k = 0; k < steps; ++k) {
+    NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(pos[cur]), st[cur], batch, n, dt,
+                               nullptr, reinterpret_cast<float*>(pos[1 - cur]), st[1 - cur],
+                               reinterpret_cast<float*>(ddx), nullptr, nullptr, nullptr, ws, wsb,
+                               sc.stream));
+    NPA_TRY(launch_mean_norm(ddx, total, partials, dmean + k, sc.stream));
+    cur = 1 - cur;
+  }
+  NPA_TRY(sc.download(positions, pos[cur], size_t(total) * 16));
+  NPA_TRY(sc.download(states, st[cur], size_t(total) * C * 4));
+  NPA_TRY(sc.download(mean_dx, dmean, size_t(steps) * 4));
+  return sc.finish();
+}
+
 }  // extern "C"

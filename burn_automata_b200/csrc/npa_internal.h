@@ -137,6 +137,11 @@ struct StochasticMask {
 };
 // step_counter[0] += 1 (after a step that used the stochastic mask).
 npa_status launch_advance_step(uint32_t* counter, cudaStream_t stream);
+// out[0] = mean over i < total of |dx[i].xyz| (run_rollout's mean_dx entry);
+// partials: mean_norm_scratch_bytes() of device scratch.
+npa_status launch_mean_norm(const float4* dx, uint32_t total, double* partials, float* out,
+                            cudaStream_t stream);
+size_t mean_norm_scratch_bytes();
 // MLP + dx/ds (+3D gates) + Euler over feature tiles in sorted order.
 // Tiles [tile_begin, tile_end) of the step (default: all).
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& s,

@@ -611,6 +611,61 @@ npa_status launch_forward_update(const DeviceModel& m, const float* features, ui
 
 __global__ void advance_step_kernel(uint32_t* counter) { counter[0] += 1u; }
 
+// mean_dx of run_rollout (rollout/mod.rs:276-283): the mean over particles of
+// |dx| = sqrt(dx0^2 + dx1^2 + dx2^2), each norm in the reference's f32 order.
+// The sum runs in f64 in a fixed order (contiguous block ranges, then the
+// block partials in index order), so it is deterministic and at least as
+// accurate as the reference's sequential f32 sum.
+constexpr int kNormThreads = 256;
+constexpr int kNormBlocks = 148;
+
+__device__ __forceinline__ double block_sum(double v, double* sh) {
+  sh[threadIdx.x] = v;
+  __syncthreads();
+  for (int stride = kNormThreads / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) sh[threadIdx.x] += sh[threadIdx.x + stride];
+    __syncthreads();
+  }
+  return sh[0];
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+norm_partials_kernel(const float4* __restrict__ dx, uint32_t total, double* __restrict__ partials) {
+  __shared__ double sh[kNormThreads];
+  const uint32_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint32_t lo = min(total, blockIdx.x * per), hi = min(total, lo + per);
+  double acc = 0.0;
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kNormThreads) {
+    const float4 v = __ldg(dx + i);
+    float n2 = v.x * v.x;
+    n2 = n2 + v.y * v.y;
+    n2 = n2 + v.z * v.z;
+    acc += static_cast<double>(sqrtf(n2));
+  }
+  const double sum = block_sum(acc, sh);
+  if (threadIdx.x == 0) partials[blockIdx.x] = sum;
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+norm_final_kernel(const double* __restrict__ partials, int count, uint32_t total,
+                  float* __restrict__ out) {
+  __shared__ double sh[kNormThreads];
+  const double v = threadIdx.x < count ? partials[threadIdx.x] : 0.0;
+  const double sum = block_sum(v, sh);
+  if (threadIdx.x == 0)
+    out[0] = static_cast<float>(sum) / static_cast<float>(total > 1 ? total : 1u);
+}
+
+npa_status launch_mean_norm(const float4* dx, uint32_t total, double* partials, float* out,
+                            cudaStream_t stream) {
+  norm_partials_kernel<<<kNormBlocks, kNormThreads, 0, stream>>>(dx, total, partials);
+  NPA_TRY(after_launch("norm_partials_kernel"));
+  norm_final_kernel<<<1, kNormThreads, 0, stream>>>(partials, kNormBlocks, total, out);
+  return after_launch("norm_final_kernel");
+}
+
+size_t mean_norm_scratch_bytes() { return kNormBlocks * sizeof(double); }
+
 npa_status launch_advance_step(uint32_t* counter, cudaStream_t stream) {
   advance_step_kernel<<<1, 1, 0, stream>>>(counter);
   return after_launch("advance_step_kernel");

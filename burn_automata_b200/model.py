@@ -175,7 +175,7 @@ class RolloutConfig:
 
 @dataclass
 class RolloutTrace:
-    """rollout/mod.rs:146-155 (mean_dx is not recorded on the device path)."""
+    """rollout/mod.rs:152-161."""
 
     positions: np.ndarray
     states: np.ndarray
@@ -183,6 +183,7 @@ class RolloutTrace:
     particle_count: int
     state_dims: int
     steps: int
+    mean_dx: np.ndarray = None
 
 
 def run_rollout_from_particles(model: NpaModel, grid: HashGridConfig, cfg: RolloutConfig,
@@ -195,11 +196,13 @@ def run_rollout_from_particles(model: NpaModel, grid: HashGridConfig, cfg: Rollo
     pos = _f32(positions).reshape(-1, 4).copy()
     st = _f32(states).reshape(-1).copy()
     g = _lib.grid_c(grid)
-    _lib.check(_lib.lib().npa_model_run_rollout(
+    mean_dx = np.zeros(max(cfg.steps, 1), np.float32)
+    _lib.check(_lib.lib().npa_model_run_rollout_trace(
         model.handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
-        cfg.batch_size, cfg.particle_count, cfg.steps, float(cfg.dt)), "run_rollout")
+        cfg.batch_size, cfg.particle_count, cfg.steps, float(cfg.dt), _fp(mean_dx)),
+        "run_rollout")
     return RolloutTrace(pos, st, cfg.batch_size, cfg.particle_count, model.config.state_dims,
-                        cfg.steps)
+                        cfg.steps, mean_dx[:cfg.steps])
 
 
 class CudaAutomataExecutor:

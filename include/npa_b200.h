@@ -232,6 +232,17 @@ npa_status npa_model_run_rollout(npa_model* model, const npa_grid_config* grid, 
                                  int64_t positions_len, float* states, int64_t states_len,
                                  int64_t batch, int64_t n, int64_t steps, float dt);
 
+/* run_rollout_from_particles with the RolloutTrace's mean_dx
+ * (rollout/mod.rs:264-296): as npa_model_run_rollout, plus mean_dx[k] = the
+ * mean over particles of |dx| in step k (steps entries).  The per-particle
+ * norms follow the reference's f32 arithmetic; their sum is taken in f64
+ * (the reference adds them sequentially in f32), so mean_dx agrees to the
+ * reference's own summation error. */
+npa_status npa_model_run_rollout_trace(npa_model* model, const npa_grid_config* grid,
+                                       float* positions, int64_t positions_len, float* states,
+                                       int64_t states_len, int64_t batch, int64_t n,
+                                       int64_t steps, float dt, float* mean_dx);
+
 /* ------------------------------------------------------------------ */
 /* Device operators (caller-owned device buffers, async on a stream)   */
 /* ------------------------------------------------------------------ */
