@@ -7,10 +7,11 @@ this package is the Python mirror of the reference's operator surface
 
 from .config import (Boundary, EquivarianceMode, GaussianDecodeConfig, GaussianDecodeMode,
                      HashGridConfig, HashGridMode, KernelError, NpaConfig, PerceptionOptions,
+                     Splat2dConfig,
                      feature_dims)
 from .kernels import (DevicePerception, Gaussian3d, HashGridSnapshot, PerceptionOutput, build_hashgrid,
                       decode_gaussians_3d, decode_gaussians_3d_records, euler_step, perceive,
-                      perceive_with_options)
+                      perceive_with_options, splat_particles_2d)
 from .model import (CudaAutomataExecutor, NpaModel, NpaWeights, RolloutConfig, RolloutTrace,
                     StepOutput, run_rollout_from_particles)
 from . import bpk

@@ -55,6 +55,13 @@ class DecodeConfigC(ctypes.Structure):
                 ("min_opacity", c_f32), ("max_opacity", c_f32), ("reserved", c_i32)]
 
 
+class Splat2dConfigC(ctypes.Structure):
+    _fields_ = [("image_size", ctypes.c_int64), ("sigma", ctypes.c_float),
+                ("lo", ctypes.c_float), ("hi", ctypes.c_float),
+                ("normalize_color", ctypes.c_int32), ("y_up", ctypes.c_int32),
+                ("pixel_size", ctypes.c_float), ("reserved", ctypes.c_int32)]
+
+
 # (name, restype, argtypes) for every entry point of include/npa_b200.h.
 SIGNATURES = [
     ("npa_abi_version", c_i32, []),
@@ -91,6 +98,10 @@ SIGNATURES = [
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp, ctypes.c_size_t, vp]),
     ("npa_dev_build_hashgrid_noalloc", c_i32,
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp]),
+    ("npa_splat_particles_2d", c_i32, [P(Splat2dConfigC), f32p, f32p, c_i64, f32p, c_i64]),
+    ("npa_dev_splat_workspace_size", c_i32, [c_i64, P(ctypes.c_size_t)]),
+    ("npa_dev_splat_particles_2d", c_i32,
+     [P(Splat2dConfigC), vp, vp, c_i64, vp, vp, ctypes.c_size_t, vp]),
     ("npa_dev_perceive_workspace_size", c_i32,
      [P(GridConfigC), c_i64, c_i64, c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_perceive_with_options", c_i32,

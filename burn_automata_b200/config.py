@@ -294,3 +294,19 @@ def _f32(x: float):
     import numpy as np
 
     return np.float32(x)
+
+
+@dataclass
+class Splat2dConfig:
+    """splat.rs:4-28 (defaults as Splat2dConfig::default)."""
+
+    image_size: int = 128
+    sigma: float = 1.0
+    lo: float = -1.0
+    hi: float = 1.0
+    normalize_color: bool = True
+    y_up: bool = True
+    pixel_size: float = 2.0 / 128.0
+
+    def with_(self, **kw) -> "Splat2dConfig":
+        return replace(self, **kw)

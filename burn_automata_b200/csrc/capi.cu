@@ -1457,6 +1457,61 @@ npa_status npa_model_run_rollout(npa_model* m, const npa_grid_config* grid, floa
   return st;
 }
 
+static npa_status check_splat(const npa_splat2d_config* cfg, int64_t count) {
+  if (!cfg) return fail(NPA_ERR_INVALID_ARGUMENT, "null config");
+  if (cfg->image_size < 0 || cfg->image_size > 32768)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "image_size must be in [0, 32768]");
+  if (count < 0 || count > int64_t(kMaxParticles))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "bad particle count");
+  return NPA_OK;
+}
+
+npa_status npa_splat_particles_2d(const npa_splat2d_config* cfg, const float* positions,
+                                  const float* colors, int64_t count, float* out,
+                                  int64_t out_len) {
+  NPA_TRY(check_splat(cfg, count));
+  const int64_t pixels = cfg->image_size * cfg->image_size;
+  NPA_TRY(output_shape(out_len, pixels * 4));
+  if ((count > 0 && (!positions || !colors)) || (pixels > 0 && !out))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float4* dpos;
+  float *dcol, *dout;
+  char* ws;
+  NPA_TRY(sc.upload(&dpos, positions, size_t(count)));
+  NPA_TRY(sc.upload(&dcol, colors, size_t(count) * 3));
+  NPA_TRY(sc.alloc(&dout, size_t(pixels) * 4));
+  NPA_TRY(sc.alloc(&ws, splat_workspace_bytes(uint32_t(count))));
+  NPA_TRY(launch_splat_2d(*cfg, dpos, dcol, uint32_t(count), reinterpret_cast<float4*>(dout), ws,
+                          sc.stream));
+  NPA_TRY(sc.download(out, dout, size_t(pixels) * 16));
+  return sc.finish();
+}
+
+npa_status npa_dev_splat_workspace_size(int64_t count, size_t* bytes) {
+  if (!bytes || count < 0 || count > int64_t(kMaxParticles))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "bad argument");
+  *bytes = splat_workspace_bytes(uint32_t(count));
+  return NPA_OK;
+}
+
+npa_status npa_dev_splat_particles_2d(const npa_splat2d_config* cfg, const float* d_positions,
+                                      const float* d_colors, int64_t count, float* d_out,
+                                      void* d_workspace, size_t workspace_bytes, void* stream) {
+  NPA_TRY(check_splat(cfg, count));
+  if (workspace_bytes < splat_workspace_bytes(uint32_t(count)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  if ((count > 0 && (!d_positions || !d_colors || !d_workspace)) ||
+      (cfg->image_size > 0 && !d_out))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  return launch_splat_2d(*cfg, reinterpret_cast<const float4*>(d_positions), d_colors,
+                         uint32_t(count), reinterpret_cast<float4*>(d_out), d_workspace,
+                         static_cast<cudaStream_t>(stream));
+}
+
 npa_status npa_model_run_rollout_trace(npa_model* m, const npa_grid_config* grid,
                                        float* positions, int64_t positions_len, float* states,
                                        int64_t states_len, int64_t batch, int64_t n,

@@ -150,6 +150,12 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 
+// ---- splat (splat.cu) ----
+size_t splat_workspace_bytes(uint32_t count);
+npa_status launch_splat_2d(const npa_splat2d_config& cfg, const float4* positions,
+                           const float* colors, uint32_t count, float4* out, void* workspace,
+                           cudaStream_t stream);
+
 // ---- decode (decode.cu) ----
 npa_status launch_decode(const npa_gaussian_decode_config& cfg, const float4* positions,
                          const float* states, uint32_t count, int state_dims, float* out,

@@ -263,3 +263,37 @@ def decode_gaussians_3d(positions, states, state_dims: int,
         out.append(Gaussian3d(list(map(float, r[0:4])), sh, list(map(float, r[4:8])),
                               list(map(float, r[8:12]))))
     return out
+
+
+def splat_particles_2d(positions, colors, cfg) -> np.ndarray:
+    """splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93):
+    [image_size * image_size, 4] (RGB + weight).  Host arrays go through the
+    host entry point; torch CUDA tensors stay on the device (a tensor result)."""
+    c = _lib.Splat2dConfigC(int(cfg.image_size), float(cfg.sigma), float(cfg.lo), float(cfg.hi),
+                            1 if cfg.normalize_color else 0, 1 if cfg.y_up else 0,
+                            float(cfg.pixel_size), 0)
+    size = int(cfg.image_size)
+    if _is_torch(positions):
+        import torch
+
+        count = positions.numel() // 4
+        if colors.numel() != count * 3:
+            raise InvalidArgument("colors must hold 3 values per particle")
+        ws_bytes = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().npa_dev_splat_workspace_size(count, ctypes.byref(ws_bytes)),
+                   "splat")
+        ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=positions.device)
+        out = torch.empty((max(size * size, 1), 4), dtype=torch.float32, device=positions.device)
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+        _lib.check(_lib.lib().npa_dev_splat_particles_2d(
+            ctypes.byref(c), positions.data_ptr(), colors.data_ptr(), count, out.data_ptr(),
+            ws.data_ptr(), ws_bytes.value, stream), "splat")
+        return out[:size * size]
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    col = _f32(colors).reshape(-1)
+    if col.size != pos.shape[0] * 3:  # assert_eq!(positions.len(), colors.len())
+        raise InvalidArgument(f"{pos.shape[0]} positions but {col.size // 3} colors")
+    out = np.zeros((size * size, 4), np.float32)
+    _lib.check(_lib.lib().npa_splat_particles_2d(ctypes.byref(c), _fp(pos), _fp(col),
+                                                 pos.shape[0], _fp(out), out.size), "splat")
+    return out

@@ -132,6 +132,18 @@ typedef struct npa_gaussian_decode_config {
   int32_t reserved;
 } npa_gaussian_decode_config;
 
+/* Splat2dConfig (crates/burn_automata_kernels/src/splat.rs:4-28). */
+typedef struct npa_splat2d_config {
+  int64_t image_size;
+  float sigma;
+  float lo;
+  float hi;
+  int32_t normalize_color;
+  int32_t y_up;
+  float pixel_size;
+  int32_t reserved;
+} npa_splat2d_config;
+
 /* ------------------------------------------------------------------ */
 /* Library                                                             */
 /* ------------------------------------------------------------------ */
@@ -243,6 +255,18 @@ npa_status npa_model_run_rollout_trace(npa_model* model, const npa_grid_config* 
                                        int64_t states_len, int64_t batch, int64_t n,
                                        int64_t steps, float dt, float* mean_dx);
 
+/* splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93):
+ * positions [count][4], colors [count][3] -> out [image_size^2][4] (RGB and
+ * the weight), row-major from the top row when y_up.  Each pixel's sums are
+ * taken in particle order, as the reference's loop; exp is computed in f64
+ * and rounded, so pixels agree with the host libm's expf to its own error.
+ * The reference asserts positions.len() == colors.len(); here the two share
+ * `count`, so a mismatch cannot be expressed.  out_len must be
+ * 4 * image_size^2 (NPA_ERR_OUTPUT_SHAPE otherwise). */
+npa_status npa_splat_particles_2d(const npa_splat2d_config* cfg, const float* positions,
+                                  const float* colors, int64_t count, float* out,
+                                  int64_t out_len);
+
 /* ------------------------------------------------------------------ */
 /* Device operators (caller-owned device buffers, async on a stream)   */
 /* ------------------------------------------------------------------ */
@@ -272,6 +296,13 @@ npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg, const floa
                                           int64_t batch, int64_t n, uint32_t* d_bin_offsets,
                                           uint32_t* d_permutation,
                                           uint32_t* d_inverse_permutation, void* stream);
+
+/* Workspace bytes of npa_dev_splat_particles_2d for `count` particles. */
+npa_status npa_dev_splat_workspace_size(int64_t count, size_t* bytes);
+/* splat_particles_2d on device buffers (see npa_splat_particles_2d). */
+npa_status npa_dev_splat_particles_2d(const npa_splat2d_config* cfg, const float* d_positions,
+                                      const float* d_colors, int64_t count, float* d_out,
+                                      void* d_workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes needed by npa_dev_perceive_with_options. */
 npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t batch, int64_t n,

@@ -91,6 +91,13 @@ class _Decode(ctypes.Structure):
     ]
 
 
+class _Splat(ctypes.Structure):
+    _fields_ = [("image_size", ctypes.c_int64), ("sigma", ctypes.c_float),
+                ("lo", ctypes.c_float), ("hi", ctypes.c_float),
+                ("normalize_color", ctypes.c_int32), ("y_up", ctypes.c_int32),
+                ("pixel_size", ctypes.c_float)]
+
+
 _BOUNDARY = {"Periodic": 0, "Clamped": 1}
 _MODE = {"Grid": 0, "Particle": 1}
 _EQUIV = {"None": 0, "ParticleDensity": 1, "ParticleDensityAndScale": 2}
@@ -152,6 +159,7 @@ def lib():
         L.ora_decode_gaussians.argtypes = [P(_Decode), f32p, f32p, i64, i64, f32p]
         L.ora_gpu_update_mask.argtypes = [i64, i64, ctypes.c_float, ctypes.c_uint32,
                                           P(ctypes.c_uint32), f32p]
+        L.ora_splat_particles_2d.argtypes = [P(_Splat), f32p, f32p, i64, f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
@@ -360,6 +368,18 @@ def gpu_update_masks(batch: int, n: int, update_prob: float, steps: int, seed: i
                                          (first_step + k) & 0xFFFFFFFF,
                                          seeds.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
                                          _ptr(out[k])), "gpu_update_mask")
+    return out
+
+
+def splat_particles_2d(positions, colors, cfg) -> np.ndarray:
+    """splat.rs:30-93 -> [image_size^2, 4]."""
+    c = _Splat(int(cfg.image_size), float(cfg.sigma), float(cfg.lo), float(cfg.hi),
+               1 if cfg.normalize_color else 0, 1 if cfg.y_up else 0, float(cfg.pixel_size))
+    pos = _f32(positions).reshape(-1, 4)
+    col = _f32(colors).reshape(-1)
+    out = np.zeros((int(cfg.image_size) ** 2, 4), np.float32)
+    _check(lib().ora_splat_particles_2d(ctypes.byref(c), _ptr(pos), _ptr(col), pos.shape[0],
+                                        _ptr(out)), "splat")
     return out
 
 

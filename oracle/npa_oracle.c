@@ -938,3 +938,61 @@ int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t st
   }
   return ORA_OK;
 }
+
+/* ---- splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93) ----
+ * Each particle adds colour * w to the pixels of its (2r+1)^2 footprint, with
+ * w = exp(-(dx^2 + dy^2) / (2 sigma^2)) / (footprint weight sum) * norm_scale
+ * when normalize_color; every pixel's sums run in particle order. */
+int ora_splat_particles_2d(const ora_splat2d_config* cfg, const float* positions,
+                           const float* colors, int64_t count, float* out) {
+  const int64_t size = cfg->image_size;
+  if (size < 0 || count < 0) return ORA_ERR_INVALID_ARGUMENT;
+  for (int64_t i = 0; i < size * size * 4; ++i) out[i] = 0.0f;
+  const float fsize = (float)size;
+  float sigma = cfg->sigma;
+  if (cfg->normalize_color) sigma = sigma * fsize * cfg->pixel_size / (cfg->hi - cfg->lo);
+  const int64_t radius = f2i64_sat(maxf_rs(ceilf(5.0f * sigma), 1.0f));
+  float norm_scale = 1.0f;
+  if (cfg->normalize_color) {
+    const float r = fsize * cfg->pixel_size / (cfg->hi - cfg->lo);
+    norm_scale = r * r; /* powi(2) */
+  }
+  const float two_s2 = 2.0f * sigma * sigma;
+  for (int64_t p = 0; p < count; ++p) {
+    const float* pos = positions + p * 4;
+    const float* color = colors + p * 3;
+    const float px = (pos[0] - cfg->lo) / (cfg->hi - cfg->lo) * (fsize - 1.0f);
+    float py = (pos[1] - cfg->lo) / (cfg->hi - cfg->lo) * (fsize - 1.0f);
+    if (cfg->y_up) py = (fsize - 1.0f) - py;
+    const int64_t base_x = f2i64_sat(floorf(px));
+    const int64_t base_y = f2i64_sat(floorf(py));
+    const float frac_x = px - (float)base_x;
+    const float frac_y = py - (float)base_y;
+    float weight_sum = 0.0f;
+    for (int64_t oy = -radius; oy <= radius; ++oy)
+      for (int64_t ox = -radius; ox <= radius; ++ox) {
+        const int64_t x = base_x + ox, y = base_y + oy;
+        if (x < 0 || y < 0 || x >= size || y >= size) continue;
+        const float dx = (float)ox - frac_x, dy = (float)oy - frac_y;
+        float t = dx * dx;
+        t = t + dy * dy;
+        weight_sum = weight_sum + expf(-t / two_s2);
+      }
+    const float denom = cfg->normalize_color ? maxf_rs(weight_sum, 1e-8f) : 1.0f;
+    for (int64_t oy = -radius; oy <= radius; ++oy)
+      for (int64_t ox = -radius; ox <= radius; ++ox) {
+        const int64_t x = base_x + ox, y = base_y + oy;
+        if (x < 0 || y < 0 || x >= size || y >= size) continue;
+        const float dx = (float)ox - frac_x, dy = (float)oy - frac_y;
+        float t = dx * dx;
+        t = t + dy * dy;
+        const float w = expf(-t / two_s2) / denom * norm_scale;
+        float* px_out = out + (y * size + x) * 4;
+        px_out[0] = px_out[0] + color[0] * w;
+        px_out[1] = px_out[1] + color[1] * w;
+        px_out[2] = px_out[2] + color[2] * w;
+        px_out[3] = px_out[3] + w;
+      }
+  }
+  return ORA_OK;
+}

@@ -162,6 +162,16 @@ int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
  * (gpu_step.wgsl:1019-1056; tests/gpu_wgpu/common.rs:115-137). */
 int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t step,
                         const uint32_t* lane_seeds, float* out);
+/* Splat2dConfig (splat.rs:4-28). */
+typedef struct ora_splat2d_config {
+  int64_t image_size;
+  float sigma, lo, hi;
+  int32_t normalize_color, y_up;
+  float pixel_size;
+} ora_splat2d_config;
+/* splat_particles_2d (splat.rs:30-93): out [size * size][4] (RGB + weight). */
+int ora_splat_particles_2d(const ora_splat2d_config* cfg, const float* positions,
+                           const float* colors, int64_t count, float* out);
 void ora_set_threads(int threads);
 int ora_get_threads(void);
 
