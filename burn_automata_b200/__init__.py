@@ -11,6 +11,7 @@ from .config import (Boundary, EquivarianceMode, GaussianDecodeConfig, GaussianD
                      feature_dims)
 from .kernels import (DevicePerception, Gaussian3d, HashGridSnapshot, PerceptionOutput, build_hashgrid,
                       decode_gaussians_3d, decode_gaussians_3d_records, euler_step, perceive,
+                      perceive_adjoint_with_options, perceive_state_adjoint_with_options,
                       perceive_with_options, splat_particles_2d)
 from .model import (CudaAutomataExecutor, NpaModel, NpaWeights, RolloutConfig, RolloutTrace,
                     StepOutput, run_rollout_from_particles)

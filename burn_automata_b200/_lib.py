@@ -98,6 +98,14 @@ SIGNATURES = [
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp, ctypes.c_size_t, vp]),
     ("npa_dev_build_hashgrid_noalloc", c_i32,
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp]),
+    ("npa_perceive_adjoint_with_options", c_i32,
+     [P(GridConfigC), P(PerceptionOptionsC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, f32p,
+      c_i64, f32p, f32p]),
+    ("npa_dev_perceive_adjoint_workspace_size", c_i32,
+     [P(GridConfigC), c_i64, c_i64, c_i64, P(ctypes.c_size_t)]),
+    ("npa_dev_perceive_adjoint_with_options", c_i32,
+     [P(GridConfigC), P(PerceptionOptionsC), vp, vp, c_i64, c_i64, c_i64, vp, vp, vp, vp,
+      ctypes.c_size_t, vp]),
     ("npa_splat_particles_2d", c_i32, [P(Splat2dConfigC), f32p, f32p, c_i64, f32p, c_i64]),
     ("npa_dev_splat_workspace_size", c_i32, [c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_splat_particles_2d", c_i32,

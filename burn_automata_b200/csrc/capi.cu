@@ -1457,6 +1457,112 @@ npa_status npa_model_run_rollout(npa_model* m, const npa_grid_config* grid, floa
   return st;
 }
 
+// Device scratch of the adjoint beyond the perception workspace (floats):
+// caller-order density, density adjoint, per-particle adjoint rows.
+static size_t adjoint_extra_floats(const GridParams& g, uint32_t total, int64_t state_dims) {
+  return 2 * size_t(total) + 64 + adjoint_scratch_floats(total, int(state_dims), g.dim);
+}
+
+static npa_status adjoint_run(const npa_grid_config* cfg, const npa_perception_options* o,
+                              const float* d_positions, const float* d_states, int64_t batch,
+                              int64_t n, int64_t state_dims, const float* d_fa,
+                              float* d_state_adj, float* d_pos_adj, void* ws, size_t ws_bytes,
+                              cudaStream_t st) {
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  const PerceptionParams p = make_perception_params(g, *o, N, int(state_dims));
+  PerceiveWorkspace w;
+  const size_t extra = adjoint_extra_floats(g, total, state_dims);
+  if (!carve_perceive(g, B, N, ws, ws_bytes, &w, extra))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  float* density = w.tiles;
+  float* dens_adj = density + total + 32;
+  float* scratch = dens_adj + total + 32;
+  if (total > 0) {
+    NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
+                            w.sort_scratch, w.sort_scratch_bytes, st));
+    const SortedGrid sv = sorted_view(w, N, B, d_positions);
+    NPA_TRY(launch_density(g, sv, B, w.volume, density, w.hits, st));
+    return launch_perception_adjoint(g, p, sv, w.hg.inverse, B, d_states, int(state_dims),
+                                     density, d_fa, scratch, d_state_adj,
+                                     reinterpret_cast<float4*>(d_pos_adj), dens_adj, st);
+  }
+  return NPA_OK;
+}
+
+npa_status npa_perceive_adjoint_with_options(const npa_grid_config* cfg,
+                                             const npa_perception_options* o,
+                                             const float* positions, int64_t positions_len,
+                                             const float* states, int64_t states_len,
+                                             int64_t batch, int64_t n, int64_t state_dims,
+                                             const float* feature_adjoint,
+                                             int64_t feature_adjoint_len, float* state_adjoint,
+                                             float* position_adjoint) {
+  if (!o) return fail(NPA_ERR_INVALID_ARGUMENT, "options are null");
+  NPA_TRY(check_counts(batch, n));
+  if (state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "state_dims must be >= 0");
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, state_dims));
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_bins(cfg, batch));
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
+  const PerceptionParams p = make_perception_params(g, *o, N, int(state_dims));
+  NPA_TRY(output_shape(feature_adjoint_len, int64_t(total) * p.feature_dims));
+  if (total > 0 && (!positions || (state_dims > 0 && (!states || !state_adjoint)) ||
+                    (p.feature_dims > 0 && !feature_adjoint)))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float4* dpos;
+  float *dst, *dfa, *dsadj, *dpadj;
+  char* ws;
+  NPA_TRY(sc.upload(&dpos, positions, total));
+  NPA_TRY(sc.upload(&dst, states, size_t(total) * state_dims));
+  NPA_TRY(sc.upload(&dfa, feature_adjoint, size_t(total) * p.feature_dims));
+  NPA_TRY(sc.alloc(&dsadj, size_t(total) * state_dims + 1));
+  NPA_TRY(sc.alloc(&dpadj, size_t(total) * 4 + 4));
+  const size_t wsb = perceive_workspace_bytes(g, B, N, adjoint_extra_floats(g, total, state_dims));
+  NPA_TRY(sc.alloc(&ws, wsb));
+  NPA_TRY(adjoint_run(cfg, o, reinterpret_cast<float*>(dpos), dst, batch, n, state_dims, dfa,
+                      dsadj, dpadj, ws, wsb, sc.stream));
+  NPA_TRY(sc.download(state_adjoint, dsadj, size_t(total) * state_dims * 4));
+  NPA_TRY(sc.download(position_adjoint, dpadj, size_t(total) * 16));
+  return sc.finish();
+}
+
+npa_status npa_dev_perceive_adjoint_workspace_size(const npa_grid_config* cfg, int64_t batch,
+                                                   int64_t n, int64_t state_dims,
+                                                   size_t* bytes) {
+  NPA_TRY(validate_grid(cfg));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(cfg, batch));
+  if (!bytes || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "bad argument");
+  const GridParams g = make_grid_params(*cfg);
+  const uint32_t total = uint32_t(batch * n);
+  *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n),
+                                    adjoint_extra_floats(g, total, state_dims));
+  return NPA_OK;
+}
+
+npa_status npa_dev_perceive_adjoint_with_options(
+    const npa_grid_config* cfg, const npa_perception_options* o, const float* d_positions,
+    const float* d_states, int64_t batch, int64_t n, int64_t state_dims,
+    const float* d_feature_adjoint, float* d_state_adjoint, float* d_position_adjoint,
+    void* d_workspace, size_t workspace_bytes, void* stream) {
+  if (!o) return fail(NPA_ERR_INVALID_ARGUMENT, "options are null");
+  size_t need = 0;
+  NPA_TRY(npa_dev_perceive_adjoint_workspace_size(cfg, batch, n, state_dims, &need));
+  if (workspace_bytes < need) return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
+  if (batch * n > 0 && (!d_positions || !d_feature_adjoint || !d_position_adjoint ||
+                        !d_workspace || (state_dims > 0 && (!d_states || !d_state_adjoint))))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  return adjoint_run(cfg, o, d_positions, d_states, batch, n, state_dims, d_feature_adjoint,
+                     d_state_adjoint, d_position_adjoint, d_workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream));
+}
+
 static npa_status check_splat(const npa_splat2d_config* cfg, int64_t count) {
   if (!cfg) return fail(NPA_ERR_INVALID_ARGUMENT, "null config");
   if (cfg->image_size < 0 || cfg->image_size > 32768)

@@ -150,6 +150,19 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 
+// ---- perception adjoint (adjoint.cu) ----
+// Scratch floats launch_perception_adjoint needs beyond its outputs.
+size_t adjoint_scratch_floats(uint32_t total, int state_dims, int dim);
+// perceive_adjoint_with_options over a built hashgrid (sorted view s, local
+// inverse permutation) and the caller-order density; zeroes and fills the
+// state / position / density adjoints.
+npa_status launch_perception_adjoint(const GridParams& g, const PerceptionParams& p,
+                                     const SortedGrid& s, const uint32_t* inverse,
+                                     uint32_t batch, const float* states, int state_dims,
+                                     const float* density, const float* feature_adjoint,
+                                     float* scratch, float* state_adjoint, float4* position_adjoint,
+                                     float* density_adjoint, cudaStream_t stream);
+
 // ---- splat (splat.cu) ----
 size_t splat_workspace_bytes(uint32_t count);
 npa_status launch_splat_2d(const npa_splat2d_config& cfg, const float4* positions,

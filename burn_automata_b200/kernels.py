@@ -297,3 +297,39 @@ def splat_particles_2d(positions, colors, cfg) -> np.ndarray:
     _lib.check(_lib.lib().npa_splat_particles_2d(ctypes.byref(c), _fp(pos), _fp(col),
                                                  pos.shape[0], _fp(out), out.size), "splat")
     return out
+
+
+@dataclass
+class PerceptionAdjointOutput:
+    """types.rs:44-47."""
+
+    state: np.ndarray     # [B*N*C]
+    position: np.ndarray  # [B*N, 4]
+
+
+def perceive_adjoint_with_options(positions, states, batch_size: int, particle_count: int,
+                                  state_dims: int, cfg: HashGridConfig,
+                                  options: PerceptionOptions,
+                                  feature_adjoint) -> PerceptionAdjointOutput:
+    """perceive_adjoint_with_options (reference/adjoint.rs:28-136) on the GPU."""
+    pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
+    st = _f32(states).reshape(-1)
+    fa = _f32(feature_adjoint).reshape(-1)
+    total = batch_size * particle_count
+    sadj = np.zeros(max(total * state_dims, 0), np.float32)
+    padj = np.zeros((max(total, 0), 4), np.float32)
+    L = _lib.lib()
+    g, o = _lib.grid_c(cfg), _lib.options_c(options)
+    _lib.check(L.npa_perceive_adjoint_with_options(
+        ctypes.byref(g), ctypes.byref(o), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
+        batch_size, particle_count, state_dims, _fp(fa), fa.shape[0], _fp(sadj), _fp(padj)),
+        "perceive_adjoint_with_options")
+    return PerceptionAdjointOutput(sadj, padj)
+
+
+def perceive_state_adjoint_with_options(positions, states, batch_size: int, particle_count: int,
+                                        state_dims: int, cfg: HashGridConfig,
+                                        options: PerceptionOptions, feature_adjoint) -> np.ndarray:
+    """perceive_state_adjoint_with_options (reference/adjoint.rs:4-26)."""
+    return perceive_adjoint_with_options(positions, states, batch_size, particle_count,
+                                         state_dims, cfg, options, feature_adjoint).state

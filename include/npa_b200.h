@@ -255,6 +255,25 @@ npa_status npa_model_run_rollout_trace(npa_model* model, const npa_grid_config* 
                                        int64_t states_len, int64_t batch, int64_t n,
                                        int64_t steps, float dt, float* mean_dx);
 
+/* perceive_adjoint_with_options
+ * (crates/burn_automata_kernels/src/reference/adjoint.rs:28-136): given the
+ * adjoint of the perception features [B*N][F] (F as perceive_with_options),
+ * writes the state adjoint [B*N*C] and, when position_adjoint is not null,
+ * the position adjoint [B*N][4] (w stays 0).  Each term is the reference's;
+ * the terms of one entry are added in a different order (one thread per
+ * particle scattering with atomics), so results agree to f32 summation error.
+ * perceive_state_adjoint_with_options (:4-26) is this call with a null
+ * position_adjoint.  A wrong feature_adjoint_len returns NPA_ERR_OUTPUT_SHAPE
+ * (KernelError::OutputShape, as the reference). */
+npa_status npa_perceive_adjoint_with_options(const npa_grid_config* cfg,
+                                             const npa_perception_options* options,
+                                             const float* positions, int64_t positions_len,
+                                             const float* states, int64_t states_len,
+                                             int64_t batch, int64_t n, int64_t state_dims,
+                                             const float* feature_adjoint,
+                                             int64_t feature_adjoint_len, float* state_adjoint,
+                                             float* position_adjoint);
+
 /* splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93):
  * positions [count][4], colors [count][3] -> out [image_size^2][4] (RGB and
  * the weight), row-major from the top row when y_up.  Each pixel's sums are
@@ -296,6 +315,17 @@ npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg, const floa
                                           int64_t batch, int64_t n, uint32_t* d_bin_offsets,
                                           uint32_t* d_permutation,
                                           uint32_t* d_inverse_permutation, void* stream);
+
+/* Workspace bytes of npa_dev_perceive_adjoint_with_options. */
+npa_status npa_dev_perceive_adjoint_workspace_size(const npa_grid_config* cfg, int64_t batch,
+                                                   int64_t n, int64_t state_dims,
+                                                   size_t* bytes);
+/* perceive_adjoint_with_options on device buffers (see the host variant). */
+npa_status npa_dev_perceive_adjoint_with_options(
+    const npa_grid_config* cfg, const npa_perception_options* options, const float* d_positions,
+    const float* d_states, int64_t batch, int64_t n, int64_t state_dims,
+    const float* d_feature_adjoint, float* d_state_adjoint, float* d_position_adjoint,
+    void* d_workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes of npa_dev_splat_particles_2d for `count` particles. */
 npa_status npa_dev_splat_workspace_size(int64_t count, size_t* bytes);

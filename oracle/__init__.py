@@ -160,6 +160,8 @@ def lib():
         L.ora_gpu_update_mask.argtypes = [i64, i64, ctypes.c_float, ctypes.c_uint32,
                                           P(ctypes.c_uint32), f32p]
         L.ora_splat_particles_2d.argtypes = [P(_Splat), f32p, f32p, i64, f32p]
+        L.ora_perceive_adjoint.argtypes = [P(_Grid), P(_Opt), f32p, f32p, i64, i64, i64, f32p,
+                                           f32p, f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
@@ -369,6 +371,22 @@ def gpu_update_masks(batch: int, n: int, update_prob: float, steps: int, seed: i
                                          seeds.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
                                          _ptr(out[k])), "gpu_update_mask")
     return out
+
+
+def perceive_adjoint_with_options(positions, states, batch: int, n: int, c: int, cfg, opt,
+                                  feature_adjoint):
+    """adjoint.rs:28 perceive_adjoint_with_options -> (state [B*N*C], position [B*N, 4])."""
+    g = grid_struct(cfg)
+    o = options_struct(opt)
+    pos = _f32(positions).reshape(-1, 4)
+    st = _f32(states).reshape(-1)
+    fa = _f32(feature_adjoint).reshape(-1)
+    total = batch * n
+    sadj = np.zeros(max(total * c, 1), np.float32)
+    padj = np.zeros((max(total, 1), 4), np.float32)
+    _check(lib().ora_perceive_adjoint(ctypes.byref(g), ctypes.byref(o), _ptr(pos), _ptr(st), batch,
+                                      n, c, _ptr(fa), _ptr(sadj), _ptr(padj)), "perceive_adjoint")
+    return sadj[:total * c], padj[:total]
 
 
 def splat_particles_2d(positions, colors, cfg) -> np.ndarray:

@@ -302,7 +302,7 @@ typedef struct {
 
 /* Visits every j with r2 < eps^2 in dz, dy, dx cell order and ascending
  * permutation order inside a bin, calling VISIT(j, delta, r2). */
-#define FOR_EACH_NEIGHBOR(CTX, IDX, J, DELTA, R2, BODY)                                  \
+#define FOR_EACH_NEIGHBOR(CTX, IDX, J, DELTA, R2, ...)                                   \
   do {                                                                                   \
     const walk_ctx* w__ = (CTX);                                                         \
     int64_t batch__ = (IDX) / w__->n;                                                    \
@@ -336,7 +336,7 @@ typedef struct {
             float R2 = 0.0f;                                                             \
             for (int a__ = 0; a__ < w__->cfg->dim; ++a__) R2 = R2 + DELTA[a__] * DELTA[a__]; \
             if (R2 < w__->eps2) {                                                        \
-              BODY                                                                       \
+              __VA_ARGS__                                                                \
             }                                                                            \
           }                                                                              \
         }                                                                                \
@@ -995,4 +995,300 @@ int ora_splat_particles_2d(const ora_splat2d_config* cfg, const float* positions
       }
   }
   return ORA_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Perception adjoint (reference/adjoint.rs:28-489), serial as the reference */
+/* ------------------------------------------------------------------------ */
+
+/* smoothing_poly6_delta_adjoint (kernels.rs:62-79). */
+static void poly6_delta_adjoint(const float delta[4], float r2, const sph_consts* k,
+                                float output_adjoint, float out[4]) {
+  out[0] = out[1] = out[2] = out[3] = 0.0f;
+  if (r2 >= k->eps2) return;
+  const float x = k->eps2 - r2;
+  const float dk = -3.0f * k->poly6_norm * x * x;
+  for (int a = 0; a < k->dim; ++a) out[a] = output_adjoint * dk * 2.0f * delta[a];
+}
+
+/* spiky_gradient_delta_adjoint (kernels.rs:100-126). */
+static void spiky_delta_adjoint(const float delta[4], float r2, const sph_consts* k, float coeff,
+                                const float adj[4], float out[4]) {
+  out[0] = out[1] = out[2] = out[3] = 0.0f;
+  if (r2 <= 0.0f || r2 >= k->eps2) return;
+  const float r = sqrtf(r2);
+  const float norm = coeff * k->spiky_norm * 3.0f;
+  const float t = k->eps - r;
+  const float scale = norm * (t * t) / r;
+  const float dscale_dr = norm * (1.0f - (k->eps * k->eps) / r2);
+  float dot = 0.0f;
+  for (int a = 0; a < k->dim; ++a) dot = dot + adj[a] * delta[a];
+  for (int a = 0; a < k->dim; ++a) out[a] = scale * adj[a] + dscale_dr * dot * delta[a] / r;
+}
+
+/* log_normalize_adjoint (normalize.rs:71-91); input_adjoint starts at zero. */
+static void log_normalize_adjoint(const float* input, const float* out_adj, float* in_adj,
+                                  int len) {
+  const float e = 1.0e-6f;
+  float s = 0.0f;
+  for (int i = 0; i < len; ++i) s = s + input[i] * input[i];
+  const float norm = maxf_rs(sqrtf(s + e * e), e);
+  const float l = log1pf(norm);
+  const float scale = l / norm;
+  const float dscale = (norm / (1.0f + norm) - l) / (norm * norm);
+  float dot = 0.0f;
+  for (int i = 0; i < len; ++i) dot = dot + input[i] * out_adj[i];
+  const float radial = dscale * dot / norm;
+  for (int i = 0; i < len; ++i) in_adj[i] = in_adj[i] + (scale * out_adj[i] + radial * input[i]);
+}
+
+/* accumulate_volume_density_adjoint (adjoint.rs:425-435). */
+static void volume_density_adjoint(const float* density, float* density_adjoint, int64_t idx,
+                                   float volume_adjoint) {
+  const float rho = density[idx];
+  if (fabsf(rho) <= 1.0e-20f || !isfinite(rho)) return;
+  density_adjoint[idx] = density_adjoint[idx] - volume_adjoint / (rho * rho);
+}
+
+/* add_delta_position_adjoint (adjoint.rs:437-448). */
+static void delta_position_adjoint(float* pos_adj, int64_t lhs, int64_t rhs, int dim,
+                                   const float d[4]) {
+  for (int a = 0; a < dim; ++a) {
+    pos_adj[4 * rhs + a] = pos_adj[4 * rhs + a] + d[a];
+    pos_adj[4 * lhs + a] = pos_adj[4 * lhs + a] - d[a];
+  }
+}
+
+int ora_perceive_adjoint(const ora_grid_config* cfg, const ora_perception_options* opt,
+                         const float* positions, const float* states, int64_t batch, int64_t n,
+                         int64_t c, const float* feature_adjoint, float* state_adjoint,
+                         float* position_adjoint) {
+  int st = check_shapes_basic(batch, n, c);
+  if (st) return st;
+  st = ora_grid_validate(cfg);
+  if (st) return st;
+  const int dim = cfg->dim;
+  const int64_t total = batch * n;
+  const int64_t fd = ora_feature_dims(cfg, opt, c);
+  const int64_t cells = ora_cell_count(cfg);
+  int64_t* offsets = (int64_t*)malloc((size_t)(batch * cells + 1) * sizeof(int64_t));
+  int64_t* perm = (int64_t*)malloc((size_t)(total > 0 ? total : 1) * sizeof(int64_t));
+  int64_t* inv = (int64_t*)malloc((size_t)(total > 0 ? total : 1) * sizeof(int64_t));
+  float* density = (float*)malloc((size_t)(total > 0 ? total : 1) * sizeof(float));
+  float* density_adjoint = (float*)calloc((size_t)(total > 0 ? total : 1), sizeof(float));
+  float* raw = (float*)malloc((size_t)(c * dim > 0 ? c * dim : 1) * sizeof(float));
+  float* raw_adj = (float*)malloc((size_t)(c * dim > 0 ? c * dim : 1) * sizeof(float));
+  if (!offsets || !perm || !inv || !density || !density_adjoint || !raw || !raw_adj) {
+    st = ORA_ERR_INVALID_ARGUMENT;
+    goto done;
+  }
+  for (int64_t i = 0; i < total * c; ++i) state_adjoint[i] = 0.0f;
+  for (int64_t i = 0; i < total * 4; ++i) position_adjoint[i] = 0.0f;
+  st = ora_build_hashgrid(cfg, positions, batch, n, offsets, perm, inv);
+  if (st) goto done;
+  walk_ctx w = {cfg, positions, offsets, perm, n, cells, cfg->eps * cfg->eps};
+  sph_consts k = make_sph(cfg);
+#pragma omp parallel for schedule(dynamic, 256) num_threads(ora_get_threads())
+  for (int64_t idx = 0; idx < total; ++idx) {
+    float rho = 0.0f;
+    FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, { (void)j; (void)delta; rho = rho + poly6(r2, &k); });
+    density[idx] = rho;
+  }
+  const float eps0 = maxf_rs(opt->eps0, 1.17549435e-38f);
+  const float grad_scale = opt->scale_equivariance ? cfg->eps / eps0 : 1.0f;
+  float dens_scale = opt->scale_equivariance ? ora_powi(cfg->eps / eps0, 1 + dim) : 1.0f;
+  dens_scale = dens_scale * (opt->particle_density_equivariance ? 1.0f / (float)(n > 1 ? n : 1)
+                                                                : 1.0f);
+
+  for (int64_t idx = 0; idx < total; ++idx) {
+    const float* fa = feature_adjoint + idx * fd;
+    int64_t cur = 0;
+    const int64_t si = idx * c;
+    for (int64_t ch = 0; ch < c; ++ch) state_adjoint[si + ch] = state_adjoint[si + ch] + fa[ch];
+    cur += c;
+    /* accumulate_blurred_state_adjoint (adjoint.rs:138-166) */
+    {
+      const float* badj = fa + cur;
+      FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+        const float vol = recip_finite(density[j]);
+        const float kern = poly6(r2, &k);
+        const float weight = kern * vol;
+        const int64_t sj = j * c;
+        float wadj = 0.0f;
+        for (int64_t ch = 0; ch < c; ++ch) {
+          state_adjoint[sj + ch] = state_adjoint[sj + ch] + badj[ch] * weight;
+          wadj = wadj + badj[ch] * states[sj + ch];
+        }
+        float da[4];
+        poly6_delta_adjoint(delta, r2, &k, wadj * vol, da);
+        delta_position_adjoint(position_adjoint, idx, j, dim, da);
+        volume_density_adjoint(density, density_adjoint, j, wadj * kern);
+      });
+    }
+    cur += c;
+    if (opt->state_grad) {
+      /* accumulate_state_gradient_adjoint (adjoint.rs:168-343) */
+      const float* gadj = fa + cur;
+      const int64_t gd = c * dim;
+      for (int64_t g = 0; g < gd; ++g) raw[g] = 0.0f;
+      float moment[9] = {0};
+      FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+        if (j != idx) {
+          const float vol = recip_finite(density[j]);
+          float gv[4];
+          spiky(delta, r2, &k, vol, gv);
+          const int64_t sj = j * c;
+          for (int64_t ch = 0; ch < c; ++ch) {
+            const float diff = states[sj + ch] - states[si + ch];
+            for (int a = 0; a < dim; ++a) raw[ch * dim + a] = raw[ch * dim + a] + diff * gv[a];
+          }
+          if (opt->hybrid_state_gradient)
+            for (int r = 0; r < dim; ++r)
+              for (int col = 0; col < dim; ++col)
+                moment[r * dim + col] = moment[r * dim + col] + delta[r] * gv[col];
+        }
+      });
+      float inverse[9];
+      const int hybrid = opt->hybrid_state_gradient;
+      if (hybrid) safe_inverse_symmetric(moment, dim, inverse);
+      float inv_adj[9] = {0};
+      for (int64_t ch = 0; ch < c; ++ch) {
+        float corrected[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const int64_t gb = ch * dim;
+        for (int a = 0; a < dim; ++a) corrected[a] = raw[gb + a];
+        if (hybrid) {
+          float mc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (int oa = 0; oa < dim; ++oa)
+            for (int ia = 0; ia < dim; ++ia) mc[oa] = mc[oa] + corrected[ia] * inverse[ia * dim + oa];
+          for (int a = 0; a < 4; ++a) corrected[a] = mc[a];
+        }
+        float ninput[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int a = 0; a < dim; ++a) ninput[a] = corrected[a] * grad_scale;
+        float cadj[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (opt->log_norm_grad)
+          log_normalize_adjoint(ninput, gadj + gb, cadj, dim);
+        else
+          for (int a = 0; a < dim; ++a) cadj[a] = gadj[gb + a];
+        for (int a = 0; a < dim; ++a) cadj[a] = cadj[a] * grad_scale;
+        float radj[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (hybrid) {
+          for (int ia = 0; ia < dim; ++ia)
+            for (int oa = 0; oa < dim; ++oa)
+              radj[ia] = radj[ia] + cadj[oa] * inverse[ia * dim + oa];
+        } else {
+          for (int a = 0; a < dim; ++a) radj[a] = cadj[a];
+        }
+        for (int a = 0; a < dim; ++a) raw_adj[gb + a] = radj[a];
+        if (hybrid)
+          for (int ia = 0; ia < dim; ++ia)
+            for (int oa = 0; oa < dim; ++oa)
+              inv_adj[ia * dim + oa] = inv_adj[ia * dim + oa] + raw[gb + ia] * cadj[oa];
+      }
+      float m_adj[9] = {0};
+      if (hybrid) {
+        /* inverse_matrix_adjoint (adjoint.rs:450-469) */
+        for (int row = 0; row < dim; ++row)
+          for (int col = 0; col < dim; ++col) {
+            float value = 0.0f;
+            for (int ir = 0; ir < dim; ++ir)
+              for (int ic = 0; ic < dim; ++ic)
+                value = value + inverse[ir * dim + row] * inv_adj[ir * dim + ic] * inverse[col * dim + ic];
+            m_adj[row * dim + col] = m_adj[row * dim + col] - value;
+          }
+      }
+      FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+        if (j != idx) {
+          const float vol = recip_finite(density[j]);
+          float vg[4], ug[4];
+          spiky(delta, r2, &k, vol, vg);
+          spiky(delta, r2, &k, 1.0f, ug);
+          const int64_t sj = j * c;
+          for (int64_t ch = 0; ch < c; ++ch) {
+            const int64_t gb = ch * dim;
+            const float diff = states[sj + ch] - states[si + ch];
+            float contrib = 0.0f;
+            for (int a = 0; a < dim; ++a) contrib = contrib + raw_adj[gb + a] * vg[a];
+            state_adjoint[sj + ch] = state_adjoint[sj + ch] + contrib;
+            state_adjoint[si + ch] = state_adjoint[si + ch] - contrib;
+            float gadj2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int a = 0; a < dim; ++a) gadj2[a] = raw_adj[gb + a] * diff;
+            float da[4];
+            spiky_delta_adjoint(delta, r2, &k, vol, gadj2, da);
+            delta_position_adjoint(position_adjoint, idx, j, dim, da);
+            float vadj = 0.0f;
+            for (int a = 0; a < dim; ++a) vadj = vadj + gadj2[a] * ug[a];
+            volume_density_adjoint(density, density_adjoint, j, vadj);
+          }
+          if (hybrid) {
+            float dda[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gadj2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int row = 0; row < dim; ++row)
+              for (int col = 0; col < dim; ++col) {
+                const float adj = m_adj[row * dim + col];
+                dda[row] = dda[row] + adj * vg[col];
+                gadj2[col] = gadj2[col] + adj * delta[row];
+              }
+            float gda[4];
+            spiky_delta_adjoint(delta, r2, &k, vol, gadj2, gda);
+            for (int a = 0; a < dim; ++a) dda[a] = dda[a] + gda[a];
+            delta_position_adjoint(position_adjoint, idx, j, dim, dda);
+            float vadj = 0.0f;
+            for (int a = 0; a < dim; ++a) vadj = vadj + gadj2[a] * ug[a];
+            volume_density_adjoint(density, density_adjoint, j, vadj);
+          }
+        }
+      });
+      cur += gd;
+    }
+    if (opt->density_grad) {
+      /* accumulate_density_gradient_position_adjoint (adjoint.rs:345-392) */
+      const float* dadj = fa + cur;
+      float rawd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+        if (j != idx) {
+          float g1[4];
+          spiky(delta, r2, &k, 1.0f, g1);
+          for (int a = 0; a < dim; ++a) rawd[a] = rawd[a] + g1[a];
+        }
+      });
+      float ninput[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int a = 0; a < dim; ++a) ninput[a] = rawd[a] * dens_scale;
+      float radj[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (opt->log_norm_density_grad) {
+        log_normalize_adjoint(ninput, dadj, radj, dim);
+        for (int a = 0; a < dim; ++a) radj[a] = radj[a] * dens_scale;
+      } else {
+        for (int a = 0; a < dim; ++a) radj[a] = dadj[a] * dens_scale;
+      }
+      FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+        if (j != idx) {
+          float da[4];
+          spiky_delta_adjoint(delta, r2, &k, 1.0f, radj, da);
+          delta_position_adjoint(position_adjoint, idx, j, dim, da);
+        }
+      });
+      cur += dim;
+    }
+    if (opt->position_features)
+      for (int a = 0; a < dim; ++a)
+        position_adjoint[4 * idx + a] = position_adjoint[4 * idx + a] + fa[cur + a];
+  }
+  /* accumulate_density_kernel_position_adjoint (adjoint.rs:394-412) */
+  for (int64_t idx = 0; idx < total; ++idx) {
+    const float adj = density_adjoint[idx];
+    if (adj == 0.0f) continue;
+    FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+      float da[4];
+      poly6_delta_adjoint(delta, r2, &k, adj, da);
+      delta_position_adjoint(position_adjoint, idx, j, dim, da);
+    });
+  }
+done:
+  free(offsets);
+  free(perm);
+  free(inv);
+  free(density);
+  free(density_adjoint);
+  free(raw);
+  free(raw_adj);
+  return st;
 }

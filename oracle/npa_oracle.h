@@ -162,6 +162,12 @@ int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
  * (gpu_step.wgsl:1019-1056; tests/gpu_wgpu/common.rs:115-137). */
 int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t step,
                         const uint32_t* lane_seeds, float* out);
+/* perceive_adjoint_with_options (reference/adjoint.rs:28-136): feature_adjoint
+ * [B*N][F] -> state_adjoint [B*N*C] and position_adjoint [B*N][4]. */
+int ora_perceive_adjoint(const ora_grid_config* cfg, const ora_perception_options* opt,
+                         const float* positions, const float* states, int64_t batch, int64_t n,
+                         int64_t c, const float* feature_adjoint, float* state_adjoint,
+                         float* position_adjoint);
 /* Splat2dConfig (splat.rs:4-28). */
 typedef struct ora_splat2d_config {
   int64_t image_size;
