@@ -87,8 +87,9 @@ def _executor_case(w, prob, steps, seed, lane_seeds=None, first_step=0):
 
 
 @pytest.mark.gpu
-def test_executor_mask_is_bit_exact_without_log_norm():
-    w = workloads.make("cfg2", batch=4, steps=1)
+@pytest.mark.parametrize("batch", [4, 8])  # 8: the 384-thread MLP tiles
+def test_executor_mask_is_bit_exact_without_log_norm(batch):
+    w = workloads.make("cfg2", batch=batch, steps=1)
     w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
     (pos, st), (rpos, rst, _) = _executor_case(w, 0.5, 6, seed=2024)
     np.testing.assert_array_equal(st, rst)
