@@ -17,10 +17,16 @@
 namespace npa {
 namespace {
 
-// Six 128-thread blocks per SM (80 registers, a few spills to L1): the
+// 2D: six 128-thread blocks per SM (80 registers, a few spills to L1): the
 // neighbour gathers are latency-bound, and 24 warps per SM beat 16 at 127
-// registers (cfg2 perception 0.446 vs 0.538 ms; 5 blocks 0.485, 8 blocks 0.512).
-constexpr int kPerceptionBlocksPerSm = 6;
+// registers (cfg2 perception 0.446 vs 0.538 ms; 5 blocks 0.485, 8 blocks
+// 0.512).  3D keeps more accumulators (3 gradient axes, a 3 x 3 moment) and
+// spills too much at 80 registers (cfg3 perception 0.261 ms); four blocks
+// (128 registers) give 0.167 ms, no bound (196 registers) 0.176 ms.
+template <int DIM>
+struct PerceptionBlocks {
+  static constexpr int value = DIM == 2 ? 6 : 4;
+};
 
 template <int DIM, bool COOP>
 __global__ void __launch_bounds__(256)
@@ -66,7 +72,7 @@ __device__ __forceinline__ void load_own(const float* __restrict__ states, size_
 }
 
 template <int DIM, int CH, bool COOP>
-__global__ void __launch_bounds__(128, kPerceptionBlocksPerSm)
+__global__ void __launch_bounds__(128, PerceptionBlocks<DIM>::value)
 perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, uint32_t total,
                   const float* __restrict__ states, int C, int chunks,
                   const float* __restrict__ volume, float* __restrict__ features,
@@ -113,7 +119,7 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
 }
 
 template <int DIM, int CH, bool COOP>
-__global__ void __launch_bounds__(128, kPerceptionBlocksPerSm)
+__global__ void __launch_bounds__(128, PerceptionBlocks<DIM>::value)
 perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl,
                         uint32_t total, uint32_t q_begin, uint32_t q_end,
                         const float* __restrict__ states, int C, int chunks,

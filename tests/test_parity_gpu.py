@@ -50,6 +50,33 @@ def test_hashgrid_full_size_cfg1(oracle_mod):
     assert_hashgrid_equal(oracle_mod, w.positions, w.batch, w.n, w.grid)
 
 
+@pytest.mark.parametrize("name", ["cfg2", "cfg4"])
+def test_hashgrid_full_size_batched_and_clustered(oracle_mod, name):
+    """The benchmark's own shapes: 256 x 4,096 (shared-memory sort) and one
+    4,194,304-particle clustered rollout (device-wide radix sort)."""
+    w = workloads.make(name)
+    assert_hashgrid_equal(oracle_mod, w.positions, w.batch, w.n, w.grid)
+
+
+def test_full_size_cfg2_step_bit_exact_without_log_norm(oracle_mod):
+    """One step of the whole benchmark workload (1,048,576 particles) through
+    the resident executor, bit for bit against the oracle."""
+    import torch
+
+    w = workloads.make("cfg2", steps=1)
+    w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
+    m = make_model(w)
+    ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
+    ex.create_state(w.positions, w.states)
+    ex.step_state_many(1, w.dt, use_graph=True, stream=torch.cuda.Stream().cuda_stream)
+    pos, st = ex.read_state()
+    ex.close()
+    rpos, rst, _ = oracle_mod.rollout(w.model, w.weights, w.grid, w.positions, w.states, w.batch,
+                                      w.n, 1, w.dt)
+    np.testing.assert_array_equal(st, rst)
+    np.testing.assert_array_equal(pos, rpos)
+
+
 def test_hashgrid_edge_cases(oracle_mod):
     g2 = HashGridConfig.growing_2d()
     # empty batch and empty rollouts
