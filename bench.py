@@ -66,8 +66,8 @@ WORKLOADS = {
 
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu captures, per particle of that launch:
-#   profiles/mlp_step_kernel_cfg2.txt: 289.7 MB + 65.7 MB for 1,048,576 rows.
-NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (289.698816e6 + 65.66272e6) / 1048576}
+#   profiles/mlp_step_kernel_cfg2.txt: 356.7 MB + 67.7 MB for 1,048,576 rows.
+NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (356.671744e6 + 67.690752e6) / 1048576}
 
 
 def env_int(name, default):
@@ -92,9 +92,9 @@ def grid_cells(grid) -> int:
 
 def mlp_kernel_bytes(model) -> int:
     """Algorithmic HBM bytes per particle of the MLP step kernel: feature row
-    read (4F), position read + write (32), next state write (4C), permutation
-    read (4)."""
-    return 4 * model.perception_dims() + 32 + 4 * model.state_dims + 4
+    read (4F), position read + write (32), own state read and next state
+    write (8C), permutation read (4)."""
+    return 4 * model.perception_dims() + 32 + 8 * model.state_dims + 4
 
 
 def step_bytes(w) -> float:
