@@ -416,6 +416,27 @@ def test_dense_cluster_step_bit_exact_without_log_norm(oracle_mod, n):
         np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
 
 
+@pytest.mark.parametrize("dim,c", [(2, 12), (2, 16), (3, 12), (3, 16)])
+def test_dense_cluster_perception_sixteen_channel_threads(oracle_mod, dim, c):
+    """Dense cells with 9 to 16 channels: the cooperative kernels run one
+    thread per particle over all its channels (a partial chunk at C = 12)."""
+    rng = np.random.Generator(np.random.PCG64(40 + dim))
+    n = 4096
+    pos = np.zeros((n, 4), np.float32)
+    pos[:, :dim] = (rng.standard_normal((n, dim)) * 0.1).astype(np.float32)
+    if dim == 2:
+        grid = workloads.cfg0_grid().with_(grid_size=(16, 16, 1))
+        opt = NpaConfig.growing_2d().perception_options()
+    else:
+        grid = HashGridConfig.growing_3dgs().with_(eps=0.06, grid_size=(8, 8, 8))
+        opt = NpaConfig.growing_3dgs().perception_options()
+    st = workloads.normal_states(n, c, 0.5, 5)
+    gpu = ba.perceive_with_options(pos, st, 1, n, c, grid, opt)
+    ref = oracle_mod.perceive_with_options(pos, st, 1, n, c, grid, opt)
+    np.testing.assert_array_equal(gpu.density, ref["density"])
+    np.testing.assert_allclose(gpu.features, ref["features"], rtol=RTOL, atol=ATOL)
+
+
 def test_dense_cluster_perception_full_options(oracle_mod):
     """Dense cluster through the API perception (all outputs, density and state
     gradients, 2 and 4 channel chunks), cooperative kernels."""
