@@ -417,10 +417,15 @@ int64_t record_floats(const npa_gaussian_decode_config* cfg) {
 // Device buffers and the stream behind a model's host-buffer step calls:
 // kept between calls (grown on demand, freed with the model), so a loop of
 // host-buffer steps pays for its copies and kernels, not for allocations.
+// Device memory and streams of the host-buffer entry points.  `stream` runs
+// the kernels; the pipelined step adds a copy-in and a copy-out stream and
+// two events per rollout chunk.
 struct HostArena {
   void* base = nullptr;
   size_t cap = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> events;
 };
 
 struct npa_model {
@@ -761,9 +766,13 @@ void npa_model_destroy(npa_model* m) {
   cudaFree(m->dm.b1);
   cudaFree(m->dm.w2);
   cudaFree(m->dm.b2);
-  if (m->arena.stream) cudaStreamSynchronize(m->arena.stream);
-  cudaFree(m->arena.base);
-  if (m->arena.stream) cudaStreamDestroy(m->arena.stream);
+  HostArena& a = m->arena;
+  for (cudaStream_t s : {a.stream, a.copy_in, a.copy_out})
+    if (s) cudaStreamSynchronize(s);
+  cudaFree(a.base);
+  for (cudaEvent_t e : a.events) cudaEventDestroy(e);
+  for (cudaStream_t s : {a.stream, a.copy_in, a.copy_out})
+    if (s) cudaStreamDestroy(s);
   cudaSetDevice(prev);
   delete m;
 }
@@ -810,6 +819,40 @@ npa_status arena_reserve(npa_model* m, size_t bytes) {
   return NPA_OK;
 }
 
+// True when `p` is page-locked host memory (or null), so that copies from and
+// to it run asynchronously on a copy engine.
+static bool host_pinned(const void* p) {
+  if (!p) return true;
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+// Rollout chunks of the host step.  Rollouts are independent, so the step of
+// a batch is the step of each run of rollouts; with page-locked buffers the
+// copy-in of chunk i + 1 and the copy-out of chunk i - 1 overlap the kernels
+// of chunk i.  Chunks keep at least 2^17 particles (full kernel grids); at
+// most 8.
+static uint32_t host_step_chunks(uint32_t B, uint32_t N, bool pinned) {
+  if (!pinned || B < 2) return 1;
+  const uint64_t by_size = (uint64_t(B) * N) >> 17;
+  return uint32_t(std::max<uint64_t>(1, std::min<uint64_t>({8, by_size, B})));
+}
+
+static npa_status arena_pipeline(HostArena& a, uint32_t chunks) {
+  for (cudaStream_t* s : {&a.copy_in, &a.copy_out})
+    if (!*s) NPA_CUDA(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "cudaStreamCreate");
+  while (a.events.size() < 2 * size_t(chunks)) {
+    cudaEvent_t e;
+    NPA_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    a.events.push_back(e);
+  }
+  return NPA_OK;
+}
+
 npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float* positions,
                           int64_t positions_len, const float* states, int64_t states_len,
                           int64_t batch, int64_t n, float dt, const float* update_mask,
@@ -825,8 +868,17 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
   if (total > 0 && (!positions || (C > 0 && (!states || !next_states)) || !next_positions))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
   NPA_TRY(ensure_device(m->dm.device));
+  bool pinned = true;
+  for (const void* h : {static_cast<const void*>(positions), static_cast<const void*>(states),
+                        static_cast<const void*>(update_mask), static_cast<const void*>(next_positions),
+                        static_cast<const void*>(next_states), static_cast<const void*>(dx),
+                        static_cast<const void*>(ds), static_cast<const void*>(features),
+                        static_cast<const void*>(density)})
+    pinned = pinned && host_pinned(h);
+  const uint32_t chunks = host_step_chunks(B, N, pinned);
+  const uint32_t chunk_max = (B + chunks - 1) / std::max<uint32_t>(chunks, 1);
   size_t wsb = 0;
-  NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, chunks > 1 ? chunk_max : batch, n, &wsb));
   std::lock_guard<std::mutex> lock(m->mu);
   struct Bufs {
     float4 *pos, *np, *dx;
@@ -850,28 +902,67 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
   };
   NPA_TRY(arena_reserve(m, layout(nullptr)));
   layout(m->arena.base);
-  cudaStream_t st = m->arena.stream;
+  HostArena& a = m->arena;
+  cudaStream_t st = a.stream, in = st, out = st;
+  if (chunks > 1) {
+    NPA_TRY(arena_pipeline(a, chunks));
+    in = a.copy_in;
+    out = a.copy_out;
+  }
   auto h2d = [&](void* d, const void* h, size_t bytes) -> npa_status {
-    if (bytes) NPA_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st), "cudaMemcpyAsync H2D");
+    if (bytes) NPA_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, in), "cudaMemcpyAsync H2D");
     return NPA_OK;
   };
   auto d2h = [&](void* h, const void* d, size_t bytes) -> npa_status {
-    if (bytes && h) NPA_CUDA(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync D2H");
+    if (bytes && h) NPA_CUDA(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, out), "cudaMemcpyAsync D2H");
     return NPA_OK;
   };
-  NPA_TRY(h2d(b.pos, positions, size_t(total) * 16));
-  NPA_TRY(h2d(b.st, states, size_t(total) * C * 4));
-  if (update_mask) NPA_TRY(h2d(b.mask, update_mask, size_t(total) * 4));
-  NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(b.pos), b.st, batch, n, dt, b.mask,
-                             reinterpret_cast<float*>(b.np), b.ns, reinterpret_cast<float*>(b.dx),
-                             b.ds, b.feat, b.dens, b.ws, wsb, st));
-  NPA_TRY(d2h(next_positions, b.np, size_t(total) * 16));
-  NPA_TRY(d2h(next_states, b.ns, size_t(total) * C * 4));
-  if (dx) NPA_TRY(d2h(dx, b.dx, size_t(total) * 16));
-  if (ds) NPA_TRY(d2h(ds, b.ds, size_t(total) * C * 4));
-  if (features) NPA_TRY(d2h(features, b.feat, size_t(total) * F * 4));
-  if (density) NPA_TRY(d2h(density, b.dens, size_t(total) * 4));
-  NPA_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  // Chunk c holds rollouts [c B / chunks, (c + 1) B / chunks); its particles
+  // [p0, p1) are contiguous in every buffer.
+  auto span = [&](uint32_t c, size_t* p0, size_t* p1) {
+    *p0 = size_t(uint64_t(c) * B / chunks) * N;
+    *p1 = size_t(uint64_t(c + 1) * B / chunks) * N;
+  };
+  const npa_status status = [&]() -> npa_status {
+    for (uint32_t c = 0; c < chunks; ++c) {
+      size_t p0, p1;
+      span(c, &p0, &p1);
+      NPA_TRY(h2d(b.pos + p0, positions + 4 * p0, (p1 - p0) * 16));
+      NPA_TRY(h2d(b.st + p0 * C, states + p0 * C, (p1 - p0) * C * 4));
+      if (update_mask) NPA_TRY(h2d(b.mask + p0, update_mask + p0, (p1 - p0) * 4));
+      if (chunks > 1) NPA_CUDA(cudaEventRecord(a.events[2 * c], in), "cudaEventRecord");
+    }
+    for (uint32_t c = 0; c < chunks; ++c) {
+      size_t p0, p1;
+      span(c, &p0, &p1);
+      const int64_t rollouts = int64_t((p1 - p0) / std::max<uint32_t>(N, 1));
+      if (chunks > 1) NPA_CUDA(cudaStreamWaitEvent(st, a.events[2 * c], 0), "cudaStreamWaitEvent");
+      NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(b.pos + p0), b.st + p0 * C,
+                                 chunks > 1 ? rollouts : batch, n, dt,
+                                 b.mask ? b.mask + p0 : nullptr, reinterpret_cast<float*>(b.np + p0),
+                                 b.ns + p0 * C, b.dx ? reinterpret_cast<float*>(b.dx + p0) : nullptr,
+                                 b.ds ? b.ds + p0 * C : nullptr, b.feat ? b.feat + p0 * F : nullptr,
+                                 b.dens ? b.dens + p0 : nullptr, b.ws, wsb, st));
+      if (chunks > 1) {
+        NPA_CUDA(cudaEventRecord(a.events[2 * c + 1], st), "cudaEventRecord");
+        NPA_CUDA(cudaStreamWaitEvent(out, a.events[2 * c + 1], 0), "cudaStreamWaitEvent");
+      }
+      NPA_TRY(d2h(next_positions + 4 * p0, b.np + p0, (p1 - p0) * 16));
+      NPA_TRY(d2h(next_states + p0 * C, b.ns + p0 * C, (p1 - p0) * C * 4));
+      if (dx) NPA_TRY(d2h(dx + 4 * p0, b.dx + p0, (p1 - p0) * 16));
+      if (ds) NPA_TRY(d2h(ds + p0 * C, b.ds + p0 * C, (p1 - p0) * C * 4));
+      if (features) NPA_TRY(d2h(features + p0 * F, b.feat + p0 * F, (p1 - p0) * F * 4));
+      if (density) NPA_TRY(d2h(density + p0, b.dens + p0, (p1 - p0) * 4));
+    }
+    return NPA_OK;
+  }();
+  // Nothing of this call is in flight on return, on success or failure.
+  const cudaError_t e_out = cudaStreamSynchronize(out);
+  const cudaError_t e_in = in != out ? cudaStreamSynchronize(in) : cudaSuccess;
+  const cudaError_t e_st = st != out ? cudaStreamSynchronize(st) : cudaSuccess;
+  if (status != NPA_OK) return status;
+  for (cudaError_t e : {e_out, e_in, e_st})
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
   return NPA_OK;
 }
 

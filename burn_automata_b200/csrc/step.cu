@@ -13,7 +13,8 @@
 // not fit in shared memory), HG x RG thread grid with
 // HG = Hp / kTH hidden groups and RG = NT / HG row groups; a tile holds
 // M = 8 * RG rows.
-//   layer 1: each thread owns an 8 rows x kTH hidden-unit register tile and
+//   layer 1: each thread owns an 8 rows x kTH hidden-unit register tile (the
+//            lane layout is described at layer1_hidden_group) and
 //            walks k = 0..F-1 in order (features of the tile feature-major in
 //            shared memory, w1 transposed in shared memory);
 //   layer 2: 2 NT / M threads per pair of rows, each owning
@@ -129,25 +130,47 @@ __device__ __forceinline__ void micro_tile(float (&acc)[8][kTH], float4 a0, floa
 }
 
 // Layer 1 for the tile in ft[F][M]: hid[r][h] = max(b1[h] + sum_k w1[h][k] f[r][k], 0).
+//
+// Thread layout: HG = Hp / 8 hidden groups times NT / HG row groups.  A warp
+// spans 8 hidden groups (lanes % 8) of 4 row groups (lanes / 8); hidden group
+// hg owns units (j4 HG + hg) 4 + e, j4 in {0, 1}, e in [0, 4), so each
+// 16-byte weight load of a warp reads 128 contiguous bytes and each feature
+// load four 32-byte-spaced rows: one shared-memory wavefront apiece.
+template <int HG>
+__device__ __forceinline__ int layer1_hidden_group() {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  return (warp % (HG / 8)) * 8 + (lane & 7);
+}
+template <int HG>
+__device__ __forceinline__ int layer1_row_group() {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  return (warp / (HG / 8)) * 4 + (lane >> 3);
+}
+static_assert(kTH == 8, "layer1_unit assumes two float4 groups per thread");
+__host__ __device__ constexpr int layer1_unit(int HG, int hg, int j4) { return (j4 * HG + hg) * 4; }
+
 // The layer-1 biases of this thread's hidden units (constant over tiles).
 template <int HG>
 __device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __restrict__ b1,
                                            float (&bias)[kTH]) {
-  const int h0 = (threadIdx.x % HG) * kTH;
+  const int hg = layer1_hidden_group<HG>();
 #pragma unroll
-  for (int j = 0; j < kTH; ++j) bias[j] = (h0 + j < s.H) ? __ldg(b1 + h0 + j) : 0.0f;
+  for (int j = 0; j < kTH; ++j) {
+    const int h = layer1_unit(HG, hg, j / 4) + (j & 3);
+    bias[j] = h < s.H ? __ldg(b1 + h) : 0.0f;
+  }
 }
 
 template <int HG, int NT>
 __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
                                            const float (&bias)[kTH], const float* ft,
                                            float* w1s, float* hid) {
+  static_assert(HG % 8 == 0 && (NT / 32) % (HG / 8) == 0, "layer-1 thread layout");
   constexpr int RG = NT / HG;
   constexpr int M = RG * 8;
   const int t = threadIdx.x;
-  const int rg = t / HG;
-  const int hg = t - rg * HG;
-  const int h0 = hg * kTH;
+  const int rg = layer1_row_group<HG>();
+  const int hg = layer1_hidden_group<HG>();
   float acc[8][kTH];
 #pragma unroll
   for (int j = 0; j < kTH; ++j)
@@ -155,7 +178,6 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
     for (int i = 0; i < 8; ++i) acc[i][j] = bias[j];
   const float* arow = ft + rg * 8;
   if (s.w1_resident) {
-    const float* wcol = w1s + h0;
 #pragma unroll 1
     for (int k = 0; k < s.F; ++k) {
       const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
@@ -163,7 +185,7 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
       float4 bq[kTH / 4];
 #pragma unroll
       for (int j4 = 0; j4 < kTH / 4; ++j4)
-        bq[j4] = *reinterpret_cast<const float4*>(wcol + k * s.Hp + 4 * j4);
+        bq[j4] = *reinterpret_cast<const float4*>(w1s + k * s.Hp + layer1_unit(HG, hg, j4));
       micro_tile(acc, a0, a1, bq);
     }
   } else {
@@ -175,7 +197,6 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
       float4* dst = reinterpret_cast<float4*>(w1s);
       for (int e = t; e < kn * hp4; e += NT) dst[e] = __ldg(src + e);
       __syncthreads();
-      const float* wcol = w1s + h0;
       for (int kk = 0; kk < kn; ++kk) {
         const int k = kc + kk;
         const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
@@ -183,17 +204,17 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
         float4 bq[kTH / 4];
 #pragma unroll
         for (int j4 = 0; j4 < kTH / 4; ++j4)
-          bq[j4] = *reinterpret_cast<const float4*>(wcol + kk * s.Hp + 4 * j4);
+          bq[j4] = *reinterpret_cast<const float4*>(w1s + kk * s.Hp + layer1_unit(HG, hg, j4));
         micro_tile(acc, a0, a1, bq);
       }
     }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float* row = hid + (rg * 8 + i) * s.hid_stride + h0;
+    float* row = hid + (rg * 8 + i) * s.hid_stride;
 #pragma unroll
     for (int j4 = 0; j4 < kTH / 4; ++j4)
-      *reinterpret_cast<float4*>(row + 4 * j4) =
+      *reinterpret_cast<float4*>(row + layer1_unit(HG, hg, j4)) =
           make_float4(fmaxf(acc[i][4 * j4], 0.0f), fmaxf(acc[i][4 * j4 + 1], 0.0f),
                       fmaxf(acc[i][4 * j4 + 2], 0.0f), fmaxf(acc[i][4 * j4 + 3], 0.0f));
   }

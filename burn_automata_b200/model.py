@@ -127,28 +127,43 @@ class NpaModel:
 
         `outputs` selects which of the StepOutput extras are copied back (the
         reference always builds all of them); `out` = (next_positions,
-        next_states) reuses caller-owned float32 host arrays (pinned ones make
-        the copies asynchronous DMA)."""
+        next_states) or (next_positions, next_states, dx, ds, features,
+        density) reuses caller-owned float32 host arrays (None entries fall
+        back to `outputs`).  With page-locked buffers throughout, a batch of
+        several rollouts is stepped in rollout chunks whose copies overlap the
+        neighbouring chunks' kernels."""
         pos = _f32(positions).reshape(-1, 4) if np.size(positions) else np.zeros((0, 4), np.float32)
         st = _f32(states).reshape(-1)
         total = batch_size * particle_count
         C = self.config.state_dims
         F = self.config.perception_dims()
         mask = _f32(update_mask).reshape(-1) if update_mask is not None else None
+        sizes = {"next_positions": max(total, 0) * 4, "next_states": max(total * C, 0),
+                 "dx": max(total, 0) * 4, "ds": max(total * C, 0),
+                 "features": max(total * F, 0), "density": max(total, 0)}
+        given = {}
         if out is not None:
-            npos, nst = out
-            if (npos.dtype != np.float32 or nst.dtype != np.float32 or not npos.flags.c_contiguous
-                    or not nst.flags.c_contiguous or npos.size != max(total, 0) * 4
-                    or nst.size != max(total * C, 0)):
-                raise InvalidArgument("out buffers must be contiguous float32 of the step's size")
-        else:
-            npos = np.zeros((max(total, 0), 4), np.float32)
-            nst = np.zeros(max(total * C, 0), np.float32)
-        want = set(outputs or ())
-        dx = np.zeros((max(total, 0), 4), np.float32) if "dx" in want else None
-        ds = np.zeros(max(total * C, 0), np.float32) if "ds" in want else None
-        feats = np.zeros(max(total * F, 0), np.float32) if "features" in want else None
-        dens = np.zeros(max(total, 0), np.float32) if "density" in want else None
+            if len(out) not in (2, 6) or out[0] is None or out[1] is None:
+                raise InvalidArgument("out is (next_positions, next_states[, dx, ds, features, "
+                                      "density])")
+            given = {k: a for k, a in zip(sizes, out) if a is not None}
+            for k, a in given.items():
+                if (not isinstance(a, np.ndarray) or a.dtype != np.float32
+                        or not a.flags.c_contiguous or a.size != sizes[k]):
+                    raise InvalidArgument(f"out buffer {k} must be contiguous float32 of the "
+                                          "step's size")
+        want = set(outputs or ()) | {"next_positions", "next_states"}
+
+        def buf(k, shape):
+            if k in given:
+                return given[k]
+            return np.zeros(shape, np.float32) if k in want else None
+        npos = buf("next_positions", (max(total, 0), 4))
+        nst = buf("next_states", max(total * C, 0))
+        dx = buf("dx", (max(total, 0), 4))
+        ds = buf("ds", max(total * C, 0))
+        feats = buf("features", max(total * F, 0))
+        dens = buf("density", max(total, 0))
         g = _lib.grid_c(grid)
         _lib.check(_lib.lib().npa_model_step(
             self._handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],

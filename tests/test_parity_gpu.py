@@ -365,6 +365,43 @@ def test_host_perception_output_selection_and_out_buffers():
     np.testing.assert_array_equal(out[1], full.density)
 
 
+def _pinned_like(a):
+    import torch
+
+    p = torch.empty(a.size, dtype=torch.float32).pin_memory().numpy().reshape(a.shape)
+    p[...] = a
+    return p
+
+
+@pytest.mark.parametrize("batch", [67, 160])
+def test_host_step_pipelined_over_rollout_chunks(oracle_mod, batch):
+    """Page-locked buffers: the host step runs in rollout chunks (2 for 67
+    rollouts, split 33 / 34; 5 for 160) whose copies overlap the other chunks'
+    kernels.  Every output equals the one-chunk step of pageable buffers bit for
+    bit, and the first and last rollouts match the oracle."""
+    w = workloads.make("cfg2", batch=batch, steps=1)
+    m = make_model(w)
+    whole = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt)
+    pos, st = _pinned_like(w.positions), _pinned_like(w.states)
+    out = tuple(_pinned_like(np.full(a.shape, np.nan, np.float32))
+                for a in (whole.next_positions, whole.next_states, whole.dx, whole.ds,
+                          whole.features, whole.density))
+    r = m.step(pos, st, w.batch, w.n, w.grid, w.dt, out=out)
+    assert r.next_positions is out[0] and r.density is out[5]
+    for key in ("next_positions", "next_states", "dx", "ds", "features", "density"):
+        np.testing.assert_array_equal(getattr(r, key), getattr(whole, key), err_msg=key)
+    C = w.state_dims
+    for b in (0, batch - 1):
+        sub = workloads.make("cfg2", batch=1, steps=1, first=b)
+        ref = oracle_mod.step(sub.model, sub.weights, sub.grid, sub.positions, sub.states, 1,
+                              sub.n, sub.dt)
+        rows = slice(b * w.n, (b + 1) * w.n)
+        np.testing.assert_allclose(r.next_positions[rows], ref["next_positions"].reshape(-1, 4),
+                                   rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(r.next_states[b * w.n * C:(b + 1) * w.n * C],
+                                   ref["next_states"], rtol=RTOL, atol=ATOL)
+
+
 def test_host_step_reuses_buffers_across_sizes(oracle_mod):
     """Repeated host-buffer steps (growing and shrinking sizes) through the
     model's reusable device buffers match the oracle each time."""
