@@ -14,7 +14,7 @@ from .kernels import (DevicePerception, Gaussian3d, HashGridSnapshot, Perception
                       perceive_adjoint_with_options, perceive_state_adjoint_with_options,
                       perceive_with_options, splat_particles_2d)
 from .model import (CudaAutomataExecutor, NpaModel, NpaWeights, RolloutConfig, RolloutTrace,
-                    StepOutput, run_rollout_from_particles)
+                    StepOutput, rollout_update_masks, run_rollout_from_particles)
 from . import bpk
 from ._lib import build as build_library, lib as load_library
 
@@ -24,5 +24,6 @@ __all__ = [
     "feature_dims", "Gaussian3d", "HashGridSnapshot", "PerceptionOutput", "build_hashgrid",
     "decode_gaussians_3d", "decode_gaussians_3d_records", "euler_step", "perceive",
     "perceive_with_options", "CudaAutomataExecutor", "NpaModel", "NpaWeights", "RolloutConfig",
-    "RolloutTrace", "StepOutput", "run_rollout_from_particles", "build_library", "load_library",
+    "RolloutTrace", "StepOutput", "rollout_update_masks", "run_rollout_from_particles",
+    "build_library", "load_library",
 ]

@@ -93,6 +93,10 @@ SIGNATURES = [
      [vp, P(GridConfigC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, c_f32]),
     ("npa_model_run_rollout_trace", c_i32,
      [vp, P(GridConfigC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, c_f32, f32p]),
+    ("npa_model_run_rollout_seeded", c_i32,
+     [vp, P(GridConfigC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, c_f32, c_f32,
+      ctypes.c_uint64, f32p]),
+    ("npa_rollout_update_masks", c_i32, [ctypes.c_uint64, c_f32, c_i64, c_i64, c_i64, f32p]),
     ("npa_dev_hashgrid_workspace_size", c_i32, [P(GridConfigC), c_i64, c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_build_hashgrid", c_i32,
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp, ctypes.c_size_t, vp]),

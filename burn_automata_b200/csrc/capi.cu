@@ -1709,54 +1709,109 @@ npa_status npa_dev_splat_particles_2d(const npa_splat2d_config* cfg, const float
                          static_cast<cudaStream_t>(stream));
 }
 
-npa_status npa_model_run_rollout_trace(npa_model* m, const npa_grid_config* grid,
-                                       float* positions, int64_t positions_len, float* states,
-                                       int64_t states_len, int64_t batch, int64_t n,
-                                       int64_t steps, float dt, float* mean_dx) {
+// run_rollout_from_particles with the reference's StdRng masks when
+// update_prob < 1 (no mask otherwise) and mean_dx when it is not null.
+static npa_status run_rollout_impl(npa_model* m, const npa_grid_config* grid, float* positions,
+                                   int64_t positions_len, float* states, int64_t states_len,
+                                   int64_t batch, int64_t n, int64_t steps, float dt,
+                                   float update_prob, uint64_t seed, float* mean_dx) {
   if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
   NPA_TRY(check_step(m, grid));
   NPA_TRY(check_counts(batch, n));
   NPA_TRY(check_shapes(positions_len, states_len, batch, n, m->dm.state_dims));
   NPA_TRY(check_bins(grid, batch));
   if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
-  if (steps > 0 && !mean_dx) return fail(NPA_ERR_INVALID_ARGUMENT, "null mean_dx");
   const uint32_t total = uint32_t(batch * n);
   const int C = m->dm.state_dims;
   if (total > 0 && (!positions || (C > 0 && !states)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
   NPA_TRY(ensure_device(m->dm.device));
   if (total == 0) {
-    for (int64_t k = 0; k < steps; ++k) mean_dx[k] = 0.0f;  // 0 / max(len, 1)
+    if (mean_dx)
+      for (int64_t k = 0; k < steps; ++k) mean_dx[k] = 0.0f;  // 0 / max(len, 1)
     return NPA_OK;
   }
+  // stochastic_mask (rollout/mod.rs:644-651): ones without drawing when
+  // update_prob >= 1, so no mask is applied then.
+  const bool stochastic = !(update_prob >= 1.0f);
+  const ChachaKey key = stdrng_key(seed ^ 0x5eedull);
   size_t wsb = 0;
   NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
   Scratch sc;
   NPA_TRY(sc.init());
-  float4 *pos[2], *ddx;
-  float *st[2], *dmean;
-  double* partials;
+  float4 *pos[2], *ddx = nullptr;
+  float *st[2], *dmean = nullptr, *mask = nullptr;
+  double* partials = nullptr;
   char* ws;
   NPA_TRY(sc.upload(&pos[0], positions, total));
   NPA_TRY(sc.upload(&st[0], states, size_t(total) * C));
   NPA_TRY(sc.alloc(&pos[1], total));
   NPA_TRY(sc.alloc(&st[1], size_t(total) * C));
-  NPA_TRY(sc.alloc(&ddx, total));
-  NPA_TRY(sc.alloc(&dmean, size_t(std::max<int64_t>(steps, 1))));
-  NPA_TRY(sc.alloc(&partials, mean_norm_scratch_bytes() / sizeof(double)));
+  if (mean_dx) {
+    NPA_TRY(sc.alloc(&ddx, total));
+    NPA_TRY(sc.alloc(&dmean, size_t(std::max<int64_t>(steps, 1))));
+    NPA_TRY(sc.alloc(&partials, mean_norm_scratch_bytes() / sizeof(double)));
+  }
+  if (stochastic) NPA_TRY(sc.alloc(&mask, total));
   NPA_TRY(sc.alloc(&ws, wsb));
   int cur = 0;
   for (int64_t k = 0; k < steps; ++k) {
+    if (stochastic)
+      NPA_TRY(launch_stdrng_mask(key, uint64_t(k) * total, total, update_prob, mask, sc.stream));
     NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(pos[cur]), st[cur], batch, n, dt,
-                               nullptr, reinterpret_cast<float*>(pos[1 - cur]), st[1 - cur],
+                               mask, reinterpret_cast<float*>(pos[1 - cur]), st[1 - cur],
                                reinterpret_cast<float*>(ddx), nullptr, nullptr, nullptr, ws, wsb,
                                sc.stream));
-    NPA_TRY(launch_mean_norm(ddx, total, partials, dmean + k, sc.stream));
+    if (mean_dx) NPA_TRY(launch_mean_norm(ddx, total, partials, dmean + k, sc.stream));
     cur = 1 - cur;
   }
   NPA_TRY(sc.download(positions, pos[cur], size_t(total) * 16));
   NPA_TRY(sc.download(states, st[cur], size_t(total) * C * 4));
-  NPA_TRY(sc.download(mean_dx, dmean, size_t(steps) * 4));
+  if (mean_dx) NPA_TRY(sc.download(mean_dx, dmean, size_t(steps) * 4));
+  return sc.finish();
+}
+
+npa_status npa_model_run_rollout_trace(npa_model* m, const npa_grid_config* grid,
+                                       float* positions, int64_t positions_len, float* states,
+                                       int64_t states_len, int64_t batch, int64_t n,
+                                       int64_t steps, float dt, float* mean_dx) {
+  if (steps > 0 && !mean_dx) return fail(NPA_ERR_INVALID_ARGUMENT, "null mean_dx");
+  return run_rollout_impl(m, grid, positions, positions_len, states, states_len, batch, n, steps,
+                          dt, 1.0f, 0, mean_dx);
+}
+
+npa_status npa_model_run_rollout_seeded(npa_model* m, const npa_grid_config* grid,
+                                        float* positions, int64_t positions_len, float* states,
+                                        int64_t states_len, int64_t batch, int64_t n,
+                                        int64_t steps, float dt, float update_prob, uint64_t seed,
+                                        float* mean_dx) {
+  return run_rollout_impl(m, grid, positions, positions_len, states, states_len, batch, n, steps,
+                          dt, update_prob, seed, mean_dx);
+}
+
+npa_status npa_rollout_update_masks(uint64_t seed, float update_prob, int64_t count,
+                                    int64_t first_step, int64_t steps, float* masks) {
+  if (count < 0 || steps < 0 || first_step < 0)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "count, first_step and steps must be >= 0");
+  if (count > int64_t(kMaxParticles)) return fail(NPA_ERR_UNSUPPORTED, "too many particles");
+  const size_t len = size_t(count) * size_t(steps);
+  if (len == 0) return NPA_OK;
+  if (!masks) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  if (update_prob >= 1.0f) {
+    for (size_t i = 0; i < len; ++i) masks[i] = 1.0f;
+    return NPA_OK;
+  }
+  int dev = 0;
+  NPA_TRY(current_device(&dev));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float* d;
+  NPA_TRY(sc.alloc(&d, len));
+  const ChachaKey key = stdrng_key(seed ^ 0x5eedull);
+  for (int64_t k = 0; k < steps; ++k)
+    NPA_TRY(launch_stdrng_mask(key, uint64_t(first_step + k) * uint64_t(count), uint32_t(count),
+                               update_prob, d + size_t(k) * count, sc.stream));
+  NPA_TRY(sc.download(masks, d, len * 4));
   return sc.finish();
 }
 

@@ -169,6 +169,16 @@ npa_status launch_splat_2d(const npa_splat2d_config& cfg, const float4* position
                            const float* colors, uint32_t count, float4* out, void* workspace,
                            cudaStream_t stream);
 
+// ---- the CPU rollout's StdRng update masks (stdrng.cu) ----
+struct ChachaKey {
+  uint32_t k[8];
+};
+// StdRng::seed_from_u64(rng_seed) as ChaCha12 key words.
+ChachaKey stdrng_key(uint64_t rng_seed);
+// mask[i] = (stream word word0 + i, as random::<f32>()) < update_prob, i < count.
+npa_status launch_stdrng_mask(const ChachaKey& key, uint64_t word0, uint32_t count,
+                              float update_prob, float* mask, cudaStream_t stream);
+
 // ---- decode (decode.cu) ----
 npa_status launch_decode(const npa_gaussian_decode_config& cfg, const float4* positions,
                          const float* states, uint32_t count, int state_dims, float* out,

@@ -203,21 +203,33 @@ class RolloutTrace:
 
 def run_rollout_from_particles(model: NpaModel, grid: HashGridConfig, cfg: RolloutConfig,
                                positions, states) -> RolloutTrace:
-    """rollout/mod.rs:201-283 for update_prob >= 1 (the all-ones mask).  The
-    reference's stochastic masks draw from Rust's StdRng and are not
-    reproducible here, so update_prob < 1 is rejected."""
-    if cfg.update_prob < 1.0:
-        raise InvalidArgument("update_prob < 1 needs the reference's StdRng mask stream")
+    """rollout/mod.rs:222-283: cfg.steps steps from the given particles.  With
+    update_prob < 1 every step's update is masked by the reference's
+    stochastic_mask stream (StdRng seeded with cfg.seed ^ 0x5eed; see
+    rollout_update_masks)."""
     pos = _f32(positions).reshape(-1, 4).copy()
     st = _f32(states).reshape(-1).copy()
     g = _lib.grid_c(grid)
     mean_dx = np.zeros(max(cfg.steps, 1), np.float32)
-    _lib.check(_lib.lib().npa_model_run_rollout_trace(
+    _lib.check(_lib.lib().npa_model_run_rollout_seeded(
         model.handle, ctypes.byref(g), _fp(pos), pos.shape[0], _fp(st), st.shape[0],
-        cfg.batch_size, cfg.particle_count, cfg.steps, float(cfg.dt), _fp(mean_dx)),
-        "run_rollout")
+        cfg.batch_size, cfg.particle_count, cfg.steps, float(cfg.dt), float(cfg.update_prob),
+        int(cfg.seed) & 0xFFFFFFFFFFFFFFFF, _fp(mean_dx)), "run_rollout")
     return RolloutTrace(pos, st, cfg.batch_size, cfg.particle_count, model.config.state_dims,
                         cfg.steps, mean_dx[:cfg.steps])
+
+
+def rollout_update_masks(seed: int, update_prob: float, count: int, steps: int,
+                         first_step: int = 0) -> np.ndarray:
+    """stochastic_mask (rollout/mod.rs:644-651) as run_rollout_from_particles
+    with cfg.seed = seed draws it: [steps, count] for steps first_step.. (0-based).
+    The stream is rand 0.9's StdRng (ChaCha12) seeded by seed_from_u64(seed ^
+    0x5eed), restated and computed on the GPU."""
+    out = np.zeros((steps, count), np.float32)
+    _lib.check(_lib.lib().npa_rollout_update_masks(int(seed) & 0xFFFFFFFFFFFFFFFF,
+                                                   float(update_prob), count, first_step, steps,
+                                                   _fp(out)), "rollout_update_masks")
+    return out
 
 
 class CudaAutomataExecutor:

@@ -255,6 +255,25 @@ npa_status npa_model_run_rollout_trace(npa_model* model, const npa_grid_config* 
                                        int64_t states_len, int64_t batch, int64_t n,
                                        int64_t steps, float dt, float* mean_dx);
 
+/* run_rollout_from_particles (crates/burn_automata/src/rollout/mod.rs:222-238)
+ * for any update_prob: the reference seeds StdRng::seed_from_u64(seed ^ 0x5eed)
+ * and multiplies every step's update by stochastic_mask (:644-651),
+ * random::<f32>() < update_prob per particle in index order (no mask when
+ * update_prob >= 1).  StdRng is rand 0.9.4's ChaCha12Rng; the masks are that
+ * stream (restated: rand_core 0.9 seed_from_u64, ChaCha12, rand's 24-bit f32),
+ * computed on the GPU.  mean_dx (steps entries) may be null. */
+npa_status npa_model_run_rollout_seeded(npa_model* model, const npa_grid_config* grid,
+                                        float* positions, int64_t positions_len, float* states,
+                                        int64_t states_len, int64_t batch, int64_t n,
+                                        int64_t steps, float dt, float update_prob,
+                                        uint64_t seed, float* mean_dx);
+
+/* The masks npa_model_run_rollout_seeded (run_rollout_from_particles with
+ * cfg.seed = seed) applies in steps [first_step, first_step + steps), 0-based:
+ * masks[k * count + i] for step first_step + k, particle i < count. */
+npa_status npa_rollout_update_masks(uint64_t seed, float update_prob, int64_t count,
+                                    int64_t first_step, int64_t steps, float* masks);
+
 /* perceive_adjoint_with_options
  * (crates/burn_automata_kernels/src/reference/adjoint.rs:28-136): given the
  * adjoint of the perception features [B*N][F] (F as perceive_with_options),

@@ -162,6 +162,10 @@ def lib():
         L.ora_splat_particles_2d.argtypes = [P(_Splat), f32p, f32p, i64, f32p]
         L.ora_perceive_adjoint.argtypes = [P(_Grid), P(_Opt), f32p, f32p, i64, i64, i64, f32p,
                                            f32p, f32p]
+        u32p = P(ctypes.c_uint32)
+        L.ora_stdrng_key.argtypes = [ctypes.c_uint64, u32p]
+        L.ora_chacha_block.argtypes = [u32p, ctypes.c_uint64, ctypes.c_int, u32p]
+        L.ora_rollout_masks.argtypes = [ctypes.c_uint64, ctypes.c_float, i64, i64, i64, f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
@@ -370,6 +374,35 @@ def gpu_update_masks(batch: int, n: int, update_prob: float, steps: int, seed: i
                                          (first_step + k) & 0xFFFFFFFF,
                                          seeds.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
                                          _ptr(out[k])), "gpu_update_mask")
+    return out
+
+
+def stdrng_key(rng_seed: int) -> np.ndarray:
+    """rand_core 0.9 seed_from_u64 as the ChaCha key words (parity unpinned)."""
+    key = np.zeros(8, np.uint32)
+    lib().ora_stdrng_key(int(rng_seed) & 0xFFFFFFFFFFFFFFFF,
+                         key.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return key
+
+
+def chacha_block(key, counter: int, rounds: int) -> np.ndarray:
+    """One ChaCha block (64-bit counter in words 12-13, stream 0) as 16 words."""
+    k = np.ascontiguousarray(key, np.uint32)
+    out = np.zeros(16, np.uint32)
+    u32p = ctypes.POINTER(ctypes.c_uint32)
+    lib().ora_chacha_block(k.ctypes.data_as(u32p), int(counter), int(rounds),
+                           out.ctypes.data_as(u32p))
+    return out
+
+
+def rollout_masks(rollout_seed: int, update_prob: float, count: int, steps: int,
+                  first_step: int = 0) -> np.ndarray:
+    """The masks run_rollout_from_particles (rollout/mod.rs:222-238) draws for
+    `steps` steps from step `first_step` (0-based): [steps, count].  Restated
+    StdRng stream; parity unpinned (no Rust, no golden values)."""
+    out = np.zeros((steps, count), np.float32)
+    _check(lib().ora_rollout_masks(int(rollout_seed) & 0xFFFFFFFFFFFFFFFF, float(update_prob),
+                                   count, first_step, steps, _ptr(out)), "rollout_masks")
     return out
 
 

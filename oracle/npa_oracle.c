@@ -939,6 +939,89 @@ int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t st
   return ORA_OK;
 }
 
+/* ---- the CPU rollout's StdRng update masks (rollout/mod.rs:222-238, :644-651) ----
+ * Restated third-party algorithms (crates absent from the reference tree; the
+ * versions are its Cargo.lock's):
+ *   rand_core 0.9 SeedableRng::seed_from_u64: a PCG32 generator (O'Neill 2014,
+ *     XSH-RR 64/32 output) whose 64-bit LCG state (multiplier
+ *     6364136223846793005, increment 11634580027462260723) is stepped before
+ *     each output; eight outputs, little-endian, are the 32-byte seed.
+ *   rand_chacha 0.9.0 ChaCha12Rng::from_seed: Bernstein's ChaCha with 12
+ *     rounds; words 0-3 the "expand 32-byte k" constants, 4-11 the seed as
+ *     little-endian words, 12-13 a 64-bit block counter from 0, 14-15 the
+ *     stream (0).  The generator's u32 outputs are the blocks' 16 words in
+ *     order, blocks in counter order.
+ *   rand 0.9.4 random::<f32>() (StandardUniform): (next_u32() >> 8) * 2^-24.
+ * stochastic_mask draws one value per particle in index order, so the mask of
+ * rollout step s (0-based) for particle i uses stream word s * count + i; with
+ * update_prob >= 1 it returns ones and draws nothing. */
+static uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+void ora_stdrng_key(uint64_t rng_seed, uint32_t key[8]) {
+  uint64_t state = rng_seed;
+  for (int k = 0; k < 8; ++k) {
+    state = state * 6364136223846793005ull + 11634580027462260723ull;
+    const uint32_t xorshifted = (uint32_t)(((state >> 18) ^ state) >> 27);
+    const uint32_t rot = (uint32_t)(state >> 59);
+    key[k] = (xorshifted >> rot) | (xorshifted << ((32 - rot) & 31));
+  }
+}
+
+#define ORA_QR(a, b, c, d)                \
+  do {                                    \
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 16); \
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 12); \
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 8);  \
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 7);  \
+  } while (0)
+
+void ora_chacha_block(const uint32_t key[8], uint64_t counter, int rounds, uint32_t out[16]) {
+  uint32_t in[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u};
+  for (int k = 0; k < 8; ++k) in[4 + k] = key[k];
+  in[12] = (uint32_t)counter;
+  in[13] = (uint32_t)(counter >> 32);
+  in[14] = 0;
+  in[15] = 0;
+  uint32_t x[16];
+  memcpy(x, in, sizeof(x));
+  for (int r = 0; r < rounds; r += 2) {
+    ORA_QR(0, 4, 8, 12);
+    ORA_QR(1, 5, 9, 13);
+    ORA_QR(2, 6, 10, 14);
+    ORA_QR(3, 7, 11, 15);
+    ORA_QR(0, 5, 10, 15);
+    ORA_QR(1, 6, 11, 12);
+    ORA_QR(2, 7, 8, 13);
+    ORA_QR(3, 4, 9, 14);
+  }
+  for (int k = 0; k < 16; ++k) out[k] = x[k] + in[k];
+}
+#undef ORA_QR
+
+int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
+                      int64_t first_step, int64_t steps, float* out) {
+  if (count < 0 || steps < 0 || first_step < 0) return ORA_ERR_INVALID_ARGUMENT;
+  if (update_prob >= 1.0f) {
+    for (int64_t i = 0; i < count * steps; ++i) out[i] = 1.0f;
+    return ORA_OK;
+  }
+  uint32_t key[8], block[16];
+  ora_stdrng_key(rollout_seed ^ 0x5eedull, key);
+  uint64_t have = UINT64_MAX;
+  for (int64_t k = 0; k < steps; ++k) {
+    for (int64_t i = 0; i < count; ++i) {
+      const uint64_t w = (uint64_t)(first_step + k) * (uint64_t)count + (uint64_t)i;
+      if (w / 16 != have) {
+        have = w / 16;
+        ora_chacha_block(key, have, 12, block);
+      }
+      const float u = (float)(block[w % 16] >> 8) * (1.0f / 16777216.0f);
+      out[k * count + i] = u < update_prob ? 1.0f : 0.0f;
+    }
+  }
+  return ORA_OK;
+}
+
 /* ---- splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93) ----
  * Each particle adds colour * w to the pixels of its (2r+1)^2 footprint, with
  * w = exp(-(dx^2 + dy^2) / (2 sigma^2)) / (footprint weight sum) * norm_scale

@@ -16,6 +16,8 @@
  *   crates/burn_automata/src/config.rs:133-162          (NpaConfig dims / eps)
  *   crates/burn_automata/src/model.rs:768-940           (step_cpu, MLP)
  *   crates/burn_automata/src/rollout/mod.rs:240-283     (rollout loop)
+ *   crates/burn_automata/src/rollout/mod.rs:222-238, :644-651 (StdRng masks;
+ *     rand 0.9.4 / rand_chacha 0.9.0 / rand_core 0.9 restated, PARITY UNPINNED)
  * Each function in npa_oracle.c cites the file:line it follows.
  *
  * Index arrays are int64 (the reference uses usize).  Status codes are the
@@ -157,7 +159,6 @@ int ora_decode_gaussians(const ora_decode_config* cfg, const float* positions,
                          const float* states, int64_t count, int64_t state_dims,
                          float* out);
 
-/* Threads used by the OpenMP loops (0 = OpenMP default). */
 /* The GPU executor's stochastic update mask for one step: out[lane * n + i]
  * (gpu_step.wgsl:1019-1056; tests/gpu_wgpu/common.rs:115-137). */
 int ora_gpu_update_mask(int64_t batch, int64_t n, float update_prob, uint32_t step,
@@ -178,6 +179,19 @@ typedef struct ora_splat2d_config {
 /* splat_particles_2d (splat.rs:30-93): out [size * size][4] (RGB + weight). */
 int ora_splat_particles_2d(const ora_splat2d_config* cfg, const float* positions,
                            const float* colors, int64_t count, float* out);
+/* The CPU rollout's update masks (rollout/mod.rs:222-238 seeds
+ * StdRng::seed_from_u64(seed ^ 0x5eed); stochastic_mask :644-651 draws
+ * random::<f32>() < update_prob per particle and step).  StdRng is rand 0.9.4's
+ * ChaCha12Rng (rand_chacha 0.9.0) seeded by rand_core 0.9's seed_from_u64;
+ * see npa_oracle.c for the restated algorithms.  PARITY UNPINNED for the
+ * seeding and the 12-round stream (no Rust toolchain, no golden values); the
+ * block function is checked at 20 rounds against OpenSSL's ChaCha20. */
+void ora_stdrng_key(uint64_t rng_seed, uint32_t key[8]);
+void ora_chacha_block(const uint32_t key[8], uint64_t counter, int rounds, uint32_t out[16]);
+/* out[k * count + i] for rollout steps first_step + k (0-based), k < steps. */
+int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
+                      int64_t first_step, int64_t steps, float* out);
+/* Threads used by the OpenMP loops (0 = OpenMP default). */
 void ora_set_threads(int threads);
 int ora_get_threads(void);
 
