@@ -12,8 +12,9 @@ cfg4  Gaussian-mixture 2D cluster, 4,194,304 particles, C=16, cfg0 MLP
 
 Model weights are Kaiming-normal (std = sqrt(2 / fan_in)) with zero biases.
 The reference's own initialisers (uniform / Xavier, model.rs:29-63) draw from
-Rust's StdRng, which cannot be reproduced without Rust; the weights are an
-input, identical for the oracle and the GPU.
+Rust's StdRng through rand's distributions, with no golden values to check a
+restatement against; the weights are an input, identical for the oracle and
+the GPU.
 """
 
 from __future__ import annotations
