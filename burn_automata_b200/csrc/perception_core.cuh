@@ -22,14 +22,22 @@ struct PerceptionAcc {
   float dgrad[DIM];
 };
 
+// log1p(norm) / norm of a squared norm s (normalize.rs:60-69).  Out of line:
+// one copy of the f64 log1p, square root and division serves every channel;
+// inlined per channel they crowded the perception kernels out of the
+// instruction cache (measured 0.437 -> 0.406 ms on cfg2's perception).
+__device__ __noinline__ float log_norm_scale(float s) {
+  const float e = 1.0e-6f;
+  const float norm = fmaxf(sqrtf(s + e * e), e);
+  return log1p_f32(norm) / norm;
+}
+
 template <int DIM>
 __device__ __forceinline__ void log_normalize_n(float (&v)[DIM]) {
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < DIM; ++i) s = s + v[i] * v[i];
-  const float e = 1.0e-6f;
-  const float norm = fmaxf(sqrtf(s + e * e), e);
-  const float scale = log1p_f32(norm) / norm;
+  const float scale = log_norm_scale(s);
 #pragma unroll
   for (int i = 0; i < DIM; ++i) v[i] = v[i] * scale;
 }
