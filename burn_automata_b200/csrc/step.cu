@@ -224,6 +224,8 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
 // two rows per thread: 2 * tpr threads per row pair, thread j owning outputs
 // o = j + 2 tpr u (u in [u0, u0 + NOUT)) of both rows; each weight load
 // serves both rows.  Outputs past O are computed on a valid row, not stored.
+// Pair p holds rows p and p + M / 2, so the eight rows a warp reads at one h
+// fall in distinct shared-memory banks (rows 2p, 2p + 1 conflicted two-way).
 template <int NOUT>
 __device__ __forceinline__ void mlp_layer2_pair(const MlpShape& s, const float* __restrict__ b2,
                                                 const float* hid, const float* w2s, float* outs,
@@ -233,25 +235,28 @@ __device__ __forceinline__ void mlp_layer2_pair(const MlpShape& s, const float* 
   const int rp = t / tpp;
   const int j = t - rp * tpp;
   float acc0[NOUT], acc1[NOUT];
-  const float* wrow[NOUT];
+  int woff[NOUT];
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
     const int o = j + tpp * (u0 + u);
     const int oo = o < s.O ? o : 0;
     acc0[u] = __ldg(b2 + oo);
     acc1[u] = acc0[u];
-    wrow[u] = w2s + oo * s.w2_stride;
+    woff[u] = oo * s.w2_stride;
   }
-  const float* h0row = hid + (2 * rp) * s.hid_stride;
-  const float* h1row = h0row + s.hid_stride;
+  const int npairs = s.M / 2;
+  const int r0 = rp, r1 = rp + npairs;
+  const float* h0row = hid + r0 * s.hid_stride;
+  const float* h1row = hid + r1 * s.hid_stride;
   const int H4 = s.H & ~3;
+#pragma unroll 2
   for (int h = 0; h < H4; h += 4) {
     const float4 hv0 = *reinterpret_cast<const float4*>(h0row + h);
     const float4 hv1 = *reinterpret_cast<const float4*>(h1row + h);
     float p0[NOUT][4], p1[NOUT][4];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
-      const float4 w = *reinterpret_cast<const float4*>(wrow[u] + h);
+      const float4 w = *reinterpret_cast<const float4*>(w2s + woff[u] + h);
       p0[u][0] = w.x * hv0.x;
       p0[u][1] = w.y * hv0.y;
       p0[u][2] = w.z * hv0.z;
@@ -273,16 +278,16 @@ __device__ __forceinline__ void mlp_layer2_pair(const MlpShape& s, const float* 
     const float hv0 = h0row[h], hv1 = h1row[h];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
-      acc0[u] = acc0[u] + wrow[u][h] * hv0;
-      acc1[u] = acc1[u] + wrow[u][h] * hv1;
+      acc0[u] = acc0[u] + w2s[woff[u] + h] * hv0;
+      acc1[u] = acc1[u] + w2s[woff[u] + h] * hv1;
     }
   }
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
     const int o = j + tpp * (u0 + u);
     if (o < s.O) {
-      outs[(2 * rp) * s.out_stride + o] = acc0[u];
-      outs[(2 * rp + 1) * s.out_stride + o] = acc1[u];
+      outs[r0 * s.out_stride + o] = acc0[u];
+      outs[r1 * s.out_stride + o] = acc1[u];
     }
   }
 }
