@@ -39,7 +39,7 @@ constexpr int kThreadsWide = 384;    // 12 warps per SM: 3 per scheduler
 constexpr int kThreadsNarrow = 256;  // when the wide tile does not fit in shared memory
 constexpr int kTH = 8;         // hidden units per thread in layer 1
 constexpr int kKC = 16;              // k slice when w1 is streamed
-constexpr int kMaxOut = 64;          // outputs per row-owning thread (layer 2 runs in passes of kL2Chunk)
+constexpr int kMaxOut = 64;          // outputs per row-owning thread (layer 2 runs in passes)
 constexpr size_t kSmemBudget = 220 * 1024;
 
 struct MlpShape {
@@ -51,6 +51,7 @@ struct MlpShape {
   int w2_stride;   // Hp + 4
   int out_stride;  // O + 1
   int w1_resident; // w1^T [F][Hp] kept in shared memory for the whole kernel
+  int l2_rows;     // layer-2 rows per thread: 2, or 3 when M splits into triples with less waste
 };
 
 struct SmemLayout {
@@ -220,88 +221,90 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
   }
 }
 
-// Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h,
-// two rows per thread: 2 * tpr threads per row pair, thread j owning outputs
-// o = j + 2 tpr u (u in [u0, u0 + NOUT)) of both rows; each weight load
-// serves both rows.  Outputs past O are computed on a valid row, not stored.
-// Pair p holds rows p and p + M / 2, so the eight rows a warp reads at one h
-// fall in distinct shared-memory banks (rows 2p, 2p + 1 conflicted two-way).
-template <int NOUT>
-__device__ __forceinline__ void mlp_layer2_pair(const MlpShape& s, const float* __restrict__ b2,
+// Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
+// R rows per thread: R * tpr threads per row group, thread j owning outputs
+// o = j + R tpr u (u in [u0, u0 + NOUT)) of the group's R rows; each weight
+// load serves R rows.  Group g holds rows g + i M / R (i < R), so the rows a
+// warp reads at one h fall in distinct shared-memory banks.  Outputs past O
+// are computed on a valid row, not stored.
+template <int R, int NOUT>
+__device__ __forceinline__ void mlp_layer2_rows(const MlpShape& s, const float* __restrict__ b2,
                                                 const float* hid, const float* w2s, float* outs,
                                                 int u0) {
-  const int tpp = 2 * s.tpr;
+  const int tpg = R * s.tpr;
   const int t = threadIdx.x;
-  const int rp = t / tpp;
-  const int j = t - rp * tpp;
-  float acc0[NOUT], acc1[NOUT];
+  const int rg = t / tpg;
+  const int j = t - rg * tpg;
+  const int ngroups = s.M / R;
+  float acc[R][NOUT];
   int woff[NOUT];
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
-    const int o = j + tpp * (u0 + u);
+    const int o = j + tpg * (u0 + u);
     const int oo = o < s.O ? o : 0;
-    acc0[u] = __ldg(b2 + oo);
-    acc1[u] = acc0[u];
+    const float bias = __ldg(b2 + oo);
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i][u] = bias;
     woff[u] = oo * s.w2_stride;
   }
-  const int npairs = s.M / 2;
-  const int r0 = rp, r1 = rp + npairs;
-  const float* h0row = hid + r0 * s.hid_stride;
-  const float* h1row = hid + r1 * s.hid_stride;
+  int hoff[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) hoff[i] = (rg + i * ngroups) * s.hid_stride;
   const int H4 = s.H & ~3;
 #pragma unroll 2
   for (int h = 0; h < H4; h += 4) {
-    const float4 hv0 = *reinterpret_cast<const float4*>(h0row + h);
-    const float4 hv1 = *reinterpret_cast<const float4*>(h1row + h);
-    float p0[NOUT][4], p1[NOUT][4];
+    float4 hv[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) hv[i] = *reinterpret_cast<const float4*>(hid + hoff[i] + h);
+    float p[R][NOUT][4];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
       const float4 w = *reinterpret_cast<const float4*>(w2s + woff[u] + h);
-      p0[u][0] = w.x * hv0.x;
-      p0[u][1] = w.y * hv0.y;
-      p0[u][2] = w.z * hv0.z;
-      p0[u][3] = w.w * hv0.w;
-      p1[u][0] = w.x * hv1.x;
-      p1[u][1] = w.y * hv1.y;
-      p1[u][2] = w.z * hv1.z;
-      p1[u][3] = w.w * hv1.w;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        p[i][u][0] = w.x * hv[i].x;
+        p[i][u][1] = w.y * hv[i].y;
+        p[i][u][2] = w.z * hv[i].z;
+        p[i][u][3] = w.w * hv[i].w;
+      }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int u = 0; u < NOUT; ++u) {
-        acc0[u] = acc0[u] + p0[u][k];
-        acc1[u] = acc1[u] + p1[u][k];
-      }
+      for (int u = 0; u < NOUT; ++u)
+#pragma unroll
+        for (int i = 0; i < R; ++i) acc[i][u] = acc[i][u] + p[i][u][k];
   }
   for (int h = H4; h < s.H; ++h) {
-    const float hv0 = h0row[h], hv1 = h1row[h];
 #pragma unroll
     for (int u = 0; u < NOUT; ++u) {
-      acc0[u] = acc0[u] + w2s[woff[u] + h] * hv0;
-      acc1[u] = acc1[u] + w2s[woff[u] + h] * hv1;
+      const float w = w2s[woff[u] + h];
+#pragma unroll
+      for (int i = 0; i < R; ++i) acc[i][u] = acc[i][u] + w * hid[hoff[i] + h];
     }
   }
 #pragma unroll
   for (int u = 0; u < NOUT; ++u) {
-    const int o = j + tpp * (u0 + u);
+    const int o = j + tpg * (u0 + u);
     if (o < s.O) {
-      outs[r0 * s.out_stride + o] = acc0[u];
-      outs[r1 * s.out_stride + o] = acc1[u];
+#pragma unroll
+      for (int i = 0; i < R; ++i) outs[(rg + i * ngroups) * s.out_stride + o] = acc[i][u];
     }
   }
 }
 
-// Outputs per thread per pass over the hidden rows (bounds the accumulators' registers).
-constexpr int kL2Chunk = 8;
-__device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
-                                               const float* hid, const float* w2s, float* outs) {
-  const int per_thread = (s.O + 2 * s.tpr - 1) / (2 * s.tpr);
-  for (int u0 = 0; u0 < per_thread; u0 += kL2Chunk) {
-    switch (min(kL2Chunk, per_thread - u0)) {
-#define NPA_L2(N) \
-  case N:         \
-    mlp_layer2_pair<N>(s, b2, hid, w2s, outs, u0); \
+// Outputs per thread per pass over the hidden rows (bounds the products'
+// registers: R * NOUT * 4 of them).
+template <int R>
+__device__ __forceinline__ void mlp_layer2_r(const MlpShape& s, const float* __restrict__ b2,
+                                             const float* hid, const float* w2s, float* outs) {
+  constexpr int kChunk = R == 2 ? 8 : 4;
+  const int per_thread = (s.O + R * s.tpr - 1) / (R * s.tpr);
+  for (int u0 = 0; u0 < per_thread; u0 += kChunk) {
+    switch (min(kChunk, per_thread - u0)) {
+#define NPA_L2(N)                                                  \
+  case N:                                                          \
+    if constexpr (N <= kChunk) mlp_layer2_rows<R, N>(s, b2, hid, w2s, outs, u0); \
     break;
       NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
 #undef NPA_L2
@@ -309,6 +312,14 @@ __device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* _
         break;
     }
   }
+}
+
+__device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
+                                               const float* hid, const float* w2s, float* outs) {
+  if (s.l2_rows == 3)
+    mlp_layer2_r<3>(s, b2, hid, w2s, outs);
+  else
+    mlp_layer2_r<2>(s, b2, hid, w2s, outs);
 }
 
 // API MLP: rows of the caller's row-major feature matrix.
@@ -548,6 +559,13 @@ MlpShape shape_with(const DeviceModel& m, int nt) {
   s.out_stride = s.O + 1;
   s.w1_resident = 1;
   if (smem_layout(s).total * sizeof(float) > kSmemBudget) s.w1_resident = 0;
+  // Layer-2 output slots per row: R tpr ceil(O / (R tpr)).  Triples when M
+  // splits into them, they waste no more slots than pairs, and a row group's
+  // R tpr threads read at most 8 distinct weight rows (8 x 16 bytes: one
+  // shared-memory wavefront per load).  Measured: cfg2 (tpr 2) MLP 0.927 vs
+  // 0.954 ms with triples; cfg3 (tpr 4, 12 weight rows) 0.0996 vs 0.0983 ms.
+  auto slots = [&](int r) { return r * s.tpr * ((s.O + r * s.tpr - 1) / (r * s.tpr)); };
+  s.l2_rows = (s.M % 3 == 0 && 3 * s.tpr <= 8 && slots(3) <= slots(2)) ? 3 : 2;
   return s;
 }
 
