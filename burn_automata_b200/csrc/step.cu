@@ -418,7 +418,8 @@ struct StepParams {
 };
 
 // Own-state channels a thread keeps in registers between layer 1 and the
-// epilogue (the rest, C > kStateRegs * threads per row, are read there).
+// epilogue (each of a row's threads owns a contiguous run of ceil(C / TPR)
+// channels; beyond kStateRegs of them the rest are read in the epilogue).
 constexpr int kStateRegs = 8;
 
 // The rollout step's MLP stage over feature tiles in sorted order.
@@ -458,6 +459,14 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   const int r = threadIdx.x / TPR;
   const int part = threadIdx.x - r * TPR;
   const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
+  // Each of a row's TPR threads owns a contiguous run of cpt channels, read
+  // and written as float4 when the rows are 16-byte aligned.
+  const int cpt = (C + TPR - 1) / TPR;
+  const int c0 = part * cpt;
+  const int cend = min(C, c0 + cpt);
+  const bool vec = (C % 4 == 0) && (cpt % 4 == 0) && cpt <= kStateRegs &&
+                   ((reinterpret_cast<uintptr_t>(sp.states) | reinterpret_cast<uintptr_t>(next_states) |
+                     reinterpret_cast<uintptr_t>(ds_out)) & 15u) == 0;
   for (; tile < tiles; tile += gridDim.x) {
     cp_async_wait<0>();
     __syncthreads();
@@ -484,10 +493,22 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
     __syncthreads();
     // own state for the Euler update, hidden behind layer 2
     float sv[kStateRegs];
+    if (vec) {
 #pragma unroll
-    for (int j = 0; j < kStateRegs; ++j) {
-      const int ch = part + j * TPR;
-      sv[j] = (live && ch < C) ? __ldg(sp.states + row * C + ch) : 0.0f;
+      for (int j4 = 0; j4 < kStateRegs / 4; ++j4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live && 4 * j4 < cpt) v = __ldg(reinterpret_cast<const float4*>(sp.states + row * C + c0) + j4);
+        sv[4 * j4] = v.x;
+        sv[4 * j4 + 1] = v.y;
+        sv[4 * j4 + 2] = v.z;
+        sv[4 * j4 + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kStateRegs; ++j) {
+        const int ch = c0 + j;
+        sv[j] = (live && ch < cend) ? __ldg(sp.states + row * C + ch) : 0.0f;
+      }
     }
     float liveness = 0.0f, sd = 0.0f;
     if (sp.gates3d && live) {
@@ -523,17 +544,40 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
         next_pos[row] = euler_position(g, ep, pi, dx, m);
         if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
       }
+      float nsv[kStateRegs], dsa[kStateRegs];
 #pragma unroll
       for (int j = 0; j < kStateRegs; ++j) {
-        const int ch = part + j * TPR;
-        if (ch < C) {
+        const int ch = c0 + j;
+        nsv[j] = 0.0f;
+        dsa[j] = 0.0f;
+        if (ch < cend) {
           float dsv = u[D + ch];
           if (sp.gates3d) dsv = dsv * state_gate;
-          next_states[row * C + ch] = euler_state(ep, C, ch, sv[j], dsv, m);
-          if (ds_out) ds_out[row * C + ch] = dsv;
+          nsv[j] = euler_state(ep, C, ch, sv[j], dsv, m);
+          dsa[j] = dsv;
         }
       }
-      for (int ch = part + kStateRegs * TPR; ch < C; ch += TPR) {
+      if (vec) {
+#pragma unroll
+        for (int j4 = 0; j4 < kStateRegs / 4; ++j4)
+          if (4 * j4 < cpt) {
+            reinterpret_cast<float4*>(next_states + row * C + c0)[j4] =
+                make_float4(nsv[4 * j4], nsv[4 * j4 + 1], nsv[4 * j4 + 2], nsv[4 * j4 + 3]);
+            if (ds_out)
+              reinterpret_cast<float4*>(ds_out + row * C + c0)[j4] =
+                  make_float4(dsa[4 * j4], dsa[4 * j4 + 1], dsa[4 * j4 + 2], dsa[4 * j4 + 3]);
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kStateRegs; ++j) {
+          const int ch = c0 + j;
+          if (ch < cend) {
+            next_states[row * C + ch] = nsv[j];
+            if (ds_out) ds_out[row * C + ch] = dsa[j];
+          }
+        }
+      }
+      for (int ch = c0 + kStateRegs; ch < cend; ++ch) {
         float dsv = u[D + ch];
         if (sp.gates3d) dsv = dsv * state_gate;
         next_states[row * C + ch] = euler_state(ep, C, ch, __ldg(sp.states + row * C + ch), dsv, m);
