@@ -59,10 +59,12 @@ __device__ __forceinline__ uint32_t mix_coord(int value_low32, uint32_t salt) {
   return x;
 }
 
-// particle_cell_hash (hashgrid.rs:147-153).
+// particle_cell_hash (hashgrid.rs:147-153).  DIM: the grid's dimension when
+// the caller knows it at compile time (equal to g.dim), 0 to read g.dim.
+template <int DIM = 0>
 __device__ __forceinline__ uint32_t particle_cell_hash(const GridParams& g, int cx, int cy, int cz) {
   uint32_t h = mix_coord(cx, 0x9e3779b9u) ^ mix_coord(cy, 0x85ebca6bu);
-  if (g.dim == 3) h ^= mix_coord(cz, 0xc2b2ae35u);
+  if ((DIM ? DIM : g.dim) == 3) h ^= mix_coord(cz, 0xc2b2ae35u);
   // h % cells; for a power-of-two cell count (Particle mode validates one)
   // the mask gives the same value without an integer division.
   return g.cells_mask ? (h & g.cells_mask) : (h % g.cells);
@@ -98,14 +100,16 @@ __device__ __forceinline__ int3 cell_coords(const GridParams& g, float4 p) {
   return make_int3(c[0], c[1], c[2]);
 }
 
-// cell_index_from_coords (hashgrid.rs:123-145); returns -1 for None.
+// cell_index_from_coords (hashgrid.rs:123-145); returns -1 for None.  DIM as
+// for particle_cell_hash.
+template <int DIM = 0>
 __device__ __forceinline__ long long cell_index(const GridParams& g, int cx, int cy, int cz) {
-  if (g.mode == kModeParticle) return particle_cell_hash(g, cx, cy, cz);
+  if (g.mode == kModeParticle) return particle_cell_hash<DIM>(g, cx, cy, cz);
   const int c[3] = {cx, cy, cz};
   unsigned long long stride = 1, hash = 0;
 #pragma unroll
   for (int axis = 0; axis < 3; ++axis) {
-    if (axis < g.dim) {
+    if (axis < (DIM ? DIM : g.dim)) {
       int size = g.grid_size[axis];
       int cell;
       if (g.boundary == kBoundaryPeriodic) {
@@ -129,13 +133,14 @@ __device__ __forceinline__ uint32_t cell_for_position(const GridParams& g, float
   return static_cast<uint32_t>(cell_index(g, c.x, c.y, c.z));
 }
 
-// neighbor_delta (hashgrid.rs:165-181).
+// neighbor_delta (hashgrid.rs:165-181).  DIM as for particle_cell_hash.
+template <int DIM = 0>
 __device__ __forceinline__ float4 neighbor_delta(const GridParams& g, float4 lhs, float4 rhs) {
   float d[3] = {rhs.x - lhs.x, rhs.y - lhs.y, rhs.z - lhs.z};
   float out[3] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int axis = 0; axis < 3; ++axis) {
-    if (axis < g.dim) {
+    if (axis < (DIM ? DIM : g.dim)) {
       float v = d[axis];
       if (g.boundary == kBoundaryPeriodic) {
         if (v > g.half[axis]) {
@@ -340,7 +345,7 @@ __device__ __forceinline__ void for_each_neighbor(const GridParams& g, const Sor
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const int3 nc = add_wrapping(center, bin_delta<DIM>(b));
-    const long long cell = cell_index(g, nc.x, nc.y, nc.z);
+    const long long cell = cell_index<DIM>(g, nc.x, nc.y, nc.z);
     uint32_t lo = 0, cnt = 0;
     if (cell >= 0) {
       const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
@@ -387,7 +392,7 @@ __device__ __forceinline__ void for_each_neighbor(const GridParams& g, const Sor
         const int3 want = add_wrapping(center, bin_delta<DIM>(bs[u]));
         if (cj[u].x != want.x || cj[u].y != want.y || cj[u].z != want.z) continue;
       }
-      const float4 d = neighbor_delta(g, pi, pj[u]);
+      const float4 d = neighbor_delta<DIM>(g, pi, pj[u]);
       float r2 = d.x * d.x;
       r2 = r2 + d.y * d.y;
       if (DIM == 3) r2 = r2 + d.z * d.z;
@@ -438,7 +443,7 @@ __device__ __forceinline__ void walk_cell_warp(const GridParams& g, const Sorted
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const int3 nc = add_wrapping(center, bin_delta<DIM>(b));
-    const long long cell = cell_index(g, nc.x, nc.y, nc.z);
+    const long long cell = cell_index<DIM>(g, nc.x, nc.y, nc.z);
     uint32_t lo = 0, cnt = 0;
     if (cell >= 0) {
       const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
@@ -485,7 +490,7 @@ __device__ __forceinline__ void walk_cell_warp(const GridParams& g, const Sorted
       for (uint32_t j = 0; j < nv; ++j) {
         const float4 pj = win.rec[j];
         if (pj.w == 0.0f) continue;
-        const float4 d = neighbor_delta(g, pi, pj);
+        const float4 d = neighbor_delta<DIM>(g, pi, pj);
         float r2 = d.x * d.x;
         r2 = r2 + d.y * d.y;
         if (DIM == 3) r2 = r2 + d.z * d.z;

@@ -224,7 +224,7 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         if (e0 + u >= nh) break;
-        const float4 d = neighbor_delta(g, pi, pj[u]);
+        const float4 d = neighbor_delta<DIM>(g, pi, pj[u]);
         float r2 = d.x * d.x;
         r2 = r2 + d.y * d.y;
         if (DIM == 3) r2 = r2 + d.z * d.z;
