@@ -876,9 +876,16 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
                         static_cast<const void*>(density)})
     pinned = pinned && host_pinned(h);
   const uint32_t chunks = host_step_chunks(B, N, pinned);
-  const uint32_t chunk_max = (B + chunks - 1) / std::max<uint32_t>(chunks, 1);
+  // Chunks hold floor(B / chunks) or ceil(B / chunks) rollouts; the workspace
+  // serves both (the MLP tile shape, hence the tile padding, may differ).
   size_t wsb = 0;
-  NPA_TRY(npa_dev_step_workspace_size(m, grid, chunks > 1 ? chunk_max : batch, n, &wsb));
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, chunks > 1 ? (B + chunks - 1) / chunks : batch, n,
+                                      &wsb));
+  if (chunks > 1 && B / chunks > 0) {
+    size_t small = 0;
+    NPA_TRY(npa_dev_step_workspace_size(m, grid, B / chunks, n, &small));
+    wsb = std::max(wsb, small);
+  }
   std::lock_guard<std::mutex> lock(m->mu);
   struct Bufs {
     float4 *pos, *np, *dx;
