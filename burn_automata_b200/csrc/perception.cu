@@ -122,7 +122,7 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
     for (int d = 0; d < DIM; ++d) density_gradient[row * DIM + d] = a.dgrad[d];
 }
 
-template <int DIM, int CH, bool COOP>
+template <int DIM, int CH, bool COOP, int OPT>
 __global__ void __launch_bounds__(128, PerceptionBlocks<DIM>::value)
 perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl,
                         uint32_t total, uint32_t q_begin, uint32_t q_end,
@@ -157,7 +157,7 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
+  perceive_chunk<DIM, CH, OPT>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
                           peers);
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
                          [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
@@ -293,14 +293,23 @@ npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& 
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(q_end - q_begin) * chunks, 128);
 #define NPA_TILES(D, CHV, CO)                                                                 \
-  perception_tiles_kernel<D, CHV, CO><<<blocks, 128, 0, stream>>>(                            \
-      g, pp, s, hl, total, q_begin, q_end, states, state_dims, chunks, volume_sorted,         \
-      tile_rows, tiles)
+  do {                                                                                        \
+    if (fixed_opts)                                                                           \
+      perception_tiles_kernel<D, CHV, CO, 1><<<blocks, 128, 0, stream>>>(                     \
+          g, pp, s, hl, total, q_begin, q_end, states, state_dims, chunks, volume_sorted,     \
+          tile_rows, tiles);                                                                  \
+    else                                                                                      \
+      perception_tiles_kernel<D, CHV, CO, 0><<<blocks, 128, 0, stream>>>(                     \
+          g, pp, s, hl, total, q_begin, q_end, states, state_dims, chunks, volume_sorted,     \
+          tile_rows, tiles);                                                                  \
+  } while (0)
 #define NPA_TILES_CH(D, CO)                                    \
   do {                                                         \
     if (ch == 4) NPA_TILES(D, 4, CO); else NPA_TILES(D, 8, CO); \
   } while (0)
   const bool coop = dense_cells(g, batch, total);
+  // the rollout models' options: state gradient, hybrid moment, no density gradient
+  const bool fixed_opts = p.state_grad && !p.density_grad && p.hybrid;
   if (g.dim == 2) {
     if (coop) NPA_TILES_CH(2, true); else NPA_TILES_CH(2, false);
   } else {

@@ -87,13 +87,18 @@ __device__ __forceinline__ void load_row(const float* __restrict__ states, size_
 
 // One neighbour's terms (second_pass_particle, forward.rs:249-295, or the
 // separate passes of the other branch), added in the reference's order.
-template <int DIM, int CH>
+// OPT = 1 fixes the rollout models' options at compile time (state gradient
+// and hybrid moment on, density gradient off; p must hold the same), which
+// drops the per-pair option branches; OPT = 0 reads them from p.
+template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionParams& p,
                                           bool self, float4 d, float r2, float vol,
                                           const float (&sjv)[CH], const float (&si)[CH],
                                           ChunkState<DIM, CH>& st) {
+  const bool sg = OPT ? true : p.state_grad, dg = OPT ? false : p.density_grad;
+  const bool hy = OPT ? true : p.hybrid;
   const float smooth = poly6(g, r2);
-  if (p.state_grad && p.density_grad) {
+  if (sg && dg) {
 #pragma unroll
     for (int c = 0; c < CH; ++c) st.acc.blur[c] = st.acc.blur[c] + sjv[c] * smooth * vol;
   } else {
@@ -103,12 +108,12 @@ __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionP
   }
   if (self) return;
   const float dv[3] = {d.x, d.y, d.z};
-  if (p.density_grad) {
+  if (dg) {
     const float m1 = spiky_mag(g, r2, 1.0f);
 #pragma unroll
     for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = st.acc.dgrad[a] + m1 * dv[a];
   }
-  if (p.state_grad) {
+  if (sg) {
     const float mv = spiky_mag(g, r2, vol);
     float gv[DIM];
 #pragma unroll
@@ -119,7 +124,7 @@ __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionP
 #pragma unroll
       for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = st.acc.sgrad[c][a] + diff * gv[a];
     }
-    if (p.hybrid) {
+    if (hy) {
 #pragma unroll
       for (int r = 0; r < DIM; ++r)
 #pragma unroll
@@ -130,10 +135,12 @@ __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionP
 }
 
 // Moment correction (normalize.rs:93-118) and gradient normalisation (:5-58).
-template <int DIM, int CH>
+template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkState<DIM, CH>& st) {
-  if (p.state_grad) {
-    if (p.hybrid) {
+  const bool sg = OPT ? true : p.state_grad, dg = OPT ? false : p.density_grad;
+  const bool hy = OPT ? true : p.hybrid;
+  if (sg) {
+    if (hy) {
       float m9[9], inv[9];
 #pragma unroll
       for (int r = 0; r < DIM; ++r)
@@ -161,7 +168,7 @@ __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkSta
       if (p.log_norm_grad) log_normalize_n<DIM>(st.acc.sgrad[c]);
     }
   }
-  if (p.density_grad) {
+  if (dg) {
 #pragma unroll
     for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = st.acc.dgrad[a] * p.density_scale;
     if (p.log_norm_density_grad) log_normalize_n<DIM>(st.acc.dgrad);
@@ -176,7 +183,7 @@ __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkSta
 // set (warp-uniformly) when the warp's lanes fall into few (batch, cell)
 // groups (`peers`: this lane's group): then a walk, if any lane needs one, is
 // the warp-cooperative walk of each group.
-template <int DIM, int CH>
+template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
                                                const SortedGrid& s, const HitLists& hl,
                                                uint32_t batch, uint32_t q, float4 pi,
@@ -201,7 +208,7 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
         [&](uint32_t j, uint32_t qn, float4 d, float r2) {
           float sjv[CH];
           load_row<CH>(states, win->row[j], C, c0, vec4, sjv);
-          chunk_add<DIM, CH>(g, p, qn == q, d, r2, win->vol[j], sjv, si, st);
+          chunk_add<DIM, CH, OPT>(g, p, qn == q, d, r2, win->vol[j], sjv, si, st);
         });
   } else if (nh <= uint32_t(hl.cap)) {
     const uint32_t* list = hl.slots + q;
@@ -228,17 +235,17 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
         float r2 = d.x * d.x;
         r2 = r2 + d.y * d.y;
         if (DIM == 3) r2 = r2 + d.z * d.z;
-        chunk_add<DIM, CH>(g, p, qj[u] == q, d, r2, vol[u], sj[u], si, st);
+        chunk_add<DIM, CH, OPT>(g, p, qj[u] == q, d, r2, vol[u], sj[u], si, st);
       }
     }
   } else {
     for_each_neighbor<DIM>(g, s, batch, pi, center, [&](uint32_t qn, float4 d, float r2) {
       float sjv[CH];
       load_row<CH>(states, batch_base + __ldg(s.permutation + qn), C, c0, vec4, sjv);
-      chunk_add<DIM, CH>(g, p, qn == q, d, r2, __ldg(volume + qn), sjv, si, st);
+      chunk_add<DIM, CH, OPT>(g, p, qn == q, d, r2, __ldg(volume + qn), sjv, si, st);
     });
   }
-  chunk_finish<DIM, CH>(p, st);
+  chunk_finish<DIM, CH, OPT>(p, st);
   out = st.acc;
 }
 
