@@ -118,21 +118,23 @@ def test_gpu_masks_match_the_oracle(seed, p, count, first, steps):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("log_norm", [False, True])
-def test_gpu_stochastic_rollout_matches_the_oracle(oracle_mod, log_norm):
+@pytest.mark.parametrize("log_norm,batch", [(False, 1), (True, 1), (False, 3)])
+def test_gpu_stochastic_rollout_matches_the_oracle(oracle_mod, log_norm, batch):
+    """One mask stream over the whole batch (stochastic_mask draws
+    batch * particle_count values per step)."""
     import burn_automata_b200 as ba
 
-    w = workloads.make("cfg0", n=2048)
+    w = workloads.make("cfg0", n=2048, batch=batch)
     w.model = w.model.with_(log_norm_grad=log_norm)
     m = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
                                            w.weights.b2))
     steps, p, seed = 12, 0.5, 42
-    cfg = ba.RolloutConfig(batch_size=1, particle_count=w.n, steps=steps, dt=w.dt,
+    cfg = ba.RolloutConfig(batch_size=batch, particle_count=w.n, steps=steps, dt=w.dt,
                            update_prob=p, seed=seed)
     trace = ba.run_rollout_from_particles(m, w.grid, cfg, w.positions, w.states)
-    masks = oracle_mod.rollout_masks(seed, p, w.n, steps)
-    pos, st, mean_dx = oracle_mod.rollout(w.model, w.weights, w.grid, w.positions, w.states, 1,
-                                          w.n, steps, w.dt, masks=masks)
+    masks = oracle_mod.rollout_masks(seed, p, batch * w.n, steps)
+    pos, st, mean_dx = oracle_mod.rollout(w.model, w.weights, w.grid, w.positions, w.states,
+                                          batch, w.n, steps, w.dt, masks=masks)
     if log_norm:
         # the rollout tolerance: log1p is correctly rounded on the GPU, the
         # host's log1pf is not, and the rare one-ulp differences grow over steps
@@ -144,7 +146,7 @@ def test_gpu_stochastic_rollout_matches_the_oracle(oracle_mod, log_norm):
     np.testing.assert_allclose(trace.mean_dx, mean_dx, rtol=1e-5)
     # the unmasked rollout differs: the mask was applied
     full = ba.run_rollout_from_particles(
-        m, w.grid, ba.RolloutConfig(batch_size=1, particle_count=w.n, steps=steps, dt=w.dt),
+        m, w.grid, ba.RolloutConfig(batch_size=batch, particle_count=w.n, steps=steps, dt=w.dt),
         w.positions, w.states)
     assert not np.array_equal(full.states, trace.states)
     m.close()
