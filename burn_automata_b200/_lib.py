@@ -68,6 +68,7 @@ SIGNATURES = [
     ("npa_status_string", ctypes.c_char_p, [c_i32]),
     ("npa_last_error_message", ctypes.c_char_p, []),
     ("npa_kernel_launch_count", c_u64, []),
+    ("npa_bulk_copy_timeouts", c_u64, []),
     ("npa_grid_validate", c_i32, [P(GridConfigC)]),
     ("npa_grid_cell_count", c_i32, [P(GridConfigC), P(c_i64)]),
     ("npa_feature_dims", c_i32, [P(GridConfigC), P(PerceptionOptionsC), c_i64, P(c_i64)]),

@@ -502,6 +502,8 @@ const char* npa_last_error_message(void) { return g_last_error.c_str(); }
 
 uint64_t npa_kernel_launch_count(void) { return g_launches.load(); }
 
+uint64_t npa_bulk_copy_timeouts(void) { return bulk_copy_timeouts(); }
+
 // Test hook for the out-of-memory path of the host-buffer entry points.
 void npa_debug_set_allocation_cap(uint64_t bytes) { g_alloc_cap.store(bytes); }
 

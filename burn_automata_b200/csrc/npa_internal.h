@@ -135,6 +135,8 @@ struct StochasticMask {
   const uint32_t* lane_seeds = nullptr;    // [B] device
   const uint32_t* step_counter = nullptr;  // device step index
 };
+// Feature-tile bulk copies that timed out in the MLP step kernel (device counter).
+uint64_t bulk_copy_timeouts();
 // step_counter[0] += 1 (after a step that used the stochastic mask).
 npa_status launch_advance_step(uint32_t* counter, cudaStream_t stream);
 // out[0] = mean over i < total of |dx[i].xyz| (run_rollout's mean_dx entry);

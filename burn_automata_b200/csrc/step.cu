@@ -17,12 +17,13 @@
 //            lane layout is described at layer1_hidden_group) and
 //            walks k = 0..F-1 in order (features of the tile feature-major in
 //            shared memory, w1 transposed in shared memory);
-//   layer 2: 2 NT / M threads per pair of rows, each owning
-//            ceil(O / (2 NT / M)) outputs of both rows, sequential over h.
+//   layer 2: R NT / M threads per group of R rows (R = 2 or 3), each owning
+//            ceil(O / (R NT / M)) outputs of the group's rows, sequential over h.
 // The rollout's MLP stage consumes the feature tiles written by
 // perception_tiles_kernel ([tile][F][M], sorted order) through one shared
-// buffer: the next tile is fetched with cp.async once layer 2 is done, behind
-// the epilogue and the wait at the top of the loop (one buffer instead of two
+// buffer: once layer 2 is done, one thread starts a bulk (TMA) copy of the next
+// tile that completes on an mbarrier, behind the epilogue and the bounded wait
+// at the top of the loop (one buffer instead of two
 // is what lets 12 warps per SM fit; measured 1.017 vs 1.067 ms at 8 warps
 // double-buffered on cfg2).  Each row finishes with forward_from_features_with_eps
 // (model.rs:867-898), the 3D position gates (model.rs:806-837) and euler_step
@@ -55,7 +56,7 @@ struct MlpShape {
 };
 
 struct SmemLayout {
-  size_t ft0, hid, w1, w2, outs, total;  // offsets in floats
+  size_t ft0, hid, w1, w2, outs, bar, total;  // offsets in floats
 };
 
 __host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
@@ -71,20 +72,56 @@ __host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
   l.w1 = take(size_t(s.w1_resident ? s.F : kKC) * s.Hp);
   l.w2 = take(size_t(s.O) * s.w2_stride);
   l.outs = take(size_t(s.M) * s.out_stride);
+  l.bar = take(4);  // the feature-tile mbarrier (8 bytes, 16-byte aligned)
   l.total = off;
   return l;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+// ---- bulk (TMA) copy of a feature tile, completed on an mbarrier ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
+__device__ __forceinline__ void mbar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(bar)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+// One elected thread: expect `bytes` on the barrier and start the copy in
+// pieces of at most kBulkPiece bytes (sizes and addresses multiples of 16).
+constexpr uint32_t kBulkPiece = 16384;
+__device__ __forceinline__ void bulk_tile_load(float* dst, const float* src, uint32_t bytes,
+                                               uint64_t* bar) {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+  for (uint32_t off = 0; off < bytes; off += kBulkPiece) {
+    const uint32_t n = bytes - off < kBulkPiece ? bytes - off : kBulkPiece;
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(reinterpret_cast<char*>(dst) + off)),
+        "l"(reinterpret_cast<const char*>(src) + off), "r"(n), "r"(smem_u32(bar))
+        : "memory");
+  }
+}
+// Waits for phase `parity` of the barrier for at most about two seconds of
+// global time; false (and a count in g_bulk_copy_timeouts) when it gave up.
+__device__ unsigned long long g_bulk_copy_timeouts = 0;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    if (t - t0 > 2000000000ull) return false;
+  }
 }
 
 // Weights into shared memory: w2 [O][H] -> rows of w2_stride; w1^T when resident.
@@ -434,24 +471,27 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
                 float* __restrict__ ds_out, float* __restrict__ features_out) {
   extern __shared__ float4 smem4[];
   float* smem = reinterpret_cast<float*>(smem4);
-  // One feature-tile buffer: the next tile is fetched while layer 2 and the
-  // epilogue of this one run (the tile is dead once layer 1 has read it).
+  // One feature-tile buffer, filled by a bulk (TMA) copy on an mbarrier: the
+  // next tile is fetched while the epilogue of this one runs (the tile is
+  // dead once layer 1 has read it).
   const SmemLayout L = smem_layout(s);
   float* ft = smem + L.ft0;
   float* hid = smem + L.hid;
   float* w1s = smem + L.w1;
   float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
   constexpr int TPR = HG / 8;  // layer-2 / epilogue threads per row (NT / M)
   const int C = sp.C, D = sp.D;
   const uint32_t tiles = tile_end;
-  const int chunks16 = s.F * s.M / 4;  // 16-byte chunks per feature tile
+  const uint32_t tile_bytes = uint32_t(s.F) * uint32_t(s.M) * 4u;  // a multiple of 16
   auto issue = [&](uint32_t t) {
-    const float* src = tiles_in + size_t(t) * s.F * s.M;
-    for (int e = threadIdx.x; e < chunks16; e += NT) cp_async16(ft + 4 * e, src + 4 * e);
-    cp_async_commit();
+    if (threadIdx.x == 0) bulk_tile_load(ft, tiles_in + size_t(t) * s.F * s.M, tile_bytes, bar);
   };
+  uint32_t phase = 0;
   uint32_t tile = tile_begin + blockIdx.x;
+  if (threadIdx.x == 0) mbar_init(bar);
+  __syncthreads();
   if (tile < tiles) issue(tile);
   load_weights(s, w1t, w2, w1s, w2s);
   float bias1[kTH];
@@ -468,8 +508,18 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
                    ((reinterpret_cast<uintptr_t>(sp.states) | reinterpret_cast<uintptr_t>(next_states) |
                      reinterpret_cast<uintptr_t>(ds_out)) & 15u) == 0;
   for (; tile < tiles; tile += gridDim.x) {
-    cp_async_wait<0>();
-    __syncthreads();
+    const bool arrived = mbar_wait(bar, phase);
+    if (__syncthreads_or(!arrived)) {
+      // The copy did not complete in time (for some thread): the whole block
+      // counts it, gives the copy a last bounded wait so nothing lands in its
+      // shared memory after it exits, and leaves the remaining tiles undone.
+      if (threadIdx.x == 0) {
+        atomicAdd(&g_bulk_copy_timeouts, 1ull);
+        mbar_wait(bar, phase);
+      }
+      return;
+    }
+    phase ^= 1u;
     // The epilogue's position / mask reads are issued before layer 1 so
     // their latency is hidden behind it.
     const uint32_t q = tile * s.M + r;
@@ -585,7 +635,6 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
       }
     }
   }
-  cp_async_wait<0>();
 }
 
 MlpShape shape_with(const DeviceModel& m, int nt) {
@@ -777,6 +826,15 @@ npa_status launch_euler(const GridParams& g, const float4* positions, const floa
   return after_launch("euler_kernel");
 }
 
+uint64_t bulk_copy_timeouts() {
+  unsigned long long v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_bulk_copy_timeouts, sizeof(v)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return v;
+}
+
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
                            uint32_t batch, const float* tiles, const float* states, float dt,
                            const float* mask, const StochasticMask& sm,
@@ -786,6 +844,9 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
   if (total == 0) return NPA_OK;
   if (!mlp_step_supported(m))
     return fail(NPA_ERR_UNSUPPORTED, "MLP shape outside the supported range");
+  // the bulk copies of the feature tiles start on 16-byte boundaries
+  if (reinterpret_cast<uintptr_t>(tiles) & 15u)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "step workspace must be 16-byte aligned");
   const MlpShape s = make_shape(m, total);
   StepParams sp;
   sp.states = states;

@@ -155,6 +155,11 @@ const char* npa_last_error_message(void);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t npa_kernel_launch_count(void);
 
+/* Diagnostic: feature-tile bulk copies of the MLP step kernel that did not
+ * complete within their bounded wait on the current device (0 in a healthy
+ * run; a block that gives up leaves its remaining tiles undone). */
+uint64_t npa_bulk_copy_timeouts(void);
+
 /* HashGridConfig::validate (config.rs:65-84). */
 npa_status npa_grid_validate(const npa_grid_config* cfg);
 /* HashGridConfig::cell_count (config.rs:86-88). */
@@ -404,7 +409,9 @@ npa_status npa_dev_step_workspace_size(npa_model* model, const npa_grid_config* 
 /* NpaModel::step_cpu on device buffers (model.rs:768-858): hashgrid, density,
  * perception into feature tiles, then one kernel for MLP + dx/ds + Euler.
  * Optional outputs (d_update_mask, d_dx, d_ds, d_features, d_density) may be
- * NULL. */
+ * NULL.  d_workspace must be 16-byte aligned (cudaMalloc memory is): the MLP
+ * kernel bulk-copies feature tiles out of it (NPA_ERR_INVALID_ARGUMENT
+ * otherwise). */
 npa_status npa_dev_model_step(npa_model* model, const npa_grid_config* grid,
                               const float* d_positions, const float* d_states, int64_t batch,
                               int64_t n, float dt, const float* d_update_mask,

@@ -230,8 +230,9 @@ def make_model(w):
     return NpaModel(w.model, NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2, w.weights.b2))
 
 
-# cfg2 x 8 (32,768 rows) runs the 384-thread MLP tiles, the others the 256-thread ones.
-@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg2", 8, 4096),
+# cfg2 x 72 (294,912 rows: 11 waves of 192-row tiles beat 16 of 128-row ones)
+# runs the 384-thread MLP tiles, the others the 256-thread ones.
+@pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg2", 72, 4096),
                                           ("cfg3", 1, 4096)])
 def test_step_parity(oracle_mod, name, batch, n):
     w = workloads.make(name, batch=batch, n=n, steps=1)
@@ -246,7 +247,7 @@ def test_step_parity(oracle_mod, name, batch, n):
     np.testing.assert_allclose(gpu.next_positions, ref["next_positions"], rtol=RTOL, atol=ATOL)
 
 
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 72])
 def test_step_bit_exact_without_log_norm(oracle_mod, batch):
     w = workloads.make("cfg2", batch=batch, steps=1)
     w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
@@ -486,3 +487,22 @@ def test_dense_cluster_perception_full_options(oracle_mod):
         ref = oracle_mod.perceive_with_options(w.positions, st, 1, w.n, c, w.grid, opt)
         np.testing.assert_array_equal(gpu.density, ref["density"])
         np.testing.assert_allclose(gpu.features, ref["features"], rtol=RTOL, atol=ATOL)
+
+
+def test_mlp_feature_tile_bulk_copies_complete():
+    """The MLP step kernel's bulk (TMA) copies of feature tiles all complete
+    within their bounded waits: the device timeout counter stays 0 over
+    executor steps of a batched and a single-rollout configuration."""
+    L = ba.load_library()
+    before = L.npa_bulk_copy_timeouts()
+    for name, batch in (("cfg2", 32), ("cfg3", None)):
+        w = workloads.make(name, batch=batch, steps=2)
+        m = make_model(w)
+        ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
+        ex.create_state(w.positions, w.states)
+        ex.step_state_many(3, w.dt, use_graph=False)
+        pos, st = ex.read_state()
+        assert np.isfinite(st).all()
+        ex.close()
+        m.close()
+    assert L.npa_bulk_copy_timeouts() == before == 0
