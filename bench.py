@@ -67,7 +67,7 @@ WORKLOADS = {
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu captures, per particle of that launch:
 #   profiles/mlp_step_kernel_cfg2.txt: 356.7 MB + 67.7 MB for 1,048,576 rows.
-NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (356.771328e6 + 68.858368e6) / 1048576}
+NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (356.673280e6 + 68.960000e6) / 1048576}
 
 
 def env_int(name, default):
