@@ -802,6 +802,18 @@ npa_status npa_model_forward_update_from_features(npa_model* m, const float* fea
   return s.finish();
 }
 
+// After a synchronising call that ran the MLP step kernel: NPA_ERR_CUDA when
+// the device's count of feature-tile copies that missed their bounded wait has
+// grown since the last check (those blocks left their tiles undone).
+static std::atomic<uint64_t> g_bulk_timeouts_seen{0};
+static npa_status check_bulk_copies() {
+  const uint64_t now = bulk_copy_timeouts();
+  uint64_t seen = g_bulk_timeouts_seen.load();
+  if (now <= seen) return NPA_OK;
+  g_bulk_timeouts_seen.compare_exchange_strong(seen, now);
+  return fail(NPA_ERR_CUDA, "an MLP feature-tile copy did not complete within its bounded wait");
+}
+
 // Reserves `bytes` of the model's host-call arena (caller holds m->mu).
 npa_status arena_reserve(npa_model* m, size_t bytes) {
   HostArena& a = m->arena;
@@ -972,7 +984,7 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
   if (status != NPA_OK) return status;
   for (cudaError_t e : {e_out, e_in, e_st})
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-  return NPA_OK;
+  return check_bulk_copies();
 }
 
 // ---- device operators ----
@@ -1519,7 +1531,7 @@ npa_status npa_executor_read_state(npa_executor* e, float* positions, float* sta
   const size_t C = size_t(e->model->dm.state_dims);
   if (positions) NPA_CUDA(cudaMemcpy(positions, e->pos[e->cur], total * 16, cudaMemcpyDeviceToHost), "read positions");
   if (states && C) NPA_CUDA(cudaMemcpy(states, e->st[e->cur], total * C * 4, cudaMemcpyDeviceToHost), "read states");
-  return NPA_OK;
+  return check_bulk_copies();
 }
 
 npa_status npa_executor_state_device(npa_executor* e, float** d_positions, float** d_states) {
@@ -1777,7 +1789,8 @@ static npa_status run_rollout_impl(npa_model* m, const npa_grid_config* grid, fl
   NPA_TRY(sc.download(positions, pos[cur], size_t(total) * 16));
   NPA_TRY(sc.download(states, st[cur], size_t(total) * C * 4));
   if (mean_dx) NPA_TRY(sc.download(mean_dx, dmean, size_t(steps) * 4));
-  return sc.finish();
+  NPA_TRY(sc.finish());
+  return check_bulk_copies();
 }
 
 npa_status npa_model_run_rollout_trace(npa_model* m, const npa_grid_config* grid,

@@ -157,7 +157,10 @@ uint64_t npa_kernel_launch_count(void);
 
 /* Diagnostic: feature-tile bulk copies of the MLP step kernel that did not
  * complete within their bounded wait on the current device (0 in a healthy
- * run; a block that gives up leaves its remaining tiles undone). */
+ * run; a block that gives up leaves its remaining tiles undone).  The
+ * synchronising host calls (npa_model_step, npa_model_run_rollout*,
+ * npa_executor_read_state) return NPA_ERR_CUDA when this count has grown
+ * since the last such check. */
 uint64_t npa_bulk_copy_timeouts(void);
 
 /* HashGridConfig::validate (config.rs:65-84). */
