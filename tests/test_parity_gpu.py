@@ -374,13 +374,14 @@ def _pinned_like(a):
     return p
 
 
-@pytest.mark.parametrize("batch", [67, 160])
-def test_host_step_pipelined_over_rollout_chunks(oracle_mod, batch):
+@pytest.mark.parametrize("batch,n", [(67, 4096), (160, 4096), (1025, 256)])
+def test_host_step_pipelined_over_rollout_chunks(oracle_mod, batch, n):
     """Page-locked buffers: the host step runs in rollout chunks (2 for 67
-    rollouts, split 33 / 34; 5 for 160) whose copies overlap the other chunks'
-    kernels.  Every output equals the one-chunk step of pageable buffers bit for
-    bit, and the first and last rollouts match the oracle."""
-    w = workloads.make("cfg2", batch=batch, steps=1)
+    rollouts, split 33 / 34; 5 for 160; 512 / 513 small rollouts for 1025)
+    whose copies overlap the other chunks' kernels.  Every output equals the
+    one-chunk step of pageable buffers bit for bit, and the first and last
+    rollouts match the oracle."""
+    w = workloads.make("cfg2", batch=batch, n=n, steps=1)
     m = make_model(w)
     whole = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt)
     pos, st = _pinned_like(w.positions), _pinned_like(w.states)
@@ -393,7 +394,7 @@ def test_host_step_pipelined_over_rollout_chunks(oracle_mod, batch):
         np.testing.assert_array_equal(getattr(r, key), getattr(whole, key), err_msg=key)
     C = w.state_dims
     for b in (0, batch - 1):
-        sub = workloads.make("cfg2", batch=1, steps=1, first=b)
+        sub = workloads.make("cfg2", batch=1, n=n, steps=1, first=b)
         ref = oracle_mod.step(sub.model, sub.weights, sub.grid, sub.positions, sub.states, 1,
                               sub.n, sub.dt)
         rows = slice(b * w.n, (b + 1) * w.n)
