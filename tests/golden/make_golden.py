@@ -3,8 +3,8 @@
 The reference ships a dependency-free SPH + MLP step in
 scripts/reference/selforg/validate_import_parity.py (density :195,
 perceive_second_pass :207, mlp :251, step_python :156).  This script imports
-it from a checkout of mosure/burn_automata (default /root/reference, or
-$BURN_AUTOMATA_REF) and records its outputs on small seeded inputs.  Run it
+it from a checkout of mosure/burn_automata whose path is given in
+$BURN_AUTOMATA_REF and records its outputs on small seeded inputs.  Run it
 where the reference is present; the .npz files it writes are committed so the
 tests never need the reference at run time.
 
@@ -24,12 +24,14 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("BURN_AUTOMATA_REF", "/root/reference"))
-SCRIPT = REF / "scripts/reference/selforg/validate_import_parity.py"
-
-
 def load_reference():
-    spec = importlib.util.spec_from_file_location("validate_import_parity", SCRIPT)
+    if "BURN_AUTOMATA_REF" not in os.environ:
+        sys.exit("set BURN_AUTOMATA_REF to a checkout of mosure/burn_automata")
+    script = (Path(os.environ["BURN_AUTOMATA_REF"])
+              / "scripts/reference/selforg/validate_import_parity.py")
+    if not script.exists():
+        sys.exit(f"reference script not found at {script}")
+    spec = importlib.util.spec_from_file_location("validate_import_parity", script)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
@@ -90,8 +92,6 @@ def make_case(ref, name, p):
 
 
 def main():
-    if not SCRIPT.exists():
-        sys.exit(f"reference script not found at {SCRIPT}")
     ref = load_reference()
     for name, p in CASES.items():
         make_case(ref, name, p)
