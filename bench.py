@@ -5,11 +5,16 @@ Workloads (--workload, default "cfg2"; seeded synthetic inputs from
 burn_automata_b200/workloads.py):
   cfg0  one 2D rollout, 4,096 particles, C=16, MLP 64->128->18
   cfg1  hashgrid build + perception alone, 1,048,576 2D particles, C=32, F=130
-  cfg2  256 independent cfg0-architecture rollouts of 4,096 particles per GPU
+  cfg2  256 independent cfg0-architecture rollouts of 4,096 particles, split
+        evenly over the GPUs ("scaling": "strong"; 32 rollouts per GPU at 8)
   cfg3  one 3D torus rollout, 16,384 particles, C=32, MLP 160->256->35
   cfg4  one clustered 2D rollout, 4,194,304 particles (64-component mixture)
-Each GPU rank runs its own shard with no collective on the step path
-("scaling": "weak"; --strong splits --rollouts over the ranks instead).
+No collective runs on the step path: each rank steps its own shard.  A
+single-rollout configuration does not shard, so at N > 1 each rank runs an
+independent replica ("weak"); --strong --rollouts R splits R rollouts over
+the ranks (cfg4 x 8), --weak gives every rank a full cfg2 batch.  After the
+timed region rank 0 checks every rank's final rollouts bit for bit against a
+1-GPU rerun of the same rollouts ("validation").
 
 A bench step is one rollout step (hashgrid -> density -> perception ->
 MLP + Euler) over every particle of the shard; for cfg1 it is one hashgrid
@@ -55,11 +60,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "particle-steps/s per rollout step at 1/2/4/8 B200; % of HBM roofline"
 DATA = "synthetic (seeded; see burn_automata_b200/workloads.py)"
 
-# rollouts per rank, kind of step, default timed steps
+# rollouts (in total for the batched configuration, per rank otherwise), kind
+# of step, default timed steps
 WORKLOADS = {
     "cfg0": {"rollouts": 1, "kind": "step", "steps": 200},
     "cfg1": {"rollouts": 1, "kind": "perception", "steps": 50},
-    "cfg2": {"rollouts": 256, "kind": "step", "steps": 200},
+    "cfg2": {"rollouts": 256, "kind": "step", "steps": 200, "batched": True},
     "cfg3": {"rollouts": 1, "kind": "step", "steps": 100},
     "cfg4": {"rollouts": 1, "kind": "step", "steps": 5},
 }
@@ -119,68 +125,118 @@ def perception_step_bytes(w, features) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled DURING the timed
+    region.  NVML is polled every few milliseconds from a thread started
+    right before the timed region and stopped right after it, on every GPU of
+    the job, so even a short region gets samples taken under load; without
+    NVML, nvidia-smi at its 100 ms floor.  sm_mhz is the median over the
+    samples taken inside the region (the GPU is busy throughout it)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4),
+               ("hw_power_brake_slowdown", 0x80))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, cuda_devices, period_s=0.004):
+        self.cuda_devices = list(cuda_devices)
+        self.period_s = period_s
+        self.samples = []
+        self.handles = []
+        self.nvml = None
         self.proc = None
         self.path = None
+        self.thread = None
+        self.running = False
+
+    def _nvml_handles(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        handles = []
+        for d in self.cuda_devices:
+            p = torch.cuda.get_device_properties(d)
+            h = None
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{p.uuid}")
+            except Exception:
+                try:
+                    bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                    h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+                except Exception:
+                    h = None
+            if h is not None:
+                handles.append(h)
+        return pynvml, handles
+
+    def _poll(self):
+        nv = self.nvml
+        while self.running:
+            for h in self.handles:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), float(mx), int(rs)))
+                except Exception:
+                    pass
+            time.sleep(self.period_s)
 
     def start(self):
+        import threading
+
+        try:
+            self.nvml, self.handles = self._nvml_handles()
+        except Exception:
+            self.nvml, self.handles = None, []
+        if self.handles:
+            self.running = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
-    def stop(self, gpu_indices):
+    def stop(self):
+        if self.thread is not None:
+            self.running = False
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            sm = [s[0] for s in self.samples]
+            names = sorted({n for s in self.samples for n, bit in self.REASONS if s[2] & bit})
+            return {"sm_mhz": float(np.median(sm)), "sm_min_mhz": min(sm),
+                    "sm_max_mhz": max(s[1] for s in self.samples), "reasons": names,
+                    "samples": len(self.samples), "gpus": len(self.handles),
+                    "source": "nvml, polled every ~4 ms inside the timed region"}
         if self.proc is None:
             return None
-        time.sleep(0.15)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                idx = int(parts[0])
-            except ValueError:
-                continue
-            if idx in gpu_indices:
-                rows.append(parts)
+        rows = [[p.strip() for p in line.split(",")]
+                for line in Path(self.path).read_text().splitlines()]
         os.unlink(self.path)
-        if not rows:
-            return None
+        rows = [r for r in rows if len(r) >= 9]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        if not sm:
+            return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k] == "Active"})
-        # Samples while the GPU is busy (under load) give the median clock.
-        busy = sorted(sm)[len(sm) // 2:] if sm else []
-        return {"sm_mhz": float(np.median(busy)) if busy else None,
+        return {"sm_mhz": float(np.median(sm)), "sm_min_mhz": min(sm),
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
-
-
-def visible_gpu_indices(world):
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if vis:
-        try:
-            return [int(x) for x in vis.split(",")][:max(world, 1)]
-        except ValueError:
-            pass
-    return list(range(max(world, 1)))
+                "samples": len(rows), "source": "nvidia-smi -lms 100 inside the timed region"}
 
 
 # ---- CPU samples (the oracle: a port of the reference CPU path) ----
@@ -291,7 +347,7 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "particle-steps/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
-        "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": shard_plan(args, world, rank)[2], "vs_baseline": None, "dtype": "f32",
         "data": DATA,
         "config": {"workload": args.workload, "sample": s.desc,
                    "note": "CPU port of the reference path (oracle/npa_oracle.c); the Rust "
@@ -312,6 +368,86 @@ def pinned(shape):
     return torch.empty(shape, dtype=torch.float32).pin_memory().numpy()
 
 
+def shard_plan(args, world, rank):
+    """(first rollout, rollouts on this rank, scaling) for this rank.
+
+    The batched configuration (cfg2) splits its 256 rollouts over the ranks
+    ("strong": 32 rollouts per GPU at 8 GPUs), as the configuration says;
+    --weak gives every rank its own full batch instead.  A single-rollout
+    configuration does not shard: at N > 1 each rank runs an independent
+    replica (rank r draws rollout r; "weak"), unless --strong splits an
+    explicit --rollouts over the ranks (cfg4 x 8: --rollouts 8 --strong)."""
+    from burn_automata_b200 import multigpu
+
+    spec = WORKLOADS[args.workload]
+    total = args.rollouts or spec["rollouts"]
+    strong = args.strong or (spec.get("batched", False) and not args.weak)
+    first, count = multigpu.shard(total, world, rank, strong)
+    return first, count, ("strong" if strong else "weak")
+
+
+def final_state(args, w, local_rank, steps, stream_ptr):
+    """One GPU's result for shard `w` after `steps` bench steps, run from the
+    start: the executor's state after `steps` rollout steps (graph replays),
+    or one perception pass (cfg1, whose input does not evolve)."""
+    import burn_automata_b200 as ba
+    import torch
+
+    dev = torch.device("cuda", local_rank)
+    if WORKLOADS[args.workload]["kind"] == "perception":
+        runner = ba.DevicePerception(w.grid, w.options, w.batch, w.n, w.state_dims, local_rank)
+        runner(torch.from_numpy(w.positions).to(dev), torch.from_numpy(w.states).to(dev),
+               stream=stream_ptr)
+        torch.cuda.synchronize()
+        return runner.features.cpu().numpy(), runner.density.cpu().numpy()
+    model = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
+                                               w.weights.b2), device=local_rank)
+    ex = ba.CudaAutomataExecutor(model, w.grid, w.batch, w.n)
+    ex.create_state(w.positions, w.states)
+    ex.step_state_many(steps, w.dt, use_graph=True, stream=stream_ptr)
+    out = ex.read_state()
+    ex.close()
+    model.close()
+    return out
+
+
+def validate_against_one_gpu(args, world, local_rank, plans, gathered, steps, stream_ptr):
+    """Rank 0, after the timed region: reruns every rank's rollouts on this
+    one GPU from the same seeded inputs for the same number of steps and
+    compares the per-rollout digests bit for bit.  Rollouts are independent
+    and the kernels deterministic, so a sharded run must reproduce the
+    1-GPU run exactly.  Returns the validation record for the JSON line."""
+    from burn_automata_b200 import multigpu, workloads
+
+    if world <= 1:
+        return {"checked": False, "reason": "1 GPU: nothing sharded"}
+    if args.workload == "cfg4":
+        return {"checked": False,
+                "reason": "a 1-GPU rerun of the 4,194,304-particle rollouts takes minutes"}
+    t0 = time.perf_counter()
+    expected = {}
+    spec = WORKLOADS[args.workload]
+    batched = spec.get("batched", False)
+    if batched and len({(f, c) for f, c in plans}) == len(plans):
+        lo = min(f for f, _ in plans)
+        hi = max(f + c for f, c in plans)
+        w = workloads.make(args.workload, batch=hi - lo, first=lo)
+        expected.update(multigpu.rollout_digests(w.batch, lo, *final_state(args, w, local_rank, steps,
+                                                            stream_ptr)))
+    else:
+        for first, count in sorted(set(plans)):
+            w = workloads.make(args.workload, batch=count, first=first)
+            expected.update(multigpu.rollout_digests(w.batch, first, *final_state(args, w, local_rank, steps,
+                                                                   stream_ptr)))
+    checked, mismatched = multigpu.compare_digests(gathered, expected)
+    return {"checked": True, "rollouts": checked, "bit_exact": not mismatched,
+            "mismatched_rollouts": mismatched[:16],
+            "method": "per-rollout blake2b digests of the final positions + states of every "
+                      "rank, gathered once after timing, against a 1-GPU rerun of the same "
+                      "rollouts for the same number of steps on rank 0",
+            "rerun_s": round(time.perf_counter() - t0, 3)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -324,8 +460,7 @@ def run_ours(args, rank, world, local_rank):
     multigpu.init("nccl", multigpu.RankInfo(rank, world, local_rank), timeout_s=180, device=dev)
     lib = ba.load_library()
     spec = WORKLOADS[args.workload]
-    total_rollouts = args.rollouts or spec["rollouts"]
-    first, per_rank = multigpu.shard(total_rollouts, world, rank, args.strong)
+    first, per_rank, scaling = shard_plan(args, world, rank)
     w = workloads.make(args.workload, batch=per_rank, first=first)
     particles_rank = w.batch * w.n
     stream = torch.cuda.Stream(dev)
@@ -348,13 +483,12 @@ def run_ours(args, rank, world, local_rank):
         features = w.model.perception_dims()
     torch.cuda.synchronize()
 
-    sampler = ClockSampler() if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
+    sampler = ClockSampler(range(world)) if rank == 0 else None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
     launches0 = lib.npa_kernel_launch_count()
     if perception_only:
         phase_ms, total_ms = runner.run_profiled(d_pos, d_st, args.steps, stream=sptr)
@@ -364,11 +498,12 @@ def run_ours(args, rank, world, local_rank):
                                                          stream=sptr)
         dominant = phase_ms[:, 3]
     torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
     launches = lib.npa_kernel_launch_count() - launches0
     if world > 1:
         dist.barrier()
     max_ms, dom_ms = multigpu.max_over_ranks([total_ms, float(dominant.mean())], dev)
-    clocks = sampler.stop(visible_gpu_indices(world)) if sampler else None
+    rank_ms = multigpu.gather_floats(total_ms, dev)
 
     # all ranks' particles (strong scaling may give ranks unequal shares)
     cnt = torch.tensor([float(particles_rank)], dtype=torch.float64, device=dev)
@@ -376,6 +511,21 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(cnt)
     particles_job = int(cnt.item())
     value = particles_job * args.steps / (max_ms / 1000.0)
+
+    # one gather of per-rollout digests of the final states, checked on rank 0
+    # against a 1-GPU rerun (validation only, outside the timed region)
+    if perception_only:
+        fp, fs = runner.features.cpu().numpy(), runner.density.cpu().numpy()
+    else:
+        fp, fs = ex.read_state()
+    digests = multigpu.rollout_digests(w.batch, first, fp, fs)
+    gathered = multigpu.gather_objects(digests)
+    plans = multigpu.gather_objects((first, per_rank))
+    validation = None
+    if rank == 0:
+        steps_done = args.warmup + args.steps
+        validation = validate_against_one_gpu(args, world, local_rank, plans, gathered,
+                                              steps_done, sptr)
 
     # e2e through the host-buffer call of a drop-in user, one call per step
     e2e = None
@@ -417,13 +567,6 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": particles_job * args.steps / e2e_s, "unit": "particle-steps/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
 
-    # one gather of per-shard checksums of the final states (validation only)
-    if perception_only:
-        fp, fs = runner.features.cpu().numpy(), runner.density.cpu().numpy()
-    else:
-        fp, fs = ex.read_state()
-    checksums = multigpu.gather_checksums(multigpu.shard_checksum(fp, fs), dev)
-
     if rank == 0:
         peak, peak_kind = load_peaks()
         if perception_only:
@@ -436,20 +579,29 @@ def run_ours(args, rank, world, local_rank):
             names = ["hashgrid", "density", "perception", "mlp_step"]
         achieved = kbytes * particles_rank / (dom_ms / 1000.0) / 1e9
         tr = NCU_TRAFFIC_PER_PARTICLE.get((args.workload, kernel))
+        if world == 1:
+            parallelism = "1 GPU"
+        elif scaling == "strong":
+            parallelism = (f"{world} shards of the {args.rollouts or spec['rollouts']} rollouts "
+                           "(no step-path collective)")
+        else:
+            parallelism = f"{world} independent replicas / shards (no step-path collective)"
         line = {
             "metric": METRIC, "value": value, "unit": "particle-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": max_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "data": DATA,
             "config": {"workload": args.workload, "rollouts_per_gpu": per_rank,
+                       "rollouts_total": sum(c for _, c in plans),
                        "particles_per_rollout": w.n, "particles_per_gpu": particles_rank,
                        "state_dims": w.state_dims, "features": features,
                        "eps": w.grid.eps, "grid": list(w.grid.grid_size[:w.grid.dim]),
-                       "parallelism": f"{world} independent shards (no step-path collective)",
+                       "parallelism": parallelism,
                        "l2": ("no flush: per-step working set exceeds the 126 MB L2"
                               if particles_rank >= (1 << 20) else
-                              "no flush: small single rollout, L2-resident by nature")},
+                              "no flush: the shard's per-step working set is below the 126 MB "
+                              "L2 and stays resident, as a rollout of this size does")},
             "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": tr * particles_rank if tr else None,
@@ -461,8 +613,10 @@ def run_ours(args, rank, world, local_rank):
                               "frac": sbytes * value / world / 1e9 / peak,
                               "bytes_per_particle": sbytes},
             "phase_ms": {k: float(phase_ms[:, i].mean()) for i, k in enumerate(names)},
+            "rank_ms_per_step": [t / args.steps for t in rank_ms],
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "validation": validation,
         }
         if not perception_only:
             sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
@@ -479,7 +633,6 @@ def run_ours(args, rank, world, local_rank):
             cpu = cpu_baseline(args.workload)
         line["cpu_baseline"] = cpu
         line["e2e"] = e2e
-        line["final_state_checksums"] = checksums
         print(json.dumps(line), flush=True)
     if not perception_only:
         ex.close()
@@ -499,15 +652,19 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
     ap.add_argument("--strong", action="store_true",
-                    help="split --rollouts over the ranks instead of running them on every rank")
+                    help="split --rollouts over the ranks (the default for cfg2)")
+    ap.add_argument("--weak", action="store_true",
+                    help="cfg2: every rank runs its own full batch instead of a share of it")
     ap.add_argument("--rollouts", type=int, default=None,
-                    help="rollouts per rank (default: 256 for cfg2, 1 otherwise), or in total "
-                         "with --strong")
+                    help="rollouts in total (split over the ranks) for cfg2 or with --strong; "
+                         "per rank otherwise (default: 256 for cfg2, 1 otherwise)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.strong and args.weak:
+        ap.error("--strong and --weak exclude each other")
     if args.steps is None:
         args.steps = WORKLOADS[args.workload]["steps"]
     rank = env_int("RANK", 0)

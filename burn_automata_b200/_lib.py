@@ -55,6 +55,10 @@ class DecodeConfigC(ctypes.Structure):
                 ("min_opacity", c_f32), ("max_opacity", c_f32), ("reserved", c_i32)]
 
 
+class ErrorDetailC(ctypes.Structure):
+    _fields_ = [("status", c_i32), ("eps", c_f32), ("a", c_i64), ("b", c_i64)]
+
+
 class Splat2dConfigC(ctypes.Structure):
     _fields_ = [("image_size", ctypes.c_int64), ("sigma", ctypes.c_float),
                 ("lo", ctypes.c_float), ("hi", ctypes.c_float),
@@ -69,6 +73,10 @@ SIGNATURES = [
     ("npa_last_error_message", ctypes.c_char_p, []),
     ("npa_kernel_launch_count", c_u64, []),
     ("npa_bulk_copy_timeouts", c_u64, []),
+    ("npa_last_error_detail", c_i32, [P(ErrorDetailC)]),
+    ("npa_prepare_host_tables", c_i32, [P(c_i64)]),
+    ("npa_prepare_device", c_i32, [c_i32]),
+    ("npa_dev_ln_1p", c_i32, [vp, c_i64, vp, vp]),
     ("npa_grid_validate", c_i32, [P(GridConfigC)]),
     ("npa_grid_cell_count", c_i32, [P(GridConfigC), P(c_i64)]),
     ("npa_feature_dims", c_i32, [P(GridConfigC), P(PerceptionOptionsC), c_i64, P(c_i64)]),
@@ -179,8 +187,12 @@ def lib() -> ctypes.CDLL:
 
 def check(status: int, where: str = "") -> None:
     if status != 0:
-        msg = lib().npa_last_error_message().decode(errors="replace")
-        raise _cfg.error_for(status, f"{where}: {msg}" if where else msg)
+        L = lib()
+        msg = L.npa_last_error_message().decode(errors="replace")
+        d = ErrorDetailC()
+        L.npa_last_error_detail(ctypes.byref(d))
+        detail = {"a": int(d.a), "b": int(d.b), "eps": float(d.eps)} if d.status == status else None
+        raise _cfg.error_for(status, f"{where}: {msg}" if where else msg, detail)
 
 
 def grid_c(cfg: _cfg.HashGridConfig) -> GridConfigC:

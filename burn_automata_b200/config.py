@@ -102,9 +102,27 @@ ERRORS_BY_CODE = {
 }
 
 
-def error_for(code: int, message: str = "") -> KernelError:
+# The fields each KernelError variant carries (config.rs:102-137), filled from
+# the C ABI's npa_last_error_detail: (attribute, source) pairs.
+PAYLOAD_FIELDS = {
+    1: (("dim", "a"),),
+    2: (("eps", "eps"),),
+    4: (("axis", "a"), ("value", "b")),
+    5: (("positions", "a"), ("expected", "b")),
+    6: (("states", "a"), ("expected", "b")),
+    7: (("actual", "a"), ("expected", "b")),
+}
+
+
+def error_for(code: int, message: str = "", detail=None) -> KernelError:
+    """The exception for a status code; `detail` (a = ..., b = ..., eps = ...)
+    becomes the variant's fields, e.g. OutputShape.actual / .expected."""
     cls = ERRORS_BY_CODE.get(int(code), KernelError)
-    return cls(message or STATUS_NAMES.get(int(code), f"status {code}"), int(code))
+    err = cls(message or STATUS_NAMES.get(int(code), f"status {code}"), int(code))
+    if detail is not None:
+        for attr, src in PAYLOAD_FIELDS.get(int(code), ()):
+            setattr(err, attr, detail[src])
+    return err
 
 
 @dataclass

@@ -53,12 +53,13 @@ __device__ __forceinline__ void spiky_delta_adjoint(const GridParams& g, const f
 
 // log_normalize_adjoint (normalize.rs:71-91) from a zero input adjoint.
 __device__ __forceinline__ void log_normalize_adjoint(const float (&in)[3], const float* out_adj,
-                                                      float (&in_adj)[3], int dim) {
+                                                      float (&in_adj)[3], int dim,
+                                                      const Log1pTable& l1p) {
   const float e = 1.0e-6f;
   float s = 0.0f;
   for (int a = 0; a < dim; ++a) s = s + in[a] * in[a];
   const float norm = fmaxf(sqrtf(s + e * e), e);
-  const float l = log1p_f32(norm);
+  const float l = log1p_host(norm, l1p);
   const float scale = l / norm;
   const float dscale = (norm / (1.0f + norm) - l) / (norm * norm);
   float dot = 0.0f;
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(128) adjoint_prep_kernel(AdjArgs A) {
       for (int a = 0; a < DIM; ++a) nin[a] = corrected[a] * A.p.state_scale;
       float cadj[3] = {0.0f, 0.0f, 0.0f};
       if (A.p.log_norm_grad)
-        log_normalize_adjoint(nin, gadj + ch * DIM, cadj, DIM);
+        log_normalize_adjoint(nin, gadj + ch * DIM, cadj, DIM, A.p.l1p);
       else
         for (int a = 0; a < DIM; ++a) cadj[a] = gadj[ch * DIM + a];
       for (int a = 0; a < DIM; ++a) cadj[a] = cadj[a] * A.p.state_scale;
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(128) adjoint_prep_kernel(AdjArgs A) {
     float nin[3] = {0.0f, 0.0f, 0.0f}, radj[3] = {0.0f, 0.0f, 0.0f};
     for (int a = 0; a < DIM; ++a) nin[a] = rawd[a] * A.p.density_scale;
     if (A.p.log_norm_density_grad) {
-      log_normalize_adjoint(nin, dadj, radj, DIM);
+      log_normalize_adjoint(nin, dadj, radj, DIM, A.p.l1p);
       for (int a = 0; a < DIM; ++a) radj[a] = radj[a] * A.p.density_scale;
     } else {
       for (int a = 0; a < DIM; ++a) radj[a] = dadj[a] * A.p.density_scale;
@@ -345,6 +346,8 @@ npa_status launch_perception_adjoint(const GridParams& g, const PerceptionParams
                                      float* density_adjoint, cudaStream_t stream) {
   const uint32_t total = batch * s.n;
   if (total == 0) return NPA_OK;
+  Log1pTable l1p{};
+  if (p.log_norm_grad || p.log_norm_density_grad) NPA_TRY(device_log1p_table(&l1p, stream));
   if (state_dims > 0)
     NPA_CUDA(cudaMemsetAsync(state_adjoint, 0, size_t(total) * state_dims * 4, stream),
              "cudaMemsetAsync");
@@ -353,6 +356,7 @@ npa_status launch_perception_adjoint(const GridParams& g, const PerceptionParams
   AdjArgs A;
   A.g = g;
   A.p = p;
+  A.p.l1p = l1p;
   A.s = s;
   A.inverse = inverse;
   A.states = states;

@@ -22,12 +22,22 @@
 namespace npa {
 
 static thread_local std::string g_last_error;
+static thread_local npa_error_detail g_last_detail{};
 static std::atomic<uint64_t> g_launches{0};
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
 npa_status fail(npa_status st, const std::string& msg) {
   set_error(msg);
+  g_last_detail = npa_error_detail{st, 0.0f, 0, 0};
+  return st;
+}
+
+// fail() with the payload the reference's KernelError variant carries.
+npa_status fail_with(npa_status st, const std::string& msg, int64_t a, int64_t b = 0,
+                     float eps = 0.0f) {
+  set_error(msg);
+  g_last_detail = npa_error_detail{st, eps, a, b};
   return st;
 }
 
@@ -63,9 +73,12 @@ static float powi_f32(float x, int n) {
 npa_status validate_grid(const npa_grid_config* cfg) {
   if (!cfg) return fail(NPA_ERR_INVALID_ARGUMENT, "grid config is null");
   if (!(cfg->dim == 2 || cfg->dim == 3))
-    return fail(NPA_ERR_INVALID_DIM, "expected spatial dim 2 or 3, got " + std::to_string(cfg->dim));
+    return fail_with(NPA_ERR_INVALID_DIM,
+                     "expected spatial dim 2 or 3, got " + std::to_string(cfg->dim), cfg->dim);
   if (!std::isfinite(cfg->eps) || cfg->eps <= 0.0f)
-    return fail(NPA_ERR_INVALID_EPS, "eps must be finite and positive");
+    return fail_with(NPA_ERR_INVALID_EPS,
+                     "eps must be finite and positive, got " + std::to_string(cfg->eps), 0, 0,
+                     cfg->eps);
   if (!(cfg->mode == NPA_MODE_GRID || cfg->mode == NPA_MODE_PARTICLE))
     return fail(NPA_ERR_INVALID_ARGUMENT, "unknown hashgrid mode");
   if (!(cfg->boundary == NPA_BOUNDARY_PERIODIC || cfg->boundary == NPA_BOUNDARY_CLAMPED))
@@ -74,9 +87,10 @@ npa_status validate_grid(const npa_grid_config* cfg) {
     const int64_t s = cfg->grid_size[axis];
     if (s <= 0) return fail(NPA_ERR_INVALID_GRID_SIZE, "grid sizes must be non-zero for active dimensions");
     if (cfg->mode == NPA_MODE_PARTICLE && (s & (s - 1)) != 0)
-      return fail(NPA_ERR_PARTICLE_MODE_REQUIRES_POW2,
-                  "particle hashgrid mode requires power-of-two grid size at axis " +
-                      std::to_string(axis) + ", got " + std::to_string(s));
+      return fail_with(NPA_ERR_PARTICLE_MODE_REQUIRES_POW2,
+                       "particle hashgrid mode requires power-of-two grid size at axis " +
+                           std::to_string(axis) + ", got " + std::to_string(s),
+                       axis, s);
   }
   int64_t cells = 1;
   for (int axis = 0; axis < cfg->dim; ++axis) {
@@ -149,20 +163,23 @@ npa_status check_shapes(int64_t positions_len, int64_t states_len, int64_t batch
                         int64_t c) {
   const int64_t expected = batch * n;
   if (positions_len != expected)
-    return fail(NPA_ERR_POSITION_SHAPE, "positions length " + std::to_string(positions_len) +
-                                            " does not match batch_size * particle_count " +
-                                            std::to_string(expected));
+    return fail_with(NPA_ERR_POSITION_SHAPE, "positions length " + std::to_string(positions_len) +
+                                                 " does not match batch_size * particle_count " +
+                                                 std::to_string(expected),
+                     positions_len, expected);
   if (states_len != expected * c)
-    return fail(NPA_ERR_STATE_SHAPE, "state length " + std::to_string(states_len) +
-                                         " does not match batch_size * particle_count * state_dims " +
-                                         std::to_string(expected * c));
+    return fail_with(NPA_ERR_STATE_SHAPE, "state length " + std::to_string(states_len) +
+                                              " does not match batch_size * particle_count * state_dims " +
+                                              std::to_string(expected * c),
+                     states_len, expected * c);
   return NPA_OK;
 }
 
 npa_status output_shape(int64_t actual, int64_t expected) {
   if (actual != expected)
-    return fail(NPA_ERR_OUTPUT_SHAPE, "output buffer length " + std::to_string(actual) +
-                                          " does not match expected " + std::to_string(expected));
+    return fail_with(NPA_ERR_OUTPUT_SHAPE, "output buffer length " + std::to_string(actual) +
+                                               " does not match expected " + std::to_string(expected),
+                     actual, expected);
   return NPA_OK;
 }
 
@@ -500,9 +517,33 @@ const char* npa_status_string(npa_status status) {
 
 const char* npa_last_error_message(void) { return g_last_error.c_str(); }
 
+npa_status npa_last_error_detail(npa_error_detail* out) {
+  if (!out) return NPA_ERR_INVALID_ARGUMENT;
+  *out = g_last_detail;
+  return NPA_OK;
+}
+
 uint64_t npa_kernel_launch_count(void) { return g_launches.load(); }
 
 uint64_t npa_bulk_copy_timeouts(void) { return bulk_copy_timeouts(); }
+
+npa_status npa_prepare_host_tables(int64_t* ln_1p_exceptions) {
+  NPA_TRY(prepare_host_log1p());
+  if (ln_1p_exceptions) *ln_1p_exceptions = int64_t(host_log1p_exceptions());
+  return NPA_OK;
+}
+
+npa_status npa_prepare_device(int32_t device) {
+  NPA_TRY(ensure_device(device));
+  Log1pTable l1p;
+  return device_log1p_table(&l1p);
+}
+
+npa_status npa_dev_ln_1p(const float* d_x, int64_t count, float* d_out, void* stream) {
+  if (count < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "count must be >= 0");
+  if (count > 0 && (!d_x || !d_out)) return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  return launch_ln_1p(d_x, uint64_t(count), d_out, static_cast<cudaStream_t>(stream));
+}
 
 // Test hook for the out-of-memory path of the host-buffer entry points.
 void npa_debug_set_allocation_cap(uint64_t bytes) { g_alloc_cap.store(bytes); }
@@ -545,7 +586,10 @@ npa_status npa_build_hashgrid(const npa_grid_config* cfg, const float* positions
   NPA_TRY(validate_grid(cfg));
   NPA_TRY(check_counts(batch, n));
   if (positions_len != batch * n)
-    return fail(NPA_ERR_POSITION_SHAPE, "positions length does not match batch_size * particle_count");
+    return fail_with(NPA_ERR_POSITION_SHAPE,
+                     "positions length " + std::to_string(positions_len) +
+                         " does not match batch_size * particle_count " + std::to_string(batch * n),
+                     positions_len, batch * n);
   NPA_TRY(check_bins(cfg, batch));
   const GridParams g = make_grid_params(*cfg);
   NPA_TRY(output_shape(bin_offsets_len, batch * int64_t(g.cells) + 1));
@@ -664,7 +708,11 @@ npa_status npa_decode_gaussians_3d(const npa_gaussian_decode_config* cfg, const 
   if (positions_len < 0 || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "negative length");
   // assert_eq!(positions.len() * state_dims, states.len()) (gaussian.rs:59)
   if (positions_len * state_dims != states_len)
-    return fail(NPA_ERR_STATE_SHAPE, "states length does not match positions * state_dims");
+    return fail_with(NPA_ERR_STATE_SHAPE,
+                     "states length " + std::to_string(states_len) +
+                         " does not match positions * state_dims " +
+                         std::to_string(positions_len * state_dims),
+                     states_len, positions_len * state_dims);
   NPA_TRY(validate_decode(cfg, state_dims));
   if (positions_len > int64_t(kMaxParticles)) return fail(NPA_ERR_UNSUPPORTED, "too many particles");
   NPA_TRY(output_shape(out_len, positions_len * record_floats(cfg)));
@@ -720,6 +768,12 @@ npa_status npa_model_create(const npa_model_config* cfg, const float* w1, int64_
       return fail(NPA_ERR_UNSUPPORTED, "update dims too large for the MLP's hidden width");
   }
   NPA_TRY(ensure_device(device));
+  if (cfg->log_norm_grad || cfg->log_norm_density_grad) {
+    // the log-normalisation's log1pf tables, uploaded now so that later steps
+    // (and executor graph captures) find them on the device
+    Log1pTable l1p;
+    NPA_TRY(device_log1p_table(&l1p));
+  }
   const int64_t Hp = hidden_padded_for(int(H));
   std::vector<float> w1t(size_t(F) * Hp, 0.0f);
   for (int64_t h = 0; h < H; ++h)
@@ -802,16 +856,21 @@ npa_status npa_model_forward_update_from_features(npa_model* m, const float* fea
   return s.finish();
 }
 
-// After a synchronising call that ran the MLP step kernel: NPA_ERR_CUDA when
-// the device's count of feature-tile copies that missed their bounded wait has
-// grown since the last check (those blocks left their tiles undone).
-static std::atomic<uint64_t> g_bulk_timeouts_seen{0};
+// After a synchronising call that ran the MLP step kernel on the current
+// device: NPA_ERR_TIMEOUT when that device's count of feature-tile copies that
+// missed their bounded wait has grown since the last check on that device
+// (those blocks left their tiles undone).  One watermark per device ordinal.
+static std::mutex g_bulk_mu;
+static std::vector<uint64_t> g_bulk_timeouts_seen;
 static npa_status check_bulk_copies() {
+  int dev = 0;
+  NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   const uint64_t now = bulk_copy_timeouts();
-  uint64_t seen = g_bulk_timeouts_seen.load();
-  if (now <= seen) return NPA_OK;
-  g_bulk_timeouts_seen.compare_exchange_strong(seen, now);
-  return fail(NPA_ERR_CUDA, "an MLP feature-tile copy did not complete within its bounded wait");
+  std::lock_guard<std::mutex> lock(g_bulk_mu);
+  if (dev >= int(g_bulk_timeouts_seen.size())) g_bulk_timeouts_seen.resize(dev + 1, 0);
+  if (now <= g_bulk_timeouts_seen[dev]) return NPA_OK;
+  g_bulk_timeouts_seen[dev] = now;
+  return fail(NPA_ERR_TIMEOUT, "an MLP feature-tile copy did not complete within its bounded wait");
 }
 
 // Reserves `bytes` of the model's host-call arena (caller holds m->mu).
@@ -1341,6 +1400,10 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   if (!mlp_step_supported(m->dm))
     return fail(NPA_ERR_UNSUPPORTED, "step shape outside the supported range");
   NPA_TRY(ensure_device(m->dm.device));
+  if (m->dm.log_norm_grad || m->dm.log_norm_density_grad) {
+    Log1pTable l1p;  // uploaded before any step is captured into a graph
+    NPA_TRY(device_log1p_table(&l1p));
+  }
   npa_executor* e = new npa_executor();
   e->model = m;
   e->grid = *grid;

@@ -19,6 +19,9 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
+
+#include <cuda.h>
 
 #include "npa_internal.h"
 
@@ -449,21 +452,55 @@ constexpr size_t kStaticScratchBytes = size_t(6656) * 1024;  // 6.5 MiB
 
 __device__ __align__(256) unsigned char g_hashgrid_static_scratch[kStaticScratchBytes];
 
+// The array's address belongs to a CUDA context: after cudaDeviceReset, or
+// with a caller-created (non-primary) context current, a cached address would
+// be stale, so the cache is keyed on the current context, not the ordinal.
+struct StaticAddress {
+  int device;
+  CUcontext ctx;
+  void* ptr;
+};
 std::mutex g_static_mu;
-void* g_static_ptr[128] = {};
+std::vector<StaticAddress> g_static_addresses;
 
-// Device address of the array on the current device, looked up once per device.
+npa_status current_context(CUcontext* out) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  static GetCurrent fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    NPA_CUDA(cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q),
+             "cudaGetDriverEntryPoint(cuCtxGetCurrent)");
+    if (q != cudaDriverEntryPointSuccess || !p)
+      return fail(NPA_ERR_CUDA, "cuCtxGetCurrent is not available");
+    fn = reinterpret_cast<GetCurrent>(p);
+  }
+  if (fn(out) != CUDA_SUCCESS) return fail(NPA_ERR_CUDA, "cuCtxGetCurrent failed");
+  return NPA_OK;
+}
+
+// Device address of the array in the current context, looked up once per
+// (device, context) with that device current.  The first call on a device
+// makes the CUDA runtime load this library's module there; make it before
+// any stream capture on that device.
 npa_status static_scratch_address(void** out) {
   int dev = 0;
   NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  if (dev < 0 || dev >= 128) return fail(NPA_ERR_UNSUPPORTED, "device ordinal above 127");
+  CUcontext ctx = nullptr;
+  NPA_TRY(current_context(&ctx));
   std::lock_guard<std::mutex> lock(g_static_mu);
-  if (!g_static_ptr[dev]) {
-    void* p = nullptr;
-    NPA_CUDA(cudaGetSymbolAddress(&p, g_hashgrid_static_scratch), "cudaGetSymbolAddress");
-    g_static_ptr[dev] = p;
-  }
-  *out = g_static_ptr[dev];
+  if (ctx)
+    for (const StaticAddress& a : g_static_addresses)
+      if (a.device == dev && a.ctx == ctx) {
+        *out = a.ptr;
+        return NPA_OK;
+      }
+  void* p = nullptr;
+  // Also makes the device's primary context current when none was.
+  NPA_CUDA(cudaGetSymbolAddress(&p, g_hashgrid_static_scratch), "cudaGetSymbolAddress");
+  NPA_TRY(current_context(&ctx));
+  g_static_addresses.push_back(StaticAddress{dev, ctx, p});
+  *out = p;
   return NPA_OK;
 }
 
@@ -477,16 +514,17 @@ extern "C" npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg,
                                                      uint32_t* d_inverse_permutation,
                                                      void* stream) {
   using namespace npa;
-  NPA_TRY(validate_grid(cfg));
-  if (batch < 0 || n < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "batch and particle count must be >= 0");
+  // The same checks, in the same order, as npa_dev_build_hashgrid (through
+  // its workspace query); the only added status is NPA_ERR_UNSUPPORTED above
+  // the fixed array's particle limit.
+  size_t workspace_equivalent = 0;
+  NPA_TRY(npa_dev_hashgrid_workspace_size(cfg, batch, n, &workspace_equivalent));
   if (batch > 0 && uint64_t(n) > kStaticMaxParticles / uint64_t(batch))
     return fail(NPA_ERR_UNSUPPORTED,
                 "batch * particle_count = " + std::to_string(uint64_t(batch) * uint64_t(n)) +
                     " exceeds the allocation-free hashgrid limit of " +
                     std::to_string(kStaticMaxParticles) + " particles");
   const GridParams g = make_grid_params(*cfg);
-  if (batch > 0 && uint64_t(g.cells) > uint64_t(0xFFFFFFFEu) / uint64_t(batch))
-    return fail(NPA_ERR_UNSUPPORTED, "batch * cell_count + 1 does not fit in uint32");
   const uint32_t B = uint32_t(batch), N = uint32_t(n), total = B * N;
   if (!d_bin_offsets || (total > 0 && (!d_positions || !d_permutation || !d_inverse_permutation)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");

@@ -237,21 +237,53 @@ __device__ __forceinline__ void safe_inverse_symmetric(const float* m, int dim, 
   out[8] = (a * d - b * b) * inv_det;
 }
 
-// ln(1 + x) rounded once to f32: evaluated in f64 (CUDA's log1p) and
-// converted.  The reference calls the host libm's log1pf, which is within one
-// ulp of this value.
-__device__ __forceinline__ float log1p_f32(float x) {
-  return static_cast<float>(log1p(static_cast<double>(x)));
+// The host C library's log1pf, bit for bit (f32::ln_1p of the reference; the
+// tables and how they are built: host_log1p.cu).  ln(1 + x) is evaluated in
+// f64 and rounded once to f32 (c); one bit per float says where the host
+// returns another value (then the neighbour of c on the side of the f64 value),
+// and a short list holds the inputs whose result is stored outright.
+struct Log1pTable {
+  const uint32_t* bits;  // bit (u - base) set where the host result is not c
+  const uint2* side;     // {input bits, host result bits}, nside entries
+  uint32_t base;         // bits of the smallest tabulated input
+  uint32_t nbits;        // tabulated inputs: [base, base + nbits)
+  int nside;
+  float min_input;       // inputs below are not tabulated (c is returned)
+};
+
+// The bitmap word holding input x's bit (0 when x is not tabulated); loaded
+// apart from log1p_host_word so that callers can issue several loads at once.
+__device__ __forceinline__ uint32_t log1p_word(float x, const Log1pTable& t) {
+  const uint32_t i = __float_as_uint(x) - t.base;
+  if (!t.bits || !(x >= t.min_input) || !(i < t.nbits)) return 0u;
+  return __ldg(t.bits + (i >> 5));
 }
 
-// log_normalize_vector (normalize.rs:60-69) on `len` (2 or 3) values.
-__device__ __forceinline__ void log_normalize(float* v, int len) {
-  float s = 0.0f;
-  for (int i = 0; i < len; ++i) s = s + v[i] * v[i];
-  const float e = 1.0e-6f;
-  float norm = fmaxf(sqrtf(s + e * e), e);
-  float scale = log1p_f32(norm) / norm;
-  for (int i = 0; i < len; ++i) v[i] = v[i] * scale;
+// log1pf(x) of the host given x's bitmap word (from log1p_word).
+__device__ __forceinline__ float log1p_host_word(float x, uint32_t word, const Log1pTable& t) {
+  const double v = log1p(static_cast<double>(x));
+  const float c = static_cast<float>(v);
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t i = u - t.base;
+  if (!t.bits || !(x >= t.min_input) || !(i < t.nbits)) return c;
+  const bool differs = (word >> (i & 31u)) & 1u;
+  const uint32_t cb = __float_as_uint(c);
+  const double cd = c;
+  const float o = __uint_as_float(cd < v ? cb + 1u : cb - 1u);  // c > 0 here
+  const double gap = fabs(static_cast<double>(o) - cd);
+  const bool near = fabs(v - 0.5 * (cd + static_cast<double>(o))) < 5e-9 * gap;
+  float r = differs ? o : c;
+  if (differs || near) {
+    for (int k = 0; k < t.nside; ++k) {
+      const uint2 e = __ldg(t.side + k);
+      if (e.x == u) r = __uint_as_float(e.y);
+    }
+  }
+  return r;
+}
+
+__device__ __forceinline__ float log1p_host(float x, const Log1pTable& t) {
+  return log1p_host_word(x, log1p_word(x, t), t);
 }
 
 // f32::clamp (NaN passes through).

@@ -68,6 +68,19 @@ npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_
                            uint32_t n, const HashgridBuffers& out, void* scratch,
                            size_t scratch_bytes, cudaStream_t stream);
 
+// ---- the host libm's log1pf on the device (host_log1p.cu) ----
+// Builds (or loads from its cache) the host-side list of inputs where the host
+// log1pf differs from the correctly rounded value.
+npa_status prepare_host_log1p();
+// The current device's lookup tables, uploaded on the first call on that
+// device.  That first call allocates and copies, so it fails (instead of
+// breaking a capture) when `stream` is capturing.
+npa_status device_log1p_table(Log1pTable* out, cudaStream_t stream = nullptr);
+// Number of tabulated inputs whose host result differs from the correctly rounded one.
+size_t host_log1p_exceptions();
+// out[i] = the host libm's log1pf(x[i]) computed on the device.
+npa_status launch_ln_1p(const float* x, uint64_t count, float* out, cudaStream_t stream);
+
 // ---- perception (perception.cu) ----
 struct PerceptionParams {
   int state_grad, density_grad, scale_eq, pde, log_norm_grad, log_norm_density_grad, hybrid,
@@ -76,6 +89,7 @@ struct PerceptionParams {
   float density_scale;  // normalize_density_gradient scale (normalize.rs:38-46)
   int feature_dims;
   int vec_states;       // state rows may be read as float4 (16-byte aligned, C % 4 == 0)
+  Log1pTable l1p;       // the host libm's log1pf on this device (set by the launchers)
 };
 PerceptionParams make_perception_params(const GridParams& g, const npa_perception_options& o,
                                         uint32_t n, int state_dims);

@@ -252,6 +252,7 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
   if (total == 0) return NPA_OK;
   PerceptionParams pp = p;
   pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+  if (p.log_norm_grad || p.log_norm_density_grad) NPA_TRY(device_log1p_table(&pp.l1p, stream));
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(total) * chunks, 128);
@@ -289,6 +290,7 @@ npa_status launch_perception_tiles(const GridParams& g, const PerceptionParams& 
   if (q_end <= q_begin) return NPA_OK;
   PerceptionParams pp = p;
   pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+  if (p.log_norm_grad || p.log_norm_density_grad) NPA_TRY(device_log1p_table(&pp.l1p, stream));
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(q_end - q_begin) * chunks, 128);

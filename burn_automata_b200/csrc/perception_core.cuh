@@ -22,24 +22,37 @@ struct PerceptionAcc {
   float dgrad[DIM];
 };
 
-// log1p(norm) / norm of a squared norm s (normalize.rs:60-69).  Out of line:
-// one copy of the f64 log1p, square root and division serves every channel;
-// inlined per channel they crowded the perception kernels out of the
-// instruction cache (measured 0.437 -> 0.406 ms on cfg2's perception).
-__device__ __noinline__ float log_norm_scale(float s) {
-  const float e = 1.0e-6f;
-  const float norm = fmaxf(sqrtf(s + e * e), e);
-  return log1p_f32(norm) / norm;
+// log_normalize_vector (normalize.rs:60-69) on every channel of a chunk:
+//   norm = max(sqrt(|v|^2 + 1e-12), 1e-6);  v *= ln_1p(norm) / norm
+// with the host libm's log1pf (log1p_host_word).  The norms come first and
+// their lookup words are loaded together, so the loads' latencies overlap;
+// the f64 log1p, the correction and the division stay out of line (one copy
+// serves every channel: inlined per channel they crowded the perception
+// kernels out of the instruction cache, cfg2 perception 0.437 -> 0.406 ms).
+__device__ __noinline__ float log_norm_scale(float norm, uint32_t word, const Log1pTable t) {
+  return log1p_host_word(norm, word, t) / norm;
 }
 
-template <int DIM>
-__device__ __forceinline__ void log_normalize_n(float (&v)[DIM]) {
-  float s = 0.0f;
+template <int DIM, int N>
+__device__ __forceinline__ void log_normalize_rows(float (&v)[N][DIM], const Log1pTable& t) {
+  const float e = 1.0e-6f;
+  float norm[N];
+  uint32_t word[N];
 #pragma unroll
-  for (int i = 0; i < DIM; ++i) s = s + v[i] * v[i];
-  const float scale = log_norm_scale(s);
+  for (int c = 0; c < N; ++c) {
+    float s = 0.0f;
 #pragma unroll
-  for (int i = 0; i < DIM; ++i) v[i] = v[i] * scale;
+    for (int i = 0; i < DIM; ++i) s = s + v[c][i] * v[c][i];
+    norm[c] = fmaxf(sqrtf(s + e * e), e);
+  }
+#pragma unroll
+  for (int c = 0; c < N; ++c) word[c] = log1p_word(norm[c], t);
+#pragma unroll
+  for (int c = 0; c < N; ++c) {
+    const float scale = log_norm_scale(norm[c], word[c], t);
+#pragma unroll
+    for (int i = 0; i < DIM; ++i) v[c][i] = v[c][i] * scale;
+  }
 }
 
 // Accumulators of one particle's chunk plus the moment matrix.
@@ -162,16 +175,22 @@ __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkSta
       }
     }
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
+    for (int c = 0; c < CH; ++c)
 #pragma unroll
       for (int a = 0; a < DIM; ++a) st.acc.sgrad[c][a] = st.acc.sgrad[c][a] * p.state_scale;
-      if (p.log_norm_grad) log_normalize_n<DIM>(st.acc.sgrad[c]);
-    }
+    if (p.log_norm_grad) log_normalize_rows<DIM, CH>(st.acc.sgrad, p.l1p);
   }
   if (dg) {
 #pragma unroll
     for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = st.acc.dgrad[a] * p.density_scale;
-    if (p.log_norm_density_grad) log_normalize_n<DIM>(st.acc.dgrad);
+    if (p.log_norm_density_grad) {
+      float row[1][DIM];
+#pragma unroll
+      for (int a = 0; a < DIM; ++a) row[0][a] = st.acc.dgrad[a];
+      log_normalize_rows<DIM, 1>(row, p.l1p);
+#pragma unroll
+      for (int a = 0; a < DIM; ++a) st.acc.dgrad[a] = row[0][a];
+    }
   }
 }
 

@@ -4,17 +4,20 @@ Batches of independent rollouts (the reference keeps them as separate lanes:
 crates/burn_automata_kernels/src/hashgrid.rs:33-58) shard across GPUs with no
 exchange on the step path.  This module holds the rank plumbing around that:
 shard assignment, process-group set-up with a short timeout, the
-max-over-ranks reduction used for timing, and one optional gather of
-per-shard checksums of the final states for validation.  Nothing here runs
-inside the timed region.
+max-over-ranks reduction used for timing, and one gather of per-rollout
+digests of the final states, which rank 0 compares with a 1-GPU rerun of
+the same rollouts (rollouts are independent and the kernels deterministic,
+so a sharded run reproduces it bit for bit).  Nothing here runs inside the
+timed region.
 """
 
 from __future__ import annotations
 
+import hashlib
 import os
 from dataclasses import dataclass
 from datetime import timedelta
-from typing import Optional, Tuple
+from typing import Dict, Iterable, List, Optional, Tuple
 
 import numpy as np
 
@@ -77,26 +80,53 @@ def max_over_ranks(values, device=None):
     return [float(v) for v in t.cpu()]
 
 
-def shard_checksum(positions: np.ndarray, states: np.ndarray) -> Tuple[float, float]:
-    """Order-dependent float64 checksums of a shard's final particles."""
-    p = np.asarray(positions, np.float64).reshape(-1)
-    s = np.asarray(states, np.float64).reshape(-1)
-    wp = np.arange(1, p.size + 1, dtype=np.float64)
-    ws = np.arange(1, s.size + 1, dtype=np.float64)
-    return float(np.dot(p, 1.0 / wp)), float(np.dot(s, 1.0 / ws))
+def rollout_digests(batch: int, first: int, positions: np.ndarray,
+                    states: np.ndarray) -> Dict[int, str]:
+    """{global rollout index: 64-bit digest of that rollout's bytes}.
+
+    positions / states hold `batch` consecutive rollouts (any per-rollout
+    layout: each array splits evenly into `batch` rows).  Equal digests mean
+    bit-identical rollouts."""
+    p = np.ascontiguousarray(positions).reshape(batch, -1)
+    s = np.ascontiguousarray(states).reshape(batch, -1)
+    return {first + b: hashlib.blake2b(p[b].tobytes() + s[b].tobytes(),
+                                       digest_size=8).hexdigest() for b in range(batch)}
 
 
-def gather_checksums(local: Tuple[float, float], device=None):
-    """All ranks' checksums, in rank order (one all_gather, after timing)."""
+def compare_digests(gathered: Iterable[Dict[int, str]],
+                    expected: Dict[int, str]) -> Tuple[int, List[int]]:
+    """(rollouts checked, rollouts whose digest differs from `expected` or
+    that `expected` lacks), over every rank's gathered digests."""
+    got: Dict[int, str] = {}
+    for d in gathered:
+        got.update(d)
+    bad = sorted(k for k, v in got.items() if expected.get(k) != v)
+    return len(got), bad
+
+
+def gather_floats(value: float, device=None):
+    """Every rank's `value`, in rank order (one all_gather, outside timing)."""
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor(list(local), dtype=torch.float64, device=device)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     if not (dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1):
-        return [tuple(float(v) for v in t.cpu())]
+        return [float(t.item())]
     out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
     dist.all_gather(out, t)
-    return [tuple(float(v) for v in o.cpu()) for o in out]
+    return [float(o.item()) for o in out]
+
+
+def gather_objects(obj):
+    """Every rank's picklable `obj`, in rank order (validation data only: one
+    all_gather_object after the timed region)."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1):
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out
 
 
 def barrier_or_fail(timeout_s: Optional[float] = None) -> None:

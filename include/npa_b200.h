@@ -22,8 +22,8 @@
  *    the matching *_workspace_size query.
  *  - Arithmetic follows the reference's f32 operation order: no FMA
  *    contraction, sequential sums in the reference's loop order, IEEE division
- *    and square root.  log1p is correctly rounded (the reference calls the host
- *    libm's log1pf, which is not).
+ *    and square root.  f32::ln_1p is the host C library's log1pf, bit for bit
+ *    (see npa_prepare_host_tables).
  *  - Every call returns an npa_status; nothing aborts the process.
  */
 #ifndef NPA_B200_H
@@ -54,7 +54,7 @@ enum {
   NPA_ERR_INVALID_ARGUMENT = 8,              /* KernelError / AutomataError::InvalidArgument */
   NPA_ERR_INVALID_MODEL = 9,                 /* AutomataError::InvalidModel */
   NPA_ERR_CUDA = 20,                         /* a CUDA runtime call failed */
-  NPA_ERR_DEVICE_STATUS = 21,                /* a kernel flagged an error in its status word */
+  NPA_ERR_DEVICE_STATUS = 21,                /* reserved: no entry point returns it */
   NPA_ERR_TIMEOUT = 22,                      /* a bounded device-side wait gave up */
   NPA_ERR_OUT_OF_MEMORY = 23,                /* an allocation failed (or hit the cap) */
   NPA_ERR_UNSUPPORTED = 24,                  /* shape outside what the kernels support */
@@ -159,9 +159,47 @@ uint64_t npa_kernel_launch_count(void);
  * complete within their bounded wait on the current device (0 in a healthy
  * run; a block that gives up leaves its remaining tiles undone).  The
  * synchronising host calls (npa_model_step, npa_model_run_rollout*,
- * npa_executor_read_state) return NPA_ERR_CUDA when this count has grown
- * since the last such check. */
+ * npa_executor_read_state) return NPA_ERR_TIMEOUT when this device's count
+ * has grown since the last such check on the device. */
 uint64_t npa_bulk_copy_timeouts(void);
+
+/* The payload of the last error on the calling thread, as the reference's
+ * KernelError variants carry it (crates/burn_automata_kernels/src/config.rs:
+ * 102-137): InvalidDim(dim) -> a = dim; InvalidEps(eps) -> eps;
+ * ParticleModeRequiresPowerOfTwo { axis, value } -> a = axis, b = value;
+ * PositionShape { positions, expected }, StateShape { states, expected } and
+ * OutputShape { actual, expected } -> a = the given length, b = expected;
+ * InvalidArgument(String) / AutomataError::InvalidModel(String) -> the text of
+ * npa_last_error_message.  status is the code that error returned (NPA_OK
+ * before any error); fields a variant does not carry are 0. */
+typedef struct npa_error_detail {
+  npa_status status;
+  float eps;
+  int64_t a;
+  int64_t b;
+} npa_error_detail;
+npa_status npa_last_error_detail(npa_error_detail* out);
+
+/* The host C library's log1pf (the reference's f32::ln_1p, which its
+ * log-normalisation calls: crates/burn_automata_kernels/src/reference/
+ * normalize.rs:60-69) is reproduced bit for bit on the device: ln(1 + x) in
+ * f64, rounded once, corrected where the host's log1pf returns the
+ * neighbouring float.  Those inputs are found by calling the host's log1pf on
+ * every float in [1e-6, inf); the list is cached next to the library file
+ * (libnpa_b200.so.log1pf, checked against the running host when read) and
+ * uploaded to each device on first use (64 MiB + 32 KiB, held until exit).
+ *
+ * npa_prepare_host_tables builds or loads that list (about 17 CPU-seconds
+ * when no valid cache exists) and reports its length.  npa_prepare_device
+ * uploads it to `device`; npa_model_create / npa_executor_create do so for
+ * models that log-normalise, and the perception entry points on first use.
+ * The upload allocates, so a first use inside a stream capture returns
+ * NPA_ERR_INVALID_ARGUMENT: call npa_prepare_device before capturing. */
+npa_status npa_prepare_host_tables(int64_t* ln_1p_exceptions);
+npa_status npa_prepare_device(int32_t device);
+/* f32::ln_1p as above on device buffers: d_out[i] = log1pf(d_x[i]) of the host
+ * C library, bit for bit for x >= 1e-6 (below, the correctly rounded value). */
+npa_status npa_dev_ln_1p(const float* d_x, int64_t count, float* d_out, void* stream);
 
 /* HashGridConfig::validate (config.rs:65-84). */
 npa_status npa_grid_validate(const npa_grid_config* cfg);

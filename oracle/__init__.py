@@ -145,6 +145,7 @@ def lib():
         L.ora_feature_dims.restype = i64
         L.ora_perceive.argtypes = [P(_Grid), P(_Opt), f32p, f32p, i64, i64, i64, f32p, f32p,
                                    f32p, f32p, f32p]
+        L.ora_moment_det.argtypes = [P(_Grid), f32p, i64, i64, f32p]
         L.ora_forward_update.argtypes = [f32p, i64, i64, i64, i64, f32p, f32p, f32p, f32p, f32p]
         L.ora_euler_step.argtypes = [P(_Grid), f32p, f32p, f32p, f32p, i64, i64, i64,
                                      ctypes.c_float, f32p, f32p, f32p]
@@ -167,9 +168,34 @@ def lib():
         L.ora_chacha_block.argtypes = [u32p, ctypes.c_uint64, ctypes.c_int, u32p]
         L.ora_rollout_masks.argtypes = [ctypes.c_uint64, ctypes.c_float, i64, i64, i64, f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
+        L.ora_set_log1p_mode.argtypes = [ctypes.c_int]
+        L.ora_ln_1p.argtypes = [f32p, i64, f32p]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
     return _lib
+
+
+def ln_1p(x) -> np.ndarray:
+    """f32::ln_1p as the reference binds it: the host C library's log1pf."""
+    a = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.empty_like(a)
+    lib().ora_ln_1p(_ptr(a), a.shape[0], _ptr(out))
+    return out
+
+
+class device_log1p:
+    """Context: the oracle's ln_1p evaluated as the device library does (f64
+    log1p rounded once to f32) instead of the reference's libm log1pf.  With
+    it the whole rollout path, log-normalisation included, is predicted bit
+    for bit; outside it the oracle is the reference's arithmetic."""
+
+    def __enter__(self):
+        lib().ora_set_log1p_mode(1)
+        return self
+
+    def __exit__(self, *exc):
+        lib().ora_set_log1p_mode(0)
+        return False
 
 
 def set_threads(n: int) -> None:
@@ -286,6 +312,17 @@ def perceive_with_options(positions, states, batch: int, n: int, c: int, cfg, op
         "density_gradient": dgrad if dgrad is not None else np.zeros(0, np.float32),
         "feature_dims": fd,
     }
+
+
+def moment_determinants(positions, batch: int, n: int, cfg) -> np.ndarray:
+    """det of each particle's hybrid moment matrix (moment_matrix,
+    forward.rs:357-382), as safe_inverse_symmetric (kernels.rs:3-51) forms it."""
+    g = grid_struct(cfg)
+    pos = _f32(positions).reshape(-1, 4)
+    det = np.zeros(batch * n, dtype=np.float32)
+    _check(lib().ora_moment_det(ctypes.byref(g), _ptr(pos), batch, n, _ptr(det)),
+           "moment_det")
+    return det
 
 
 def forward_update(features, rows: int, in_dims: int, hidden: int, out_dims: int, w1, b1, w2, b2):

@@ -34,8 +34,25 @@
 static const float ORA_PI = 3.14159274101257324219f; /* std::f32::consts::PI */
 
 static int g_threads = 0;
+/* 0: f32::ln_1p as the reference binds it (the host libm's log1pf);
+ * 1: ln(1 + x) evaluated in f64 and rounded once to f32, the CUDA library's
+ *    choice.  Mode 1 predicts the device's arithmetic exactly, so the GPU
+ *    can be compared bit for bit even with log-normalisation on; mode 0 is
+ *    the reference and the default. */
+static int g_log1p_mode = 0;
 
 void ora_set_threads(int threads) { g_threads = threads; }
+void ora_set_log1p_mode(int mode) { g_log1p_mode = mode; }
+
+static float ln_1p_f32(float x) {
+  return g_log1p_mode ? (float)log1p((double)x) : log1pf(x);
+}
+
+/* f32::ln_1p as the reference binds it (the host libm's log1pf), elementwise. */
+void ora_ln_1p(const float* x, int64_t count, float* out) {
+#pragma omp parallel for schedule(static) num_threads(ora_get_threads())
+  for (int64_t i = 0; i < count; ++i) out[i] = log1pf(x[i]);
+}
 
 int ora_get_threads(void) {
 #ifdef _OPENMP
@@ -434,7 +451,7 @@ static void log_normalize_vector(float* v, int len) {
   for (int i = 0; i < len; ++i) s = s + v[i] * v[i];
   const float e = 1.0e-6f;
   float norm = maxf_rs(sqrtf(s + e * e), e);
-  float scale = log1pf(norm) / norm;
+  float scale = ln_1p_f32(norm) / norm;
   for (int i = 0; i < len; ++i) v[i] = v[i] * scale;
 }
 
@@ -595,6 +612,68 @@ done:
   free(blurred);
   free(sgrad);
   free(dgrad);
+  return st;
+}
+
+/* Determinant of each particle's hybrid moment matrix M_i = sum over j != i of
+ * delta (x) spiky(V_j) (moment_matrix, forward.rs:357-382; V_j =
+ * recip_finite(density_j)), computed as safe_inverse_symmetric
+ * (kernels.rs:3-51) computes it before comparing |det| with its 1e-3 switch.
+ * Test infrastructure: the parity tests count particles whose det lies near
+ * the switch, where a last-bit difference in M can flip the branch. */
+int ora_moment_det(const ora_grid_config* cfg, const float* positions, int64_t batch, int64_t n,
+                   float* det_out) {
+  int st = check_shapes_basic(batch, n, 0);
+  if (st) return st;
+  st = ora_grid_validate(cfg);
+  if (st) return st;
+  const int dim = cfg->dim;
+  const int64_t total = batch * n;
+  const int64_t cells = ora_cell_count(cfg);
+  int64_t* offsets = (int64_t*)malloc((size_t)(batch * cells + 1) * sizeof(int64_t));
+  int64_t* perm = (int64_t*)malloc((size_t)(total > 0 ? total : 1) * sizeof(int64_t));
+  int64_t* inv = (int64_t*)malloc((size_t)(total > 0 ? total : 1) * sizeof(int64_t));
+  float* density = (float*)malloc((size_t)(total > 0 ? total : 1) * sizeof(float));
+  if (!offsets || !perm || !inv || !density) {
+    st = ORA_ERR_INVALID_ARGUMENT;
+    goto done;
+  }
+  st = ora_build_hashgrid(cfg, positions, batch, n, offsets, perm, inv);
+  if (st) goto done;
+  walk_ctx w = {cfg, positions, offsets, perm, n, cells, cfg->eps * cfg->eps};
+  sph_consts k = make_sph(cfg);
+#pragma omp parallel for schedule(dynamic, 256) num_threads(ora_get_threads())
+  for (int64_t idx = 0; idx < total; ++idx) {
+    float rho = 0.0f;
+    FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, { (void)j; (void)delta; rho = rho + poly6(r2, &k); });
+    density[idx] = rho;
+  }
+#pragma omp parallel for schedule(dynamic, 256) num_threads(ora_get_threads())
+  for (int64_t idx = 0; idx < total; ++idx) {
+    float m[9] = {0};
+    FOR_EACH_NEIGHBOR(&w, idx, j, delta, r2, {
+      if (j != idx) {
+        float gv[4];
+        spiky(delta, r2, &k, recip_finite(density[j]), gv);
+        for (int r = 0; r < dim; ++r)
+          for (int col = 0; col < dim; ++col) m[r * dim + col] = m[r * dim + col] + delta[r] * gv[col];
+      }
+    });
+    if (dim == 2) {
+      det_out[idx] = m[0] * m[3] - m[1] * m[1];
+    } else {
+      float a = m[0], b = m[1], c = m[2], d = m[4], e = m[5], f = m[8];
+      float t1 = d * f - e * e;
+      float t2 = c * e - b * f;
+      float t3 = b * e - c * d;
+      det_out[idx] = a * t1 + b * t2 + c * t3;
+    }
+  }
+done:
+  free(offsets);
+  free(perm);
+  free(inv);
+  free(density);
   return st;
 }
 
@@ -1116,7 +1195,7 @@ static void log_normalize_adjoint(const float* input, const float* out_adj, floa
   float s = 0.0f;
   for (int i = 0; i < len; ++i) s = s + input[i] * input[i];
   const float norm = maxf_rs(sqrtf(s + e * e), e);
-  const float l = log1pf(norm);
+  const float l = ln_1p_f32(norm);
   const float scale = l / norm;
   const float dscale = (norm / (1.0f + norm) - l) / (norm * norm);
   float dot = 0.0f;

@@ -122,6 +122,11 @@ int ora_perceive(const ora_grid_config* cfg, const ora_perception_options* opt,
                  float* blurred_state, float* state_gradient,
                  float* density_gradient);
 
+/* Per-particle determinant of the hybrid moment matrix, as
+ * safe_inverse_symmetric computes it (test infrastructure). */
+int ora_moment_det(const ora_grid_config* cfg, const float* positions, int64_t batch, int64_t n,
+                   float* det_out);
+
 int ora_forward_update(const float* features, int64_t rows, int64_t in_dims,
                        int64_t hidden_dims, int64_t out_dims, const float* w1,
                        const float* b1, const float* w2, const float* b2,
@@ -191,6 +196,11 @@ void ora_chacha_block(const uint32_t key[8], uint64_t counter, int rounds, uint3
 /* out[k * count + i] for rollout steps first_step + k (0-based), k < steps. */
 int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
                       int64_t first_step, int64_t steps, float* out);
+/* out[i] = log1pf(x[i]) of the host C library (f32::ln_1p of the reference). */
+void ora_ln_1p(const float* x, int64_t count, float* out);
+/* 0 (default): log1pf as the reference binds it; 1: f64 log1p rounded to f32,
+ * the device library's arithmetic (to compare the GPU bit for bit). */
+void ora_set_log1p_mode(int mode);
 /* Threads used by the OpenMP loops (0 = OpenMP default). */
 void ora_set_threads(int threads);
 int ora_get_threads(void);

@@ -108,3 +108,52 @@ def test_model_weight_validation():
 def test_valid_call_without_device_reports_no_device():
     with pytest.raises(C.NoDevice):
         K.build_hashgrid(np.zeros((2, 4)), 1, 2, HashGridConfig.growing_2d())
+
+
+def test_errors_carry_the_reference_payloads():
+    """KernelError's fields (config.rs:102-137) come across the C ABI through
+    npa_last_error_detail, so a binding can rebuild the exact variant."""
+    with pytest.raises(C.InvalidDim) as e:
+        K.build_hashgrid(np.zeros((1, 4)), 1, 1, HashGridConfig.growing_2d().with_(dim=4))
+    assert e.value.dim == 4
+    with pytest.raises(C.InvalidEps) as e:
+        K.build_hashgrid(np.zeros((1, 4)), 1, 1, HashGridConfig.growing_2d().with_(eps=-0.5))
+    assert e.value.eps == -0.5
+    with pytest.raises(C.ParticleModeRequiresPowerOfTwo) as e:
+        K.build_hashgrid(np.zeros((1, 4)), 1, 1, HashGridConfig.growing_2d().with_(grid_size=(64, 6, 1)))
+    assert (e.value.axis, e.value.value) == (1, 6)
+    cfg = HashGridConfig.growing_2d()
+    with pytest.raises(C.PositionShape) as e:
+        K.perceive(np.zeros((3, 4)), np.zeros(4), 1, 2, 2, cfg, True, True)
+    assert (e.value.positions, e.value.expected) == (3, 2)
+    with pytest.raises(C.StateShape) as e:
+        K.perceive(np.zeros((2, 4)), np.zeros(5), 1, 2, 2, cfg, True, True)
+    assert (e.value.states, e.value.expected) == (5, 4)
+    with pytest.raises(C.OutputShape) as e:
+        K.euler_step(np.zeros((2, 4)), np.zeros(4), np.zeros((1, 4)), np.zeros(4), 1, 2, 2, cfg,
+                     1.0)
+    assert (e.value.actual, e.value.expected) == (1, 2)
+
+
+def test_noalloc_hashgrid_validates_like_the_workspace_entry_point(npa_lib):
+    """Bad arguments get the same status from npa_dev_build_hashgrid_noalloc
+    as from npa_dev_build_hashgrid (checked before any CUDA call); only sizes
+    above the fixed array's limit add NPA_ERR_UNSUPPORTED."""
+    cases = [
+        (HashGridConfig.growing_2d().with_(dim=5), 1, 10),
+        (HashGridConfig.growing_2d().with_(eps=0.0), 1, 10),
+        (HashGridConfig.growing_2d().with_(grid_size=(6, 64, 1)), 1, 10),
+        (HashGridConfig.growing_2d(), -1, 10),
+        (HashGridConfig.growing_2d(), 2, -3),
+        (HashGridConfig.growing_2d().with_(grid_size=(1 << 15, 1 << 15, 1)), 8, 1),
+    ]
+    for cfg, batch, n in cases:
+        g = _lib.grid_c(cfg)
+        a = npa_lib.npa_dev_build_hashgrid(ctypes.byref(g), None, batch, n, None, None, None,
+                                           None, 0, None)
+        b = npa_lib.npa_dev_build_hashgrid_noalloc(ctypes.byref(g), None, batch, n, None, None,
+                                                   None, None)
+        assert a == b and a != 0, (cfg, batch, n, a, b)
+    g = _lib.grid_c(HashGridConfig.growing_2d())
+    assert npa_lib.npa_dev_build_hashgrid_noalloc(ctypes.byref(g), None, 3, 1 << 16, None, None,
+                                                  None, None) == 24

@@ -2,8 +2,9 @@
 
 The step itself is stood in for by the CPU oracle (tests only); what is
 checked is the product's multi-process logic: shard assignment, the
-max-over-ranks reduction, the gather of final-state checksums, and that a
-rank which dies is reported by the others instead of hanging them.
+max-over-ranks reduction, the gather of per-rollout digests and their check
+against a single-process run (as the benchmark does after timing), and that
+a rank which dies is reported by the others instead of hanging them.
 """
 
 import multiprocessing as mp
@@ -59,8 +60,10 @@ def _rank_main(rank, world, port, mode, out):
         elapsed = time.perf_counter() - t0
         multigpu.barrier_or_fail(timeout_s=5)
         mx = multigpu.max_over_ranks([elapsed, float(rank)])
-        sums = multigpu.gather_checksums(multigpu.shard_checksum(pos, st))
-        out.put((rank, "ok", mx, sums))
+        times = multigpu.gather_floats(float(rank) + 0.5)
+        digests = multigpu.gather_objects(multigpu.rollout_digests(w.batch, first, pos, st))
+        plans = multigpu.gather_objects((first, count))
+        out.put((rank, "ok", mx, (digests, plans, times)))
         multigpu.finish()
     except Exception as e:  # reported to the parent, never swallowed
         out.put((rank, "error", repr(e), None))
@@ -94,15 +97,20 @@ def test_two_gloo_ranks_match_a_single_process_run():
 
     res = _run(2, "ok")
     assert set(res) == {0, 1} and all(r[1] == "ok" for r in res.values()), res
-    sums = res[0][3]
-    assert sums == res[1][3]
+    digests, plans, times = res[0][3]
+    assert res[1][3] == (digests, plans, times)
+    assert plans == [(0, 2), (2, 2)] and times == [0.5, 1.5]
     assert res[0][2][1] == 1.0  # max over ranks of the rank id
-    for rank in range(2):
-        first, count = multigpu.shard(4, 2, rank, strong=True)
-        w = workloads.make("cfg0", batch=count, n=64, first=first)
-        pos, st, _ = oracle.rollout(w.model, w.weights, w.grid, w.positions, w.states, w.batch,
-                                    w.n, 2, w.dt)
-        assert sums[rank] == pytest.approx(multigpu.shard_checksum(pos, st), rel=0, abs=0)
+    # the single-process run of all four rollouts, as rank 0 of the benchmark reruns them
+    w = workloads.make("cfg0", batch=4, n=64)
+    pos, st, _ = oracle.rollout(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n,
+                                2, w.dt)
+    expected = multigpu.rollout_digests(w.batch, 0, pos, st)
+    assert multigpu.compare_digests(digests, expected) == (4, [])
+    # one changed bit in rollout 3 of the reference run is caught (planted on the CPU side)
+    st2 = st.copy()
+    st2[3 * 64 * 16 + 5] = np.nextafter(st2[3 * 64 * 16 + 5], np.float32(np.inf))
+    assert multigpu.compare_digests(digests, multigpu.rollout_digests(4, 0, pos, st2)) == (4, [3])
 
 
 def test_a_dead_rank_is_reported_not_waited_on():

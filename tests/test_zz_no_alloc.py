@@ -54,6 +54,8 @@ def run_both(torch, grid, positions, batch, n):
 
 
 def test_noalloc_hashgrid_matches_workspace_entry_point_twice():
+    """Batches of small rollouts: the per-rollout shared-memory sort, which
+    takes only the sorted-record slices of the fixed array."""
     torch = pytest.importorskip("torch")
     first = workloads.make("cfg2", batch=32, steps=1)          # 131,072 particles: the limit
     second = workloads.make("cfg0", n=3000, steps=1, seed=5)  # smaller, different grid use
@@ -62,6 +64,21 @@ def test_noalloc_hashgrid_matches_workspace_entry_point_twice():
         for x, y in zip(a, b):
             np.testing.assert_array_equal(x, y)
     assert first.batch * first.n == MAX_PARTICLES
+
+
+def test_noalloc_hashgrid_device_wide_sort_matches_twice():
+    """Shapes that take the device-wide radix sort, whose key / value
+    ping-pong buffers and tile histograms are carved from the fixed array:
+    one 16,384-particle 3D rollout, then 2 x 65,536 particles on cfg1's
+    262,144-cell grid (131,072 particles, the largest carve)."""
+    torch = pytest.importorskip("torch")
+    first = workloads.make("cfg3", steps=1)
+    second = workloads.make("cfg1", batch=2, n=1 << 16, steps=1, seed=7)
+    for w in (first, second):
+        a, b = run_both(torch, w.grid, w.positions, w.batch, w.n)
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(x, y)
+    assert second.batch * second.n == MAX_PARTICLES
 
 
 def test_noalloc_hashgrid_rejects_sizes_beyond_its_limit():
