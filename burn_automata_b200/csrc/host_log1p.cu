@@ -10,33 +10,34 @@
 // above the 64-step tolerance; to follow the reference's trajectory the device
 // must return the host's value itself.
 //
-// The device computes ln(1 + x) in f64 and rounds it once to f32 (c), then
-// corrects it with tables built here by CALLING the host's log1pf on every
-// float in [1e-6, inf) and comparing (no part of the C library's
-// implementation is restated; only its outputs are recorded):
-//   bits  one bit per float of the range, set where the host's result is not
-//         c.  Except for the inputs of the side list, the host's result is
-//         then c's neighbour on the side of the f64 value (the host is off by
-//         less than 1.5 ulp).  Norms of similar size share bitmap words, so the
-//         words a step reads stay resident in L2 / L1.
-//   side  the inputs whose exact host result is stored: the differing ones
-//         whose result is the neighbour on the far side (one on glibc 2.39),
-//         and every input whose f64 value lies within 1e-8 of a float gap
-//         from a rounding midpoint, where the device's and the host's f64
-//         log1p (each within an ulp or two of f64) may round to different
-//         floats; the device consults the list when the bit is set or its own
-//         value lies within 5e-9 of a gap from a midpoint.
+// What the host returns is recorded by CALLING the host's log1pf on every
+// float in [1e-6, inf) and comparing with the correctly rounded value c (ln(1 +
+// x) in f64, rounded once); no part of the C library's implementation is
+// restated, only its outputs:
+//   differ  the inputs where the host's result is not c.  Except for those of
+//           the side list, the host's result is then c's neighbour on the
+//           side of the f64 value (the host is off by less than 1.5 ulp);
+//   side    the inputs whose host result is stored outright: the differing
+//           ones whose result is the neighbour on the far side (one on glibc
+//           2.39), and every input whose f64 value lies within 1e-8 of a float
+//           gap from a rounding midpoint, where two f64 log1p implementations
+//           (each within an ulp or two of f64) may round to different floats.
+// On each device a setup kernel turns that into the table the kernels use:
+// for every input, the host's result relative to CUDA's f32 log1pf (f) as a
+// 2-bit code -- same, one ulp up, one ulp down, or stored in a sorted list --
+// so a kernel evaluates ln_1p with one f32 log1pf, one table word (norms of
+// similar size share words, which stay resident in L2 / L1) and an add.
 //
-// Inputs below 1e-6 are not tabulated (the device returns c there): the
+// Inputs below 1e-6 are not tabulated (the device returns CUDA's log1pf): the
 // reference's norm is max(sqrt(|v|^2 + 1e-12), 1e-6) >= 1e-6, so
 // log-normalisation never passes a smaller value.
 //
 // The scan (two libm calls per float, ~17 CPU-seconds) runs once per host
 // library: the list of differing inputs is cached next to this library
 // (libnpa_b200.so.log1pf) and re-validated against the running host's log1pf
-// when loaded; a cache that disagrees is rebuilt.  The device tables (the
-// bitmap, 128 MiB, and the side list) are uploaded on first use on a device and
-// kept until process exit.
+// when loaded; a cache that disagrees is rebuilt.  The device table (2 bits per
+// input, 256 MiB, plus the list of stored results) is built on first use on a
+// device and kept until process exit.
 #include <dlfcn.h>
 #include <unistd.h>
 #include <gnu/libc-version.h>
@@ -248,7 +249,7 @@ const HostTables& host_tables() {
 }
 
 struct DeviceTables {
-  uint32_t* bits = nullptr;
+  uint32_t* codes = nullptr;
   uint2* side = nullptr;
   uint32_t base = 0;
   uint32_t nbits = 0;
@@ -265,47 +266,134 @@ uint32_t range_base() {
   return u;
 }
 
+constexpr uint32_t kSideCapacity = 1u << 16;  // inputs whose code is 3 (stored outright)
+
+// One thread per 16 inputs (one word of 2-bit codes).  For each input x:
+// the host's log1pf g (the correctly rounded value c = f64 log1p rounded once,
+// moved to the neighbour on the f64 value's side where the host bitmap says
+// the host differs, or taken from the host's side list), CUDA's log1pf f, and
+// the code of g relative to f: 0 same, 1 one ulp up, 2 one ulp down, 3 stored
+// in the side list (appended, unordered; sorted on the host afterwards).
+__global__ void build_codes_kernel(const uint32_t* __restrict__ host_bits,
+                                   const uint2* __restrict__ host_side, int host_nside,
+                                   uint32_t base, uint32_t nbits, uint32_t* __restrict__ codes,
+                                   uint2* __restrict__ side_out, uint32_t* __restrict__ side_count) {
+  const uint32_t words = (nbits + 15u) / 16u;
+  for (uint32_t w = blockIdx.x * blockDim.x + threadIdx.x; w < words; w += gridDim.x * blockDim.x) {
+    uint32_t word = 0;
+    for (uint32_t j = 0; j < 16u; ++j) {
+      const uint32_t i = w * 16u + j;
+      if (i >= nbits) break;
+      const uint32_t u = base + i;
+      const float x = __uint_as_float(u);
+      const double v = log1p(static_cast<double>(x));
+      const float c = static_cast<float>(v);
+      const uint32_t cb = __float_as_uint(c);
+      const double cd = c;
+      const float o = __uint_as_float(cd < v ? cb + 1u : cb - 1u);  // c > 0 on the range
+      const double gap = fabs(static_cast<double>(o) - cd);
+      const bool near = fabs(v - 0.5 * (cd + static_cast<double>(o))) < 5e-9 * gap;
+      const bool differs = (__ldg(host_bits + (i >> 5)) >> (i & 31u)) & 1u;
+      float g = differs ? o : c;
+      if (differs || near)
+        for (int k = 0; k < host_nside; ++k) {
+          const uint2 e = __ldg(host_side + k);
+          if (e.x == u) g = __uint_as_float(e.y);
+        }
+      const float f = log1pf(x);
+      const int diff = static_cast<int>(__float_as_uint(g) - __float_as_uint(f));
+      const uint32_t code = diff == 0 ? 0u : diff == 1 ? 1u : diff == -1 ? 2u : 3u;
+      if (code == 3u) {
+        const uint32_t slot = atomicAdd(side_count, 1u);
+        if (slot < kSideCapacity) side_out[slot] = make_uint2(u, __float_as_uint(g));
+      }
+      word |= code << (2u * j);
+    }
+    codes[w] = word;
+  }
+}
+
 npa_status upload(const HostTables& h, DeviceTables* out) {
   if (h.side_keys.size() > size_t(kMaxSide))
     return fail(NPA_ERR_UNSUPPORTED, "log1pf side list larger than its capacity");
   const uint32_t base = range_base();
   const uint32_t nbits = 0x7f800000u - base;
-  const size_t words = (size_t(nbits) + 31) / 32;
-  std::vector<uint32_t> bits(words, 0u);
+  const size_t bit_words = (size_t(nbits) + 31) / 32;
+  const size_t code_words = (size_t(nbits) + 15) / 16;
+  std::vector<uint32_t> bits(bit_words, 0u);
   for (uint32_t u : h.differ) {
     const uint32_t i = u - base;
     bits[i >> 5] |= 1u << (i & 31);
   }
-  std::vector<uint2> side(std::max<size_t>(h.side_keys.size(), 1), make_uint2(0xffffffffu, 0));
-  for (size_t i = 0; i < h.side_keys.size(); ++i) side[i] = make_uint2(h.side_keys[i], h.side_vals[i]);
+  std::vector<uint2> hside(std::max<size_t>(h.side_keys.size(), 1), make_uint2(0xffffffffu, 0));
+  for (size_t i = 0; i < h.side_keys.size(); ++i)
+    hside[i] = make_uint2(h.side_keys[i], h.side_vals[i]);
+  // Temporaries (the host bitmap and side list, the unordered code-3 list and
+  // its count) live only while the codes are built.
+  uint32_t* d_bits = nullptr;
+  uint2* d_hside = nullptr;
+  uint2* d_out = nullptr;
+  uint32_t* d_count = nullptr;
   DeviceTables d;
-  NPA_CUDA(cudaMalloc(&d.bits, words * sizeof(uint32_t)), "cudaMalloc(log1pf bitmap)");
-  cudaError_t e = cudaMalloc(&d.side, side.size() * sizeof(uint2));
-  if (e != cudaSuccess) {
-    cudaFree(d.bits);
-    return cuda_fail(e, "cudaMalloc(log1pf side list)");
+  auto release = [&]() {
+    cudaFree(d_bits);
+    cudaFree(d_hside);
+    cudaFree(d_out);
+    cudaFree(d_count);
+  };
+  cudaError_t e = cudaMalloc(&d_bits, bit_words * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d_hside, hside.size() * sizeof(uint2));
+  if (e == cudaSuccess) e = cudaMalloc(&d_out, kSideCapacity * sizeof(uint2));
+  if (e == cudaSuccess) e = cudaMalloc(&d_count, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d.codes, code_words * 4);
+  // synchronous copies followed by a device synchronisation: a pageable-memory
+  // cudaMemcpy may return before its DMA ends
+  if (e == cudaSuccess) e = cudaMemcpy(d_bits, bits.data(), bit_words * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(d_hside, hside.data(), hside.size() * sizeof(uint2), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(d_count, 0, 4);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) {
+    build_codes_kernel<<<148 * 8, 256>>>(d_bits, d_hside, int(h.side_keys.size()), base, nbits,
+                                         d.codes, d_out, d_count);
+    e = cudaGetLastError();
   }
-  // synchronous copies that have completed on return (a pageable-memory
-  // cudaMemcpy may return before its DMA ends; the explicit synchronisation
-  // keeps kernels on other streams from reading a partial table)
-  e = cudaMemcpy(d.bits, bits.data(), words * sizeof(uint32_t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  uint32_t count = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&count, d_count, 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    release();
+    cudaFree(d.codes);
+    return cuda_fail(e, "building the log1pf code table");
+  }
+  if (count > kSideCapacity) {
+    release();
+    cudaFree(d.codes);
+    return fail(NPA_ERR_UNSUPPORTED, "log1pf: more stored results than the side list holds");
+  }
+  std::vector<uint2> side(std::max<uint32_t>(count, 1u), make_uint2(0xffffffffu, 0));
+  if (count) e = cudaMemcpy(side.data(), d_out, count * sizeof(uint2), cudaMemcpyDeviceToHost);
+  std::sort(side.begin(), side.begin() + count,
+            [](const uint2& a, const uint2& b) { return a.x < b.x; });
+  if (e == cudaSuccess) e = cudaMalloc(&d.side, side.size() * sizeof(uint2));
   if (e == cudaSuccess)
     e = cudaMemcpy(d.side, side.data(), side.size() * sizeof(uint2), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  release();
   if (e != cudaSuccess) {
-    cudaFree(d.bits);
+    cudaFree(d.codes);
     cudaFree(d.side);
-    return cuda_fail(e, "cudaMemcpy(log1pf tables)");
+    return cuda_fail(e, "uploading the log1pf side list");
   }
   d.base = base;
   d.nbits = nbits;
-  d.nside = int(h.side_keys.size());
+  d.nside = int(count);
   *out = d;
   return NPA_OK;
 }
 
 Log1pTable as_table(const DeviceTables& d) {
-  return Log1pTable{d.bits, d.side, d.base, d.nbits, d.nside, table_min()};
+  return Log1pTable{d.codes, d.side, d.base, d.nbits, d.nside, table_min()};
 }
 
 }  // namespace
@@ -320,7 +408,7 @@ npa_status device_log1p_table(Log1pTable* out, cudaStream_t stream) {
   NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    if (dev < int(g_dev.size()) && g_dev[dev].bits) {
+    if (dev < int(g_dev.size()) && g_dev[dev].codes) {
       *out = as_table(g_dev[dev]);
       return NPA_OK;
     }
@@ -328,7 +416,7 @@ npa_status device_log1p_table(Log1pTable* out, cudaStream_t stream) {
   const HostTables& h = host_tables();
   std::lock_guard<std::mutex> lock(g_dev_mu);
   if (dev >= int(g_dev.size())) g_dev.resize(dev + 1);
-  if (!g_dev[dev].bits) {
+  if (!g_dev[dev].codes) {
     if (stream) {
       cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
       NPA_CUDA(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");

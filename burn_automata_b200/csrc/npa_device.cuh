@@ -238,48 +238,48 @@ __device__ __forceinline__ void safe_inverse_symmetric(const float* m, int dim, 
 }
 
 // The host C library's log1pf, bit for bit (f32::ln_1p of the reference; the
-// tables and how they are built: host_log1p.cu).  ln(1 + x) is evaluated in
-// f64 and rounded once to f32 (c); one bit per float says where the host
-// returns another value (then the neighbour of c on the side of the f64 value),
-// and a short list holds the inputs whose result is stored outright.
+// table and how it is built: host_log1p.cu): CUDA's f32 log1pf corrected by a
+// 2-bit code per input (0 same, 1 one ulp up, 2 one ulp down, 3 the result is
+// stored in a sorted list).
 struct Log1pTable {
-  const uint32_t* bits;  // bit (u - base) set where the host result is not c
-  const uint2* side;     // {input bits, host result bits}, nside entries
-  uint32_t base;         // bits of the smallest tabulated input
-  uint32_t nbits;        // tabulated inputs: [base, base + nbits)
+  const uint32_t* codes;  // 16 codes per word, input (u - base) at bits 2 (i % 16)
+  const uint2* side;      // {input bits, host result bits}, ascending inputs
+  uint32_t base;          // bits of the smallest tabulated input
+  uint32_t nbits;         // tabulated inputs: [base, base + nbits)
   int nside;
-  float min_input;       // inputs below are not tabulated (c is returned)
+  float min_input;        // inputs below are not tabulated (CUDA's log1pf is returned)
 };
 
-// The bitmap word holding input x's bit (0 when x is not tabulated); loaded
+// The code word holding input x's code (0 when x is not tabulated); loaded
 // apart from log1p_host_word so that callers can issue several loads at once.
 __device__ __forceinline__ uint32_t log1p_word(float x, const Log1pTable& t) {
   const uint32_t i = __float_as_uint(x) - t.base;
-  if (!t.bits || !(x >= t.min_input) || !(i < t.nbits)) return 0u;
-  return __ldg(t.bits + (i >> 5));
+  if (!t.codes || !(x >= t.min_input) || !(i < t.nbits)) return 0u;
+  return __ldg(t.codes + (i >> 4));
 }
 
-// log1pf(x) of the host given x's bitmap word (from log1p_word).
+// log1pf(x) of the host given x's code word (from log1p_word).
 __device__ __forceinline__ float log1p_host_word(float x, uint32_t word, const Log1pTable& t) {
-  const double v = log1p(static_cast<double>(x));
-  const float c = static_cast<float>(v);
+  const float f = log1pf(x);
   const uint32_t u = __float_as_uint(x);
   const uint32_t i = u - t.base;
-  if (!t.bits || !(x >= t.min_input) || !(i < t.nbits)) return c;
-  const bool differs = (word >> (i & 31u)) & 1u;
-  const uint32_t cb = __float_as_uint(c);
-  const double cd = c;
-  const float o = __uint_as_float(cd < v ? cb + 1u : cb - 1u);  // c > 0 here
-  const double gap = fabs(static_cast<double>(o) - cd);
-  const bool near = fabs(v - 0.5 * (cd + static_cast<double>(o))) < 5e-9 * gap;
-  float r = differs ? o : c;
-  if (differs || near) {
-    for (int k = 0; k < t.nside; ++k) {
-      const uint2 e = __ldg(t.side + k);
-      if (e.x == u) r = __uint_as_float(e.y);
+  if (!t.codes || !(x >= t.min_input) || !(i < t.nbits)) return f;
+  const uint32_t code = (word >> (2u * (i & 15u))) & 3u;
+  if (code != 3u)
+    return __uint_as_float(__float_as_uint(f) + (code == 1u ? 1u : code == 2u ? ~0u : 0u));
+  // lower bound of u among the stored results (every code-3 input is there)
+  int lo = 0, n = t.nside;
+  while (n > 0) {
+    const int half = n >> 1;
+    if (__ldg(t.side + lo + half).x < u) {
+      lo += half + 1;
+      n -= half + 1;
+    } else {
+      n = half;
     }
   }
-  return r;
+  const uint2 e = lo < t.nside ? __ldg(t.side + lo) : make_uint2(0u, 0u);
+  return e.x == u ? __uint_as_float(e.y) : f;
 }
 
 __device__ __forceinline__ float log1p_host(float x, const Log1pTable& t) {

@@ -187,7 +187,8 @@ npa_status npa_last_error_detail(npa_error_detail* out);
  * neighbouring float.  Those inputs are found by calling the host's log1pf on
  * every float in [1e-6, inf); the list is cached next to the library file
  * (libnpa_b200.so.log1pf, checked against the running host when read) and
- * uploaded to each device on first use (64 MiB + 32 KiB, held until exit).
+ * turned on each device, on first use, into a 2-bit correction code per input
+ * relative to CUDA's log1pf (256 MiB, held until exit).
  *
  * npa_prepare_host_tables builds or loads that list (about 17 CPU-seconds
  * when no valid cache exists) and reports its length.  npa_prepare_device
@@ -198,7 +199,7 @@ npa_status npa_last_error_detail(npa_error_detail* out);
 npa_status npa_prepare_host_tables(int64_t* ln_1p_exceptions);
 npa_status npa_prepare_device(int32_t device);
 /* f32::ln_1p as above on device buffers: d_out[i] = log1pf(d_x[i]) of the host
- * C library, bit for bit for x >= 1e-6 (below, the correctly rounded value). */
+ * C library, bit for bit for x >= 1e-6 (below, CUDA's log1pf). */
 npa_status npa_dev_ln_1p(const float* d_x, int64_t count, float* d_out, void* stream);
 
 /* HashGridConfig::validate (config.rs:65-84). */
