@@ -72,8 +72,16 @@ WORKLOADS = {
 
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu captures, per particle of that launch:
-#   profiles/mlp_step_kernel_cfg2.txt: 356.7 MB + 67.7 MB for 1,048,576 rows.
-NCU_TRAFFIC_PER_PARTICLE = {("cfg2", "mlp_step_kernel"): (356.673280e6 + 68.960000e6) / 1048576}
+#   profiles/mlp_step_kernel_cfg2.txt: 356.9 MB + 68.6 MB for 1,048,576 rows;
+#   profiles/perception_kernel_cfg1.txt: 1306.5 MB + 620.9 MB for 1,048,576 particles.
+NCU_TRAFFIC_PER_PARTICLE = {
+    ("cfg2", "mlp_step_kernel"): (356.874496e6 + 68.579840e6) / 1048576,
+    ("cfg1", "perception_kernel"): (1306.484736e6 + 620.867840e6) / 1048576,
+}
+NCU_TRAFFIC_SOURCE = {
+    ("cfg2", "mlp_step_kernel"): "profiles/mlp_step_kernel_cfg2.txt",
+    ("cfg1", "perception_kernel"): "profiles/perception_kernel_cfg1.txt",
+}
 
 
 def env_int(name, default):
@@ -115,6 +123,35 @@ def perception_kernel_bytes(w, features) -> int:
     """cfg1 perception kernel per particle: own position (16) and state (4C)
     read, volume read (4), feature row write (4F)."""
     return 16 + 4 * w.state_dims + 4 + 4 * features
+
+
+def mean_neighbours(w) -> float:
+    """Mean in-radius neighbours per particle (self included) of a workload's
+    positions: r < eps, within each rollout (2D / 3D Euclidean; Grid-mode
+    periodic wrap is not modelled -- cfg1 is Particle mode)."""
+    from scipy.spatial import cKDTree
+
+    d = w.grid.dim
+    counts = []
+    for b in range(w.batch):
+        p = w.positions[b * w.n:(b + 1) * w.n, :d].astype(np.float64)
+        counts.append(cKDTree(p).query_ball_point(p, w.grid.eps, return_length=True))
+    return float(np.mean(np.concatenate(counts)))
+
+
+def perception_flops(w, neighbours) -> float:
+    """Algorithmic FP32 operations of one particle's perception with the full
+    option set (state and density gradients, hybrid moment, log-normalised;
+    forward.rs:249-295, normalize.rs), each multiply, add, square root,
+    division and ln_1p counted as one:
+      per in-radius neighbour other than itself: 8 per channel (blur 3, state
+        gradient 5) + 37 (delta 2, r^2 3, poly6 4, two spiky magnitudes 14,
+        gradient vector 2, density gradient 4, moment 8);
+      its own pair: 9 + 3 per channel;
+      per particle: moment inverse 8 + 19 per channel (correction 8, scale 2,
+        log-normalisation 9) + density gradient 11."""
+    c = w.state_dims
+    return (neighbours - 1.0) * (8 * c + 37) + (9 + 3 * c) + 8 + 19 * c + 11
 
 
 def perception_step_bytes(w, features) -> float:
@@ -606,7 +643,7 @@ def run_ours(args, rank, world, local_rank):
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": tr * particles_rank if tr else None,
                          "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                            "profiles/mlp_step_kernel_cfg2.txt") if tr else None,
+                                            + NCU_TRAFFIC_SOURCE[(args.workload, kernel)]) if tr else None,
                          "bytes_per_particle": kbytes, "avg_launch_ms": dom_ms},
             "step_roofline": {"bound": "hbm", "achieved": sbytes * value / world / 1e9,
                               "peak": peak, "unit": "GB/s",
@@ -618,8 +655,20 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks,
             "validation": validation,
         }
+        sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+        fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12
+        if perception_only:
+            nbr = mean_neighbours(w)
+            flops = perception_flops(w, nbr)
+            fp32_achieved = flops * particles_rank / (dom_ms / 1000.0) / 1e12
+            line["compute_roof"] = {
+                "bound": "fp32", "kernel": kernel, "achieved": fp32_achieved, "peak": fp32_peak,
+                "frac": fp32_achieved / fp32_peak, "flops_per_particle": flops,
+                "mean_neighbours": nbr,
+                "unit": "TFLOP/s (algorithmic FP32 operations of the pair sums and the "
+                        "per-particle finish, sqrt / division / ln_1p counted as one; peak = 148 SM "
+                        "x 128 lanes x median SM clock)"}
         if not perception_only:
-            sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
             mlp_ops = 2 * (features * w.model.hidden_dims
                            + w.model.hidden_dims * w.model.update_dims())
             fp32_peak = 148 * 128 * sm_mhz * 1e6 / 1e12
