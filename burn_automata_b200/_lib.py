@@ -106,6 +106,14 @@ SIGNATURES = [
      [vp, P(GridConfigC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, c_f32, c_f32,
       ctypes.c_uint64, f32p]),
     ("npa_rollout_update_masks", c_i32, [ctypes.c_uint64, c_f32, c_i64, c_i64, c_i64, f32p]),
+    ("npa_model_mlp_backward", c_i32,
+     [vp, f32p, c_i64, f32p, c_i64, f32p, f32p, f32p, f32p, f32p]),
+    ("npa_model_rollout_for_training", c_i32,
+     [vp, P(GridConfigC), f32p, c_i64, f32p, c_i64, c_i64, c_i64, c_i64, c_f32, ctypes.c_uint64,
+      f32p, f32p, f32p, f32p, f32p, f32p]),
+    ("npa_model_bptt_gradients", c_i32,
+     [vp, P(GridConfigC), f32p, f32p, f32p, c_i64, c_i64, c_i64, f32p, f32p, c_f32, c_i32, c_i32,
+      f32p, f32p, f32p, f32p, f32p, f32p]),
     ("npa_dev_hashgrid_workspace_size", c_i32, [P(GridConfigC), c_i64, c_i64, P(ctypes.c_size_t)]),
     ("npa_dev_build_hashgrid", c_i32,
      [P(GridConfigC), vp, c_i64, c_i64, vp, vp, vp, vp, ctypes.c_size_t, vp]),

@@ -1901,3 +1901,298 @@ npa_status npa_rollout_update_masks(uint64_t seed, float update_prob, int64_t co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Training rollout (crates/burn_automata/src/target2d.rs:3414-3722,
+// crates/burn_automata/src/training.rs:558-640)
+// ---------------------------------------------------------------------------
+namespace {
+
+// ensure_finite (training.rs:1053-1060).
+npa_status ensure_finite_host(const char* name, const float* v, size_t count) {
+  for (size_t i = 0; i < count; ++i)
+    if (!std::isfinite(v[i])) return fail(NPA_ERR_INVALID_ARGUMENT, std::string(name) + " contain non-finite values");
+  return NPA_OK;
+}
+
+// The training rollout's forward step is step_cpu's without the 3D position
+// gates (rollout_for_training uses update_to_dx_ds + euler_step,
+// target2d.rs:3430-3452); the step kernel would apply them.
+npa_status check_training_model(const npa_model* m, const npa_grid_config* grid) {
+  NPA_TRY(check_step(m, grid));
+  if (grid->dim == 3 && m->cfg.position_features && m->dm.state_dims > 3)
+    return fail(NPA_ERR_UNSUPPORTED,
+                "the training rollout has no 3D position gates; models with 3D position "
+                "features are not supported by it");
+  return NPA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+npa_status npa_model_mlp_backward(npa_model* m, const float* features, int64_t features_len,
+                                  const float* output_gradients, int64_t output_gradients_len,
+                                  float* gw1, float* gb1, float* gw2, float* gb2,
+                                  float* gfeatures) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  const int64_t F = m->dm.feature_dims, H = m->dm.hidden_dims, O = m->dm.update_dims;
+  const int64_t rows = F > 0 ? features_len / F : 0;
+  if (rows == 0 || features_len != rows * F)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "features do not form whole perception rows");
+  if (output_gradients_len != rows * O)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "output_gradients len " + std::to_string(output_gradients_len) +
+                                              " != " + std::to_string(rows * O));
+  if (rows > int64_t(kMaxParticles)) return fail(NPA_ERR_UNSUPPORTED, "too many rows");
+  if (!features || !output_gradients || !gw1 || !gb1 || !gw2 || !gb2 || !gfeatures)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_finite_host("features", features, size_t(features_len)));
+  NPA_TRY(ensure_finite_host("output_gradients", output_gradients, size_t(output_gradients_len)));
+  NPA_TRY(ensure_device(m->dm.device));
+  const uint32_t R = uint32_t(rows);
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float *df, *dg, *dhid, *dpre, *dgf, *dw;
+  NPA_TRY(sc.upload(&df, features, size_t(features_len)));
+  NPA_TRY(sc.upload(&dg, output_gradients, size_t(output_gradients_len)));
+  NPA_TRY(sc.alloc(&dhid, size_t(R) * H));
+  NPA_TRY(sc.alloc(&dpre, size_t(R) * H));
+  NPA_TRY(sc.alloc(&dgf, size_t(R) * F));
+  const size_t nw = size_t(H * F + H + O * H + O);
+  NPA_TRY(sc.alloc(&dw, nw));
+  NPA_CUDA(cudaMemsetAsync(dw, 0, nw * 4, sc.stream), "cudaMemsetAsync");
+  float* dgw1 = dw;
+  float* dgb1 = dgw1 + H * F;
+  float* dgw2 = dgb1 + H;
+  float* dgb2 = dgw2 + O * H;
+  NPA_TRY(launch_mlp_backward(m->dm, df, dg, R, dhid, dpre, dgf, dgw1, dgb1, dgw2, dgb2, sc.stream));
+  NPA_TRY(sc.download(gw1, dgw1, size_t(H * F) * 4));
+  NPA_TRY(sc.download(gb1, dgb1, size_t(H) * 4));
+  NPA_TRY(sc.download(gw2, dgw2, size_t(O * H) * 4));
+  NPA_TRY(sc.download(gb2, dgb2, size_t(O) * 4));
+  NPA_TRY(sc.download(gfeatures, dgf, size_t(R) * F * 4));
+  NPA_TRY(sc.finish());
+  // validate_gradients (training.rs:1017-1023)
+  NPA_TRY(ensure_finite_host("w1 gradients", gw1, size_t(H * F)));
+  NPA_TRY(ensure_finite_host("b1 gradients", gb1, size_t(H)));
+  NPA_TRY(ensure_finite_host("w2 gradients", gw2, size_t(O * H)));
+  NPA_TRY(ensure_finite_host("b2 gradients", gb2, size_t(O)));
+  return ensure_finite_host("feature gradients", gfeatures, size_t(R) * F);
+}
+
+npa_status npa_model_rollout_for_training(npa_model* m, const npa_grid_config* grid,
+                                          const float* positions, int64_t positions_len,
+                                          const float* states, int64_t states_len, int64_t batch,
+                                          int64_t n, int64_t steps, float update_prob,
+                                          uint64_t seed, float* snapshot_positions,
+                                          float* snapshot_states, float* snapshot_masks,
+                                          float* final_positions, float* final_states,
+                                          float* mean_dx_norm_sum) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_training_model(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_shapes(positions_len, states_len, batch, n, m->dm.state_dims));
+  NPA_TRY(check_bins(grid, batch));
+  if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
+  const uint32_t total = uint32_t(batch * n);
+  const int C = m->dm.state_dims;
+  if (!mean_dx_norm_sum || (total > 0 && (!positions || !final_positions ||
+                                          (C > 0 && (!states || !final_states)) ||
+                                          (steps > 0 && (!snapshot_positions || !snapshot_masks ||
+                                                         (C > 0 && !snapshot_states))))))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_device(m->dm.device));
+  *mean_dx_norm_sum = 0.0f;
+  if (total == 0) return NPA_OK;
+  // stochastic_mask draws of StdRng::seed_from_u64(seed ^ 0x5eed2d), one
+  // stream for the whole rollout (target2d.rs:3425-3429); ones without
+  // drawing when update_prob >= 1 (rollout/mod.rs:644-651).
+  const bool stochastic = !(update_prob >= 1.0f);
+  const ChachaKey key = stdrng_key(seed ^ 0x5eed2dull);
+  size_t wsb = 0;
+  NPA_TRY(npa_dev_step_workspace_size(m, grid, batch, n, &wsb));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  float4 *pos[2], *ddx, *snap_p;
+  float *st[2], *dmean, *mask, *snap_s = nullptr, *snap_m;
+  double* partials;
+  char* ws;
+  const int64_t S = std::max<int64_t>(steps, 1);
+  NPA_TRY(sc.upload(&pos[0], positions, total));
+  NPA_TRY(sc.upload(&st[0], states, size_t(total) * C));
+  NPA_TRY(sc.alloc(&pos[1], total));
+  NPA_TRY(sc.alloc(&st[1], size_t(total) * C));
+  NPA_TRY(sc.alloc(&ddx, total));
+  NPA_TRY(sc.alloc(&dmean, size_t(S)));
+  NPA_TRY(sc.alloc(&partials, mean_norm_scratch_bytes() / sizeof(double)));
+  NPA_TRY(sc.alloc(&mask, total));
+  NPA_TRY(sc.alloc(&snap_p, size_t(S) * total));
+  if (C > 0) NPA_TRY(sc.alloc(&snap_s, size_t(S) * total * C));
+  NPA_TRY(sc.alloc(&snap_m, size_t(S) * total));
+  NPA_TRY(sc.alloc(&ws, wsb));
+  if (!stochastic) {
+    std::vector<float> ones(total, 1.0f);
+    NPA_CUDA(cudaMemcpyAsync(mask, ones.data(), size_t(total) * 4, cudaMemcpyHostToDevice, sc.stream),
+             "cudaMemcpyAsync");
+    NPA_CUDA(cudaStreamSynchronize(sc.stream), "cudaStreamSynchronize");
+  }
+  int cur = 0;
+  for (int64_t k = 0; k < steps; ++k) {
+    if (stochastic)
+      NPA_TRY(launch_stdrng_mask(key, uint64_t(k) * total, total, update_prob, mask, sc.stream));
+    NPA_CUDA(cudaMemcpyAsync(snap_p + size_t(k) * total, pos[cur], size_t(total) * 16,
+                             cudaMemcpyDeviceToDevice, sc.stream), "cudaMemcpyAsync");
+    if (C > 0)
+      NPA_CUDA(cudaMemcpyAsync(snap_s + size_t(k) * total * C, st[cur], size_t(total) * C * 4,
+                               cudaMemcpyDeviceToDevice, sc.stream), "cudaMemcpyAsync");
+    NPA_CUDA(cudaMemcpyAsync(snap_m + size_t(k) * total, mask, size_t(total) * 4,
+                             cudaMemcpyDeviceToDevice, sc.stream), "cudaMemcpyAsync");
+    NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(pos[cur]), st[cur], batch, n, 1.0f,
+                               mask, reinterpret_cast<float*>(pos[1 - cur]), st[1 - cur],
+                               reinterpret_cast<float*>(ddx), nullptr, nullptr, nullptr, ws, wsb,
+                               sc.stream));
+    NPA_TRY(launch_mean_norm(ddx, total, partials, dmean + k, sc.stream));
+    cur = 1 - cur;
+  }
+  std::vector<float> means(size_t(S), 0.0f);
+  NPA_TRY(sc.download(final_positions, pos[cur], size_t(total) * 16));
+  if (C > 0) NPA_TRY(sc.download(final_states, st[cur], size_t(total) * C * 4));
+  if (steps > 0) {
+    NPA_TRY(sc.download(snapshot_positions, snap_p, size_t(steps) * total * 16));
+    if (C > 0) NPA_TRY(sc.download(snapshot_states, snap_s, size_t(steps) * total * C * 4));
+    NPA_TRY(sc.download(snapshot_masks, snap_m, size_t(steps) * total * 4));
+    NPA_TRY(sc.download(means.data(), dmean, size_t(steps) * 4));
+  }
+  NPA_TRY(sc.finish());
+  NPA_TRY(check_bulk_copies());
+  // mean_dx_norm_sum += mean_dx_norm(dx) per step, in f32 (target2d.rs:3434)
+  float sum = 0.0f;
+  for (int64_t k = 0; k < steps; ++k) sum = sum + means[size_t(k)];
+  *mean_dx_norm_sum = sum;
+  return NPA_OK;
+}
+
+npa_status npa_model_bptt_gradients(npa_model* m, const npa_grid_config* grid,
+                                    const float* snapshot_positions, const float* snapshot_states,
+                                    const float* snapshot_masks, int64_t batch, int64_t n,
+                                    int64_t steps, const float* position_gradients,
+                                    const float* state_gradients,
+                                    float displacement_regularizer_weight, int32_t stopgrad_pos,
+                                    int32_t stopgrad_state, float* gw1, float* gb1, float* gw2,
+                                    float* gb2, float* initial_position_adjoint,
+                                    float* initial_state_adjoint) {
+  if (!m) return fail(NPA_ERR_INVALID_ARGUMENT, "null model");
+  NPA_TRY(check_training_model(m, grid));
+  NPA_TRY(check_counts(batch, n));
+  NPA_TRY(check_bins(grid, batch));
+  if (steps < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "steps must be >= 0");
+  const uint32_t total = uint32_t(batch * n);
+  // mlp_backward_from_output_gradients rejects a step with no rows
+  if (total == 0 && steps > 0)
+    return fail(NPA_ERR_INVALID_ARGUMENT, "features do not form whole perception rows");
+  const int C = m->dm.state_dims, D = m->dm.spatial_dims, H = m->dm.hidden_dims;
+  const int F = m->dm.feature_dims, O = m->dm.update_dims;
+  if (!gw1 || !gb1 || !gw2 || !gb2 ||
+      (total > 0 && (!position_gradients || (C > 0 && !state_gradients) ||
+                     (steps > 0 && (!snapshot_positions || !snapshot_masks ||
+                                    (C > 0 && !snapshot_states))))))
+    return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
+  NPA_TRY(ensure_device(m->dm.device));
+  const npa_perception_options opt = model_options(m->cfg);
+  const float motion_eps =
+      m->dm.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? grid->eps : m->dm.eps0;
+  const float scale = m->dm.alpha * motion_eps;
+  // displacement_scale (target2d.rs:3568-3572)
+  const float reg = displacement_regularizer_weight == 0.0f
+                        ? 0.0f
+                        : displacement_regularizer_weight / float(std::max<uint32_t>(total, 1u));
+  size_t pws = 0, aws = 0;
+  NPA_TRY(npa_dev_perceive_workspace_size(grid, batch, n, C, &pws));
+  NPA_TRY(npa_dev_perceive_adjoint_workspace_size(grid, batch, n, C, &aws));
+  Scratch sc;
+  NPA_TRY(sc.init());
+  const size_t T = std::max<uint32_t>(total, 1u);
+  float4 *pos, *padj, *ppos;
+  float *stt = nullptr, *sadj = nullptr, *pst = nullptr, *mask, *feat, *upd, *oadj, *hid, *dpre,
+        *gfeat, *dw;
+  int* flag;
+  char *pw, *aw;
+  NPA_TRY(sc.alloc(&pos, T));
+  NPA_TRY(sc.alloc(&stt, T * std::max(C, 1)));
+  NPA_TRY(sc.alloc(&mask, T));
+  NPA_TRY(sc.alloc(&padj, T));
+  NPA_TRY(sc.alloc(&sadj, T * std::max(C, 1)));
+  NPA_TRY(sc.alloc(&ppos, T));
+  NPA_TRY(sc.alloc(&pst, T * std::max(C, 1)));
+  NPA_TRY(sc.alloc(&feat, T * F));
+  NPA_TRY(sc.alloc(&upd, T * O));
+  NPA_TRY(sc.alloc(&oadj, T * O));
+  NPA_TRY(sc.alloc(&hid, T * H));
+  NPA_TRY(sc.alloc(&dpre, T * H));
+  NPA_TRY(sc.alloc(&gfeat, T * F));
+  const size_t nw = size_t(H) * F + H + size_t(O) * H + O;
+  NPA_TRY(sc.alloc(&dw, nw));
+  NPA_TRY(sc.alloc(&flag, 1));
+  NPA_TRY(sc.alloc(&pw, pws));
+  NPA_TRY(sc.alloc(&aw, aws));
+  float* dgw1 = dw;
+  float* dgb1 = dgw1 + size_t(H) * F;
+  float* dgw2 = dgb1 + H;
+  float* dgb2 = dgw2 + size_t(O) * H;
+  cudaStream_t s = sc.stream;
+  NPA_CUDA(cudaMemsetAsync(dw, 0, nw * 4, s), "cudaMemsetAsync");
+  NPA_CUDA(cudaMemsetAsync(flag, 0, 4, s), "cudaMemsetAsync");
+  if (total > 0) {
+    NPA_CUDA(cudaMemcpyAsync(padj, position_gradients, size_t(total) * 16, cudaMemcpyHostToDevice, s),
+             "cudaMemcpyAsync");
+    if (C > 0)
+      NPA_CUDA(cudaMemcpyAsync(sadj, state_gradients, size_t(total) * C * 4, cudaMemcpyHostToDevice, s),
+               "cudaMemcpyAsync");
+  }
+  for (int64_t k = steps - 1; k >= 0 && total > 0; --k) {
+    NPA_CUDA(cudaMemcpyAsync(pos, snapshot_positions + size_t(k) * total * 4, size_t(total) * 16,
+                             cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    if (C > 0)
+      NPA_CUDA(cudaMemcpyAsync(stt, snapshot_states + size_t(k) * total * C, size_t(total) * C * 4,
+                               cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    NPA_CUDA(cudaMemcpyAsync(mask, snapshot_masks + size_t(k) * total, size_t(total) * 4,
+                             cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    // features and raw update of the recorded step (target2d.rs:3570-3579)
+    NPA_TRY(npa_dev_perceive_with_options(grid, &opt, reinterpret_cast<float*>(pos), stt, batch, n,
+                                          C, feat, nullptr, nullptr, nullptr, nullptr, pw, pws, s));
+    NPA_TRY(launch_forward_update(m->dm, feat, total, upd, s));
+    NPA_TRY(launch_output_adjoint(upd, padj, sadj, mask, total, D, C, scale, reg, oadj, s));
+    // ensure_finite of mlp_backward_from_output_gradients' inputs (training.rs:577-578)
+    NPA_TRY(launch_finite_check(feat, uint64_t(total) * F, flag, 1, s));
+    NPA_TRY(launch_finite_check(oadj, uint64_t(total) * O, flag, 2, s));
+    NPA_TRY(launch_mlp_backward(m->dm, feat, oadj, total, hid, dpre, gfeat, dgw1, dgb1, dgw2, dgb2, s));
+    NPA_TRY(launch_finite_check(gfeat, uint64_t(total) * F, flag, 4, s));
+    // perception adjoint of the step, added to the running adjoints
+    NPA_TRY(npa_dev_perceive_adjoint_with_options(grid, &opt, reinterpret_cast<float*>(pos), stt,
+                                                  batch, n, C, gfeat, pst,
+                                                  reinterpret_cast<float*>(ppos), aw, aws, s));
+    NPA_TRY(launch_add_adjoint(padj, sadj, ppos, pst, total, D, C, !stopgrad_pos, !stopgrad_state, s));
+    // the snapshot buffers are refilled next step: finish this one first
+    NPA_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  }
+  int fl = 0;
+  NPA_TRY(sc.download(&fl, flag, 4));
+  NPA_TRY(sc.download(gw1, dgw1, size_t(H) * F * 4));
+  NPA_TRY(sc.download(gb1, dgb1, size_t(H) * 4));
+  NPA_TRY(sc.download(gw2, dgw2, size_t(O) * H * 4));
+  NPA_TRY(sc.download(gb2, dgb2, size_t(O) * 4));
+  if (initial_position_adjoint && total > 0)
+    NPA_TRY(sc.download(initial_position_adjoint, padj, size_t(total) * 16));
+  if (initial_state_adjoint && total > 0 && C > 0)
+    NPA_TRY(sc.download(initial_state_adjoint, sadj, size_t(total) * C * 4));
+  NPA_TRY(sc.finish());
+  if (fl & 1) return fail(NPA_ERR_INVALID_ARGUMENT, "features contain non-finite values");
+  if (fl & 2) return fail(NPA_ERR_INVALID_ARGUMENT, "output_gradients contain non-finite values");
+  if (fl & 4) return fail(NPA_ERR_INVALID_ARGUMENT, "feature gradients contain non-finite values");
+  NPA_TRY(ensure_finite_host("w1 gradients", gw1, size_t(H) * F));
+  NPA_TRY(ensure_finite_host("b1 gradients", gb1, size_t(H)));
+  NPA_TRY(ensure_finite_host("w2 gradients", gw2, size_t(O) * H));
+  return ensure_finite_host("b2 gradients", gb2, size_t(O));
+}
+
+}  // extern "C"

@@ -166,6 +166,27 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 
+// ---- training rollout backward (train.cu) ----
+// out[r][O] = adjoint of row r's raw update (target2d.rs:3566-3604): the masked
+// position adjoint through raw_motion_adjoint, the displacement regularizer
+// (reg = weight / rows; 0 = off) and the masked state adjoint.
+npa_status launch_output_adjoint(const float* update, const float4* pos_adj, const float* state_adj,
+                                 const float* mask, uint32_t rows, int dims, int C, float scale,
+                                 float reg, float* out, cudaStream_t stream);
+// mlp_backward_from_output_gradients (training.rs:558-640) over `rows` rows:
+// the input adjoint into gfeat and the weight / bias gradients ADDED to
+// gw1 [H][F], gb1, gw2 [O][H], gb2; hidden / dpre are [rows][H] scratch.
+npa_status launch_mlp_backward(const DeviceModel& m, const float* features, const float* out_adj,
+                               uint32_t rows, float* hidden, float* dpre, float* gfeat,
+                               float* gw1, float* gb1, float* gw2, float* gb2,
+                               cudaStream_t stream);
+npa_status launch_add_adjoint(float4* pos_adj, float* state_adj, const float4* dpos,
+                              const float* dstate, uint32_t rows, int dims, int C, bool add_pos,
+                              bool add_state, cudaStream_t stream);
+// *flag |= code when any of the count values is not finite.
+npa_status launch_finite_check(const float* v, uint64_t count, int* flag, int code,
+                               cudaStream_t stream);
+
 // ---- perception adjoint (adjoint.cu) ----
 // Scratch floats launch_perception_adjoint needs beyond its outputs.
 size_t adjoint_scratch_floats(uint32_t total, int state_dims, int dim);

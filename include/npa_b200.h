@@ -321,6 +321,63 @@ npa_status npa_model_run_rollout_seeded(npa_model* model, const npa_grid_config*
 npa_status npa_rollout_update_masks(uint64_t seed, float update_prob, int64_t count,
                                     int64_t first_step, int64_t steps, float* masks);
 
+/* ---- training rollout (f32 backprop through time) ---- */
+
+/* mlp_backward_from_output_gradients (crates/burn_automata/src/training.rs:558-640):
+ * rows = features_len / perception_dims; output_gradients [rows][update_dims].
+ * Writes the weight gradients gw1 [hidden][perception_dims], gb1 [hidden],
+ * gw2 [update_dims][hidden], gb2 [update_dims] and the feature gradients
+ * gfeatures [rows][perception_dims].  Every sum is taken in the reference's
+ * order (weight gradients over rows in row order), so the results are its
+ * own bit for bit.  Non-finite inputs or results return
+ * NPA_ERR_INVALID_ARGUMENT naming the buffer (ensure_finite, :1053-1060). */
+npa_status npa_model_mlp_backward(npa_model* model, const float* features, int64_t features_len,
+                                  const float* output_gradients, int64_t output_gradients_len,
+                                  float* gw1, float* gb1, float* gw2, float* gb2,
+                                  float* gfeatures);
+
+/* rollout_for_training (crates/burn_automata/src/target2d.rs:3414-3466):
+ * `steps` Euler steps with dt = 1 under stochastic_mask draws of
+ * StdRng::seed_from_u64(seed ^ 0x5eed2d) (ones when update_prob >= 1).
+ * Step k's input is recorded: snapshot_positions [steps][B*N][4],
+ * snapshot_states [steps][B*N*C], snapshot_masks [steps][B*N].  The final
+ * particles go to final_positions / final_states and *mean_dx_norm_sum is
+ * the f32 running sum over steps of mean_dx_norm.  3D models with position
+ * features and C > 3 return NPA_ERR_UNSUPPORTED (the training rollout
+ * applies no position gates, the device step does). */
+npa_status npa_model_rollout_for_training(npa_model* model, const npa_grid_config* grid,
+                                          const float* positions, int64_t positions_len,
+                                          const float* states, int64_t states_len, int64_t batch,
+                                          int64_t n, int64_t steps, float update_prob,
+                                          uint64_t seed, float* snapshot_positions,
+                                          float* snapshot_states, float* snapshot_masks,
+                                          float* final_positions, float* final_states,
+                                          float* mean_dx_norm_sum);
+
+/* bptt_gradients (crates/burn_automata/src/target2d.rs:3550-3722) over the
+ * snapshots npa_model_rollout_for_training recorded: starting from the loss
+ * adjoints position_gradients [B*N][4] and state_gradients [B*N*C], each
+ * step in reverse recomputes the perception and raw update, forms the
+ * output adjoint (raw_motion_adjoint, the displacement regularizer with
+ * weight / rows, the masked state adjoint), back-propagates the MLP (sums
+ * into gw1..gb2) and adds the perception adjoint to the running adjoints
+ * unless stopgrad_pos / stopgrad_state.  The Euler step's Jacobian is the
+ * identity, as the reference's.  The MLP terms are bit for bit the
+ * reference's; the perception adjoint scatters with atomics
+ * (npa_perceive_adjoint_with_options), so across steps the results agree to
+ * f32 summation error.  initial_position_adjoint [B*N][4] and
+ * initial_state_adjoint [B*N*C] (the adjoints at the rollout's input) may
+ * be NULL. */
+npa_status npa_model_bptt_gradients(npa_model* model, const npa_grid_config* grid,
+                                    const float* snapshot_positions, const float* snapshot_states,
+                                    const float* snapshot_masks, int64_t batch, int64_t n,
+                                    int64_t steps, const float* position_gradients,
+                                    const float* state_gradients,
+                                    float displacement_regularizer_weight, int32_t stopgrad_pos,
+                                    int32_t stopgrad_state, float* gw1, float* gb1, float* gw2,
+                                    float* gb2, float* initial_position_adjoint,
+                                    float* initial_state_adjoint);
+
 /* perceive_adjoint_with_options
  * (crates/burn_automata_kernels/src/reference/adjoint.rs:28-136): given the
  * adjoint of the perception features [B*N][F] (F as perceive_with_options),

@@ -167,12 +167,93 @@ def lib():
         L.ora_stdrng_key.argtypes = [ctypes.c_uint64, u32p]
         L.ora_chacha_block.argtypes = [u32p, ctypes.c_uint64, ctypes.c_int, u32p]
         L.ora_rollout_masks.argtypes = [ctypes.c_uint64, ctypes.c_float, i64, i64, i64, f32p]
+        L.ora_mlp_backward.argtypes = [f32p, i64, i64, i64, i64, f32p, f32p, f32p, f32p, f32p,
+                                       f32p, f32p, f32p, f32p]
+        L.ora_rollout_for_training.argtypes = [P(_Model), f32p, f32p, f32p, f32p, P(_Grid), f32p,
+                                               f32p, i64, i64, i64, ctypes.c_float,
+                                               ctypes.c_uint64, f32p, f32p, f32p, f32p, f32p,
+                                               f32p]
+        L.ora_bptt_gradients.argtypes = [P(_Model), f32p, f32p, f32p, f32p, P(_Grid), f32p, f32p,
+                                         f32p, i64, i64, i64, f32p, f32p, ctypes.c_float,
+                                         ctypes.c_int, ctypes.c_int, f32p, f32p, f32p, f32p, f32p,
+                                         f32p]
         L.ora_set_threads.argtypes = [ctypes.c_int]
         L.ora_set_log1p_mode.argtypes = [ctypes.c_int]
         L.ora_ln_1p.argtypes = [f32p, i64, f32p]
         L.ora_get_threads.restype = ctypes.c_int
         _lib = L
     return _lib
+
+
+def mlp_backward(features, rows: int, in_dims: int, hidden: int, out_dims: int, w1, b1, w2,
+                 output_gradients):
+    """training.rs:558 mlp_backward_from_output_gradients -> (gw1, gb1, gw2, gb2, gfeatures)."""
+    f = _f32(features).reshape(-1)
+    g = _f32(output_gradients).reshape(-1)
+    ws = [_f32(w).reshape(-1) for w in (w1, b1, w2)]
+    out = [np.zeros(hidden * in_dims, np.float32), np.zeros(hidden, np.float32),
+           np.zeros(out_dims * hidden, np.float32), np.zeros(out_dims, np.float32),
+           np.zeros(rows * in_dims, np.float32)]
+    _check(lib().ora_mlp_backward(_ptr(f), rows, in_dims, hidden, out_dims, *[_ptr(w) for w in ws],
+                                  _ptr(g), *[_ptr(o) for o in out]), "mlp_backward")
+    return tuple(out)
+
+
+def rollout_for_training(model_cfg, weights, grid, positions, states, batch, n, steps,
+                         update_prob=1.0, seed=0):
+    """target2d.rs:3414 rollout_for_training -> dict(snapshot positions [steps, B*N, 4],
+    states [steps, B*N*C], masks [steps, B*N], final positions / states, mean_dx_norm_sum)."""
+    m = model_struct(model_cfg)
+    g = grid_struct(grid)
+    c = model_cfg.state_dims
+    total = batch * n
+    w1, b1, w2, b2 = [_f32(w) for w in (weights.w1, weights.b1, weights.w2, weights.b2)]
+    pos = _f32(positions).reshape(-1, 4)
+    st = _f32(states).reshape(-1)
+    sp = np.zeros((steps, total, 4), np.float32)
+    ss = np.zeros((steps, total * c), np.float32)
+    sm = np.zeros((steps, total), np.float32)
+    fp = np.zeros((total, 4), np.float32)
+    fs = np.zeros(total * c, np.float32)
+    mean = np.zeros(1, np.float32)
+    _check(lib().ora_rollout_for_training(ctypes.byref(m), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
+                                          ctypes.byref(g), _ptr(pos), _ptr(st), batch, n, steps,
+                                          float(update_prob), int(seed) & 0xFFFFFFFFFFFFFFFF,
+                                          _ptr(sp), _ptr(ss), _ptr(sm), _ptr(fp), _ptr(fs),
+                                          _ptr(mean)), "rollout_for_training")
+    return {"snapshot_positions": sp, "snapshot_states": ss, "snapshot_masks": sm,
+            "final_positions": fp, "final_states": fs, "mean_dx_norm_sum": float(mean[0])}
+
+
+def bptt_gradients(model_cfg, weights, grid, rollout, batch, n, position_gradients,
+                   state_gradients, regularizer_weight=0.0, stopgrad_pos=False,
+                   stopgrad_state=False):
+    """target2d.rs:3550 bptt_gradients -> dict(w1, b1, w2, b2, position_adjoint, state_adjoint)."""
+    m = model_struct(model_cfg)
+    g = grid_struct(grid)
+    c = model_cfg.state_dims
+    total = batch * n
+    steps = rollout["snapshot_masks"].shape[0]
+    f = int(lib().ora_model_perception_dims(ctypes.byref(m)))
+    h, o = model_cfg.hidden_dims, model_cfg.spatial_dims + c
+    w1, b1, w2, b2 = [_f32(w) for w in (weights.w1, weights.b1, weights.w2, weights.b2)]
+    sp = _f32(rollout["snapshot_positions"]).reshape(-1)
+    ss = _f32(rollout["snapshot_states"]).reshape(-1)
+    sm = _f32(rollout["snapshot_masks"]).reshape(-1)
+    pg = _f32(position_gradients).reshape(-1)
+    sg = _f32(state_gradients).reshape(-1)
+    out = {"w1": np.zeros(h * f, np.float32), "b1": np.zeros(h, np.float32),
+           "w2": np.zeros(o * h, np.float32), "b2": np.zeros(o, np.float32),
+           "position_adjoint": np.zeros((total, 4), np.float32),
+           "state_adjoint": np.zeros(total * c, np.float32)}
+    _check(lib().ora_bptt_gradients(ctypes.byref(m), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
+                                    ctypes.byref(g), _ptr(sp), _ptr(ss), _ptr(sm), batch, n, steps,
+                                    _ptr(pg), _ptr(sg), float(regularizer_weight),
+                                    int(bool(stopgrad_pos)), int(bool(stopgrad_state)),
+                                    _ptr(out["w1"]), _ptr(out["b1"]), _ptr(out["w2"]),
+                                    _ptr(out["b2"]), _ptr(out["position_adjoint"]),
+                                    _ptr(out["state_adjoint"])), "bptt_gradients")
+    return out
 
 
 def ln_1p(x) -> np.ndarray:

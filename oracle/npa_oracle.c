@@ -1077,15 +1077,17 @@ void ora_chacha_block(const uint32_t key[8], uint64_t counter, int rounds, uint3
 }
 #undef ORA_QR
 
-int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
-                      int64_t first_step, int64_t steps, float* out) {
+/* stochastic_mask draws of StdRng::seed_from_u64(rng_seed) for `steps` steps
+ * of `count` particles from step first_step. */
+static int stdrng_masks(uint64_t rng_seed, float update_prob, int64_t count, int64_t first_step,
+                        int64_t steps, float* out) {
   if (count < 0 || steps < 0 || first_step < 0) return ORA_ERR_INVALID_ARGUMENT;
   if (update_prob >= 1.0f) {
     for (int64_t i = 0; i < count * steps; ++i) out[i] = 1.0f;
     return ORA_OK;
   }
   uint32_t key[8], block[16];
-  ora_stdrng_key(rollout_seed ^ 0x5eedull, key);
+  ora_stdrng_key(rng_seed, key);
   uint64_t have = UINT64_MAX;
   for (int64_t k = 0; k < steps; ++k) {
     for (int64_t i = 0; i < count; ++i) {
@@ -1099,6 +1101,277 @@ int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
     }
   }
   return ORA_OK;
+}
+
+int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
+                      int64_t first_step, int64_t steps, float* out) {
+  return stdrng_masks(rollout_seed ^ 0x5eedull, update_prob, count, first_step, steps, out);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Training rollout (crates/burn_automata/src/target2d.rs, training.rs)      */
+/* ------------------------------------------------------------------------ */
+
+/* mlp_backward_from_output_gradients (training.rs:558-640): per row the
+ * forward pass again (pre-activation and ReLU), then the hidden and input
+ * adjoints; the weight gradients are summed over the rows in row order. */
+int ora_mlp_backward(const float* features, int64_t rows, int64_t in_dims, int64_t hidden,
+                     int64_t out_dims, const float* w1, const float* b1, const float* w2,
+                     const float* output_gradients, float* gw1, float* gb1, float* gw2,
+                     float* gb2, float* gfeatures) {
+  if (rows <= 0 || in_dims <= 0 || hidden <= 0 || out_dims <= 0) return ORA_ERR_INVALID_ARGUMENT;
+  memset(gw1, 0, (size_t)(hidden * in_dims) * sizeof(float));
+  memset(gb1, 0, (size_t)hidden * sizeof(float));
+  memset(gw2, 0, (size_t)(out_dims * hidden) * sizeof(float));
+  memset(gb2, 0, (size_t)out_dims * sizeof(float));
+  memset(gfeatures, 0, (size_t)(rows * in_dims) * sizeof(float));
+  float* pre = (float*)malloc((size_t)hidden * sizeof(float));
+  float* hid = (float*)malloc((size_t)hidden * sizeof(float));
+  float* dh = (float*)malloc((size_t)hidden * sizeof(float));
+  if (!pre || !hid || !dh) {
+    free(pre);
+    free(hid);
+    free(dh);
+    return ORA_ERR_INVALID_ARGUMENT;
+  }
+  for (int64_t row = 0; row < rows; ++row) {
+    for (int64_t h = 0; h < hidden; ++h) dh[h] = 0.0f;
+    const float* f = features + row * in_dims;
+    for (int64_t h = 0; h < hidden; ++h) {
+      float sum = b1[h];
+      for (int64_t i = 0; i < in_dims; ++i) sum = sum + w1[h * in_dims + i] * f[i];
+      pre[h] = sum;
+      hid[h] = maxf_rs(sum, 0.0f);
+    }
+    const float* g = output_gradients + row * out_dims;
+    for (int64_t o = 0; o < out_dims; ++o) {
+      const float d = g[o];
+      gb2[o] = gb2[o] + d;
+      for (int64_t h = 0; h < hidden; ++h) {
+        gw2[o * hidden + h] = gw2[o * hidden + h] + d * hid[h];
+        dh[h] = dh[h] + d * w2[o * hidden + h];
+      }
+    }
+    for (int64_t h = 0; h < hidden; ++h) {
+      const float dp = pre[h] > 0.0f ? dh[h] : 0.0f;
+      gb1[h] = gb1[h] + dp;
+      for (int64_t i = 0; i < in_dims; ++i) {
+        gw1[h * in_dims + i] = gw1[h * in_dims + i] + dp * f[i];
+        gfeatures[row * in_dims + i] = gfeatures[row * in_dims + i] + dp * w1[h * in_dims + i];
+      }
+    }
+  }
+  free(pre);
+  free(hid);
+  free(dh);
+  return ORA_OK;
+}
+
+/* raw_motion_adjoint (target2d.rs:3644-3673): the adjoint of
+ * dx = scale * raw / (1 + |raw|) with respect to raw, added into out. */
+static void raw_motion_adjoint(const float* raw, const float* dx_adj, int dims, float scale,
+                               float* out) {
+  float norm = 0.0f;
+  for (int a = 0; a < dims; ++a) norm = norm + raw[a] * raw[a];
+  norm = sqrtf(norm);
+  const float denom = 1.0f + norm;
+  float dot = 0.0f;
+  for (int a = 0; a < dims; ++a) dot = dot + raw[a] * dx_adj[a];
+  for (int a = 0; a < dims; ++a) {
+    float grad = dx_adj[a] / denom;
+    if (norm > 0.0f) grad = grad - raw[a] * dot / (norm * denom * denom);
+    out[a] = out[a] + scale * grad;
+  }
+}
+
+/* add_dx_norm_regularizer_adjoint (target2d.rs:3675-3722). */
+static void dx_norm_regularizer_adjoint(const float* raw, int dims, float scale, float weight,
+                                        float* out) {
+  if (weight == 0.0f) return;
+  float norm = 0.0f;
+  for (int a = 0; a < dims; ++a) norm = norm + raw[a] * raw[a];
+  norm = sqrtf(norm);
+  float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int a = 0; a < dims; ++a) dx[a] = scale * raw[a] / (1.0f + norm);
+  float dx_norm = 0.0f;
+  for (int a = 0; a < dims; ++a) dx_norm = dx_norm + dx[a] * dx[a];
+  dx_norm = sqrtf(dx_norm);
+  if (dx_norm == 0.0f) return;
+  float adj[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int a = 0; a < dims; ++a) adj[a] = weight * dx[a] / dx_norm;
+  raw_motion_adjoint(raw, adj, dims, scale, out);
+}
+
+/* rollout_for_training (target2d.rs:3414-3466): `steps` steps with dt = 1 and
+ * the masks of StdRng::seed_from_u64(seed ^ 0x5eed2d); every step's input
+ * positions, states and mask are recorded; mean_dx_norm_sum adds each step's
+ * mean |dx| (spatial axes) in f32. */
+int ora_rollout_for_training(const ora_model_config* m, const float* w1, const float* b1,
+                             const float* w2, const float* b2, const ora_grid_config* grid,
+                             const float* positions, const float* states, int64_t batch,
+                             int64_t n, int64_t steps, float update_prob, uint64_t seed,
+                             float* snap_positions, float* snap_states, float* snap_masks,
+                             float* final_positions, float* final_states,
+                             float* mean_dx_norm_sum) {
+  const int64_t total = batch * n, c = m->state_dims;
+  float* masks = (float*)malloc((size_t)(total * steps > 0 ? total * steps : 1) * sizeof(float));
+  float* pos = (float*)malloc((size_t)(total > 0 ? total : 1) * 4 * sizeof(float));
+  float* st = (float*)malloc((size_t)(total * c > 0 ? total * c : 1) * sizeof(float));
+  float* np = (float*)malloc((size_t)(total > 0 ? total : 1) * 4 * sizeof(float));
+  float* ns = (float*)malloc((size_t)(total * c > 0 ? total * c : 1) * sizeof(float));
+  float* dx = (float*)malloc((size_t)(total > 0 ? total : 1) * 4 * sizeof(float));
+  int rc = ORA_OK;
+  if (!masks || !pos || !st || !np || !ns || !dx) {
+    rc = ORA_ERR_INVALID_ARGUMENT;
+    goto done;
+  }
+  rc = stdrng_masks(seed ^ 0x5eed2dull, update_prob, total, 0, steps, masks);
+  if (rc) goto done;
+  memcpy(pos, positions, (size_t)total * 4 * sizeof(float));
+  memcpy(st, states, (size_t)(total * c) * sizeof(float));
+  float sum = 0.0f;
+  for (int64_t k = 0; k < steps; ++k) {
+    memcpy(snap_positions + k * total * 4, pos, (size_t)total * 4 * sizeof(float));
+    memcpy(snap_states + k * total * c, st, (size_t)(total * c) * sizeof(float));
+    memcpy(snap_masks + k * total, masks + k * total, (size_t)total * sizeof(float));
+    rc = ora_step(m, w1, b1, w2, b2, grid, pos, st, batch, n, 1.0f, masks + k * total, np, ns,
+                  dx, NULL, NULL, NULL);
+    if (rc) goto done;
+    /* mean_dx_norm (target2d.rs:3536-3548) */
+    float norms = 0.0f;
+    for (int64_t i = 0; i < total; ++i) {
+      float s = 0.0f;
+      for (int a = 0; a < m->spatial_dims; ++a) s = s + dx[4 * i + a] * dx[4 * i + a];
+      norms = norms + sqrtf(s);
+    }
+    sum = sum + norms / (float)(total > 1 ? total : 1);
+    float* t = pos;
+    pos = np;
+    np = t;
+    t = st;
+    st = ns;
+    ns = t;
+  }
+  memcpy(final_positions, pos, (size_t)total * 4 * sizeof(float));
+  memcpy(final_states, st, (size_t)(total * c) * sizeof(float));
+  *mean_dx_norm_sum = sum;
+done:
+  free(masks);
+  free(pos);
+  free(st);
+  free(np);
+  free(ns);
+  free(dx);
+  return rc;
+}
+
+/* bptt_gradients (target2d.rs:3550-3642): back through the recorded steps in
+ * reverse; per step the features and raw update again, the output adjoint
+ * (raw_motion_adjoint of the masked position adjoint, the optional
+ * displacement regularizer, the masked state adjoint), the MLP backward, and
+ * the perception adjoint added to the running position / state adjoints
+ * (unless stopped).  The Euler step is differentiated as the reference does:
+ * identity plus the masked update (no wrap or clamp terms). */
+int ora_bptt_gradients(const ora_model_config* m, const float* w1, const float* b1,
+                       const float* w2, const float* b2, const ora_grid_config* grid,
+                       const float* snap_positions, const float* snap_states,
+                       const float* snap_masks, int64_t batch, int64_t n, int64_t steps,
+                       const float* position_gradients, const float* state_gradients,
+                       float regularizer_weight, int stopgrad_pos, int stopgrad_state,
+                       float* gw1, float* gb1, float* gw2, float* gb2, float* pos_adj_out,
+                       float* state_adj_out) {
+  const int64_t total = batch * n, c = m->state_dims, dim = m->spatial_dims;
+  const int64_t hdim = m->hidden_dims, od = dim + c;
+  const int scale_eq = m->equivariance == 2;
+  const int pde = m->equivariance == 1 || m->equivariance == 2;
+  ora_perception_options opt;
+  memset(&opt, 0, sizeof opt);
+  opt.state_grad = m->state_grad;
+  opt.density_grad = m->density_grad;
+  opt.eps0 = m->eps0;
+  opt.scale_equivariance = (uint8_t)scale_eq;
+  opt.particle_density_equivariance = (uint8_t)pde;
+  opt.log_norm_grad = m->log_norm_grad;
+  opt.log_norm_density_grad = m->log_norm_density_grad;
+  opt.hybrid_state_gradient = 1;
+  opt.position_features = m->position_features;
+  const int64_t fd = ora_feature_dims(grid, &opt, c);
+  const float motion_eps = scale_eq ? grid->eps : m->eps0;
+  const float scale = m->alpha * motion_eps;
+  const float reg_scale =
+      regularizer_weight == 0.0f ? 0.0f : regularizer_weight / (float)(total > 1 ? total : 1);
+  float* pos_adj = (float*)malloc((size_t)(total > 0 ? total : 1) * 4 * sizeof(float));
+  float* st_adj = (float*)malloc((size_t)(total * c > 0 ? total * c : 1) * sizeof(float));
+  float* feat = (float*)malloc((size_t)(total * fd > 0 ? total * fd : 1) * sizeof(float));
+  float* upd = (float*)malloc((size_t)(total * od > 0 ? total * od : 1) * sizeof(float));
+  float* oadj = (float*)malloc((size_t)(total * od > 0 ? total * od : 1) * sizeof(float));
+  float* sw1 = (float*)malloc((size_t)(hdim * fd) * sizeof(float));
+  float* sb1 = (float*)malloc((size_t)hdim * sizeof(float));
+  float* sw2 = (float*)malloc((size_t)(od * hdim) * sizeof(float));
+  float* sb2 = (float*)malloc((size_t)od * sizeof(float));
+  float* gfeat = (float*)malloc((size_t)(total * fd > 0 ? total * fd : 1) * sizeof(float));
+  float* pst = (float*)malloc((size_t)(total * c > 0 ? total * c : 1) * sizeof(float));
+  float* ppos = (float*)malloc((size_t)(total > 0 ? total : 1) * 4 * sizeof(float));
+  int rc = ORA_OK;
+  if (!pos_adj || !st_adj || !feat || !upd || !oadj || !sw1 || !sb1 || !sw2 || !sb2 || !gfeat ||
+      !pst || !ppos) {
+    rc = ORA_ERR_INVALID_ARGUMENT;
+    goto done;
+  }
+  memcpy(pos_adj, position_gradients, (size_t)total * 4 * sizeof(float));
+  memcpy(st_adj, state_gradients, (size_t)(total * c) * sizeof(float));
+  memset(gw1, 0, (size_t)(hdim * fd) * sizeof(float));
+  memset(gb1, 0, (size_t)hdim * sizeof(float));
+  memset(gw2, 0, (size_t)(od * hdim) * sizeof(float));
+  memset(gb2, 0, (size_t)od * sizeof(float));
+  for (int64_t k = steps - 1; k >= 0; --k) {
+    const float* sp = snap_positions + k * total * 4;
+    const float* ss = snap_states + k * total * c;
+    const float* sm = snap_masks + k * total;
+    rc = ora_perceive(grid, &opt, sp, ss, batch, n, c, feat, NULL, NULL, NULL, NULL);
+    if (rc) goto done;
+    rc = ora_forward_update(feat, total, fd, hdim, od, w1, b1, w2, b2, upd);
+    if (rc) goto done;
+    for (int64_t row = 0; row < total; ++row) {
+      float* o = oadj + row * od;
+      for (int64_t j = 0; j < od; ++j) o[j] = 0.0f;
+      const float mask = sm[row];
+      float dxa[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int64_t a = 0; a < dim; ++a) dxa[a] = pos_adj[4 * row + a] * mask;
+      dx_norm_regularizer_adjoint(upd + row * od, (int)dim, scale, reg_scale, o);
+      raw_motion_adjoint(upd + row * od, dxa, (int)dim, scale, o);
+      for (int64_t ch = 0; ch < c; ++ch) o[dim + ch] = o[dim + ch] + st_adj[row * c + ch] * mask;
+    }
+    rc = ora_mlp_backward(feat, total, fd, hdim, od, w1, b1, w2, oadj, sw1, sb1, sw2, sb2, gfeat);
+    if (rc) goto done;
+    for (int64_t i = 0; i < hdim * fd; ++i) gw1[i] = gw1[i] + sw1[i];
+    for (int64_t i = 0; i < hdim; ++i) gb1[i] = gb1[i] + sb1[i];
+    for (int64_t i = 0; i < od * hdim; ++i) gw2[i] = gw2[i] + sw2[i];
+    for (int64_t i = 0; i < od; ++i) gb2[i] = gb2[i] + sb2[i];
+    rc = ora_perceive_adjoint(grid, &opt, sp, ss, batch, n, c, gfeat, pst, ppos);
+    if (rc) goto done;
+    if (!stopgrad_pos)
+      for (int64_t row = 0; row < total; ++row)
+        for (int64_t a = 0; a < dim; ++a) pos_adj[4 * row + a] = pos_adj[4 * row + a] + ppos[4 * row + a];
+    if (!stopgrad_state)
+      for (int64_t i = 0; i < total * c; ++i) st_adj[i] = st_adj[i] + pst[i];
+  }
+  if (pos_adj_out) memcpy(pos_adj_out, pos_adj, (size_t)total * 4 * sizeof(float));
+  if (state_adj_out) memcpy(state_adj_out, st_adj, (size_t)(total * c) * sizeof(float));
+done:
+  free(pos_adj);
+  free(st_adj);
+  free(feat);
+  free(upd);
+  free(oadj);
+  free(sw1);
+  free(sb1);
+  free(sw2);
+  free(sb2);
+  free(gfeat);
+  free(pst);
+  free(ppos);
+  return rc;
 }
 
 /* ---- splat_particles_2d (crates/burn_automata_kernels/src/splat.rs:30-93) ----

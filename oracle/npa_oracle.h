@@ -196,6 +196,27 @@ void ora_chacha_block(const uint32_t key[8], uint64_t counter, int rounds, uint3
 /* out[k * count + i] for rollout steps first_step + k (0-based), k < steps. */
 int ora_rollout_masks(uint64_t rollout_seed, float update_prob, int64_t count,
                       int64_t first_step, int64_t steps, float* out);
+/* Training rollout (crates/burn_automata/src/training.rs:558-640,
+ * target2d.rs:3414-3722). */
+int ora_mlp_backward(const float* features, int64_t rows, int64_t in_dims, int64_t hidden,
+                     int64_t out_dims, const float* w1, const float* b1, const float* w2,
+                     const float* output_gradients, float* gw1, float* gb1, float* gw2,
+                     float* gb2, float* gfeatures);
+int ora_rollout_for_training(const ora_model_config* m, const float* w1, const float* b1,
+                             const float* w2, const float* b2, const ora_grid_config* grid,
+                             const float* positions, const float* states, int64_t batch,
+                             int64_t n, int64_t steps, float update_prob, uint64_t seed,
+                             float* snap_positions, float* snap_states, float* snap_masks,
+                             float* final_positions, float* final_states,
+                             float* mean_dx_norm_sum);
+int ora_bptt_gradients(const ora_model_config* m, const float* w1, const float* b1,
+                       const float* w2, const float* b2, const ora_grid_config* grid,
+                       const float* snap_positions, const float* snap_states,
+                       const float* snap_masks, int64_t batch, int64_t n, int64_t steps,
+                       const float* position_gradients, const float* state_gradients,
+                       float regularizer_weight, int stopgrad_pos, int stopgrad_state,
+                       float* gw1, float* gb1, float* gw2, float* gb2, float* pos_adj_out,
+                       float* state_adj_out);
 /* out[i] = log1pf(x[i]) of the host C library (f32::ln_1p of the reference). */
 void ora_ln_1p(const float* x, int64_t count, float* out);
 /* 0 (default): log1pf as the reference binds it; 1: f64 log1p rounded to f32,
