@@ -516,6 +516,8 @@ def run_ours(args, rank, world, local_rank):
                                                    w.weights.b2), device=local_rank)
         ex = ba.CudaAutomataExecutor(model, w.grid, w.batch, w.n)
         ex.create_state(w.positions, w.states)
+        if args.fused:
+            ex.set_fused_step(True)
         ex.step_state_many(args.warmup, w.dt, use_graph=True, stream=sptr)
         features = w.model.perception_dims()
     torch.cuda.synchronize()
@@ -635,6 +637,8 @@ def run_ours(args, rank, world, local_rank):
                        "state_dims": w.state_dims, "features": features,
                        "eps": w.grid.eps, "grid": list(w.grid.grid_size[:w.grid.dim]),
                        "parallelism": parallelism,
+                       "step_kernels": ("fused perception + MLP + Euler" if args.fused
+                                        else "perception tiles, then MLP + Euler"),
                        "l2": ("no flush: per-step working set exceeds the 126 MB L2"
                               if particles_rank >= (1 << 20) else
                               "no flush: the shard's per-step working set is below the 126 MB "
@@ -707,6 +711,9 @@ def main():
     ap.add_argument("--rollouts", type=int, default=None,
                     help="rollouts in total (split over the ranks) for cfg2 or with --strong; "
                          "per rank otherwise (default: 256 for cfg2, 1 otherwise)")
+    ap.add_argument("--fused", action="store_true",
+                    help="executor step as one perception + MLP + Euler kernel after the density "
+                         "pass (2D, sparse cells)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -159,6 +159,7 @@ SIGNATURES = [
     ("npa_executor_read_state", c_i32, [vp, f32p, f32p]),
     ("npa_executor_state_device", c_i32, [vp, P(vp), P(vp)]),
     ("npa_executor_launches_per_step", c_i32, [vp, P(c_i64)]),
+    ("npa_executor_set_fused_step", c_i32, [vp, c_i32]),
 ]
 
 # Symbols exported beyond the public header (test hooks).

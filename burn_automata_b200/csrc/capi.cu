@@ -1305,6 +1305,9 @@ struct npa_executor {
   uint32_t* d_lane_seeds = nullptr;  // [batch]
   uint32_t* d_step = nullptr;
   uint32_t step_index = 0;
+  // Fused step: phase 2 is empty and phase 3 runs perception + MLP + Euler in
+  // one kernel (npa_executor_set_fused_step).
+  int fused = 0;
 };
 
 namespace {
@@ -1319,6 +1322,7 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
     case 1:
       return launch_density(e->g, sv, B, e->w.volume, nullptr, e->w.hits, s);
     case 2:
+      if (e->fused) return NPA_OK;
       return launch_perception_tiles(e->g, e->p, sv, e->w.hits, B, e->st[from], e->model->dm.state_dims,
                                      e->w.volume, e->tile_rows, e->w.tiles, s);
     default: {
@@ -1334,8 +1338,12 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
         sm.lane_seeds = e->d_lane_seeds;
         sm.step_counter = e->d_step;
       }
-      NPA_TRY(launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr, sm,
-                              out, s));
+      if (e->fused)
+        NPA_TRY(launch_fused_step(e->model->dm, e->g, e->p, sv, e->w.hits, B, e->st[from],
+                                  e->w.volume, dt, nullptr, sm, out, s));
+      else
+        NPA_TRY(launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr,
+                                sm, out, s));
       if (e->stochastic) NPA_TRY(launch_advance_step(e->d_step, s));
       return NPA_OK;
     }
@@ -1379,6 +1387,7 @@ npa_status exec_capture(npa_executor* e, float dt, cudaStream_t stream) {
 npa_status exec_run_phase(npa_executor* e, int phase, float dt, int32_t use_graph,
                           cudaStream_t s) {
   if (use_graph) {
+    if (e->launches[phase] == 0) return NPA_OK;  // an empty phase (perception when fused)
     NPA_CUDA(cudaGraphLaunch(e->graph[e->cur][phase], s), "cudaGraphLaunch");
     g_launches.fetch_add(uint64_t(e->launches[phase]), std::memory_order_relaxed);
     return NPA_OK;
@@ -1601,6 +1610,22 @@ npa_status npa_executor_state_device(npa_executor* e, float** d_positions, float
   if (!e || !d_positions || !d_states) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
   *d_positions = e->pos[e->cur];
   *d_states = e->st[e->cur];
+  return NPA_OK;
+}
+
+npa_status npa_executor_set_fused_step(npa_executor* e, int32_t fused) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  const uint32_t B = uint32_t(e->batch), N = uint32_t(e->n);
+  if (fused && !fused_step_supported(e->model->dm, e->g, e->p, B, B * N))
+    return fail(NPA_ERR_UNSUPPORTED,
+                "the fused step covers 2D models with more than 4 channels, hidden width up to "
+                "128 and sparse cells");
+  if ((fused != 0) != (e->fused != 0)) {
+    NPA_TRY(ensure_device(e->model->dm.device));
+    exec_drop_graphs(e);
+    for (auto& l : e->launches) l = 0;
+  }
+  e->fused = fused != 0;
   return NPA_OK;
 }
 

@@ -166,6 +166,17 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
                            const StepOutputs& out, cudaStream_t stream, uint32_t tile_begin = 0,
                            uint32_t tile_end = 0xffffffffu);
 
+// The fused step (perception + MLP + Euler in one kernel, after the density
+// pass): supported for 2D models with more than 4 channels, hidden width up
+// to 128 and sparse cells; the same results as perception tiles + MLP step.
+bool fused_step_supported(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                          uint32_t batch, uint32_t total);
+npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                             const SortedGrid& s, const HitLists& hl, uint32_t batch,
+                             const float* states, const float* volume_sorted, float dt,
+                             const float* mask, const StochasticMask& sm, const StepOutputs& out,
+                             cudaStream_t stream);
+
 // ---- training rollout backward (train.cu) ----
 // out[r][O] = adjoint of row r's raw update (target2d.rs:3566-3604): the masked
 // position adjoint through raw_motion_adjoint, the displacement regularizer

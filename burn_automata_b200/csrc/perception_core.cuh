@@ -29,7 +29,8 @@ struct PerceptionAcc {
 // the f64 log1p, the correction and the division stay out of line (one copy
 // serves every channel: inlined per channel they crowded the perception
 // kernels out of the instruction cache, cfg2 perception 0.437 -> 0.406 ms).
-__device__ __noinline__ float log_norm_scale(float norm, uint32_t word, const Log1pTable t) {
+static __device__ __noinline__ float log_norm_scale(float norm, uint32_t word,
+                                                  const Log1pTable t) {
   return log1p_host_word(norm, word, t) / norm;
 }
 

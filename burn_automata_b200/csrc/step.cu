@@ -31,7 +31,7 @@
 // position / state in the caller's particle order.
 #include <algorithm>
 
-#include "npa_internal.h"
+#include "perception_core.cuh"
 
 namespace npa {
 namespace {
@@ -53,6 +53,7 @@ struct MlpShape {
   int out_stride;  // O + 1
   int w1_resident; // w1^T [F][Hp] kept in shared memory for the whole kernel
   int l2_rows;     // layer-2 rows per thread: 2, or 3 when M splits into triples with less waste
+  int alias;       // the feature tile and the hidden rows share one region (fused step)
 };
 
 struct SmemLayout {
@@ -67,8 +68,14 @@ __host__ __device__ inline SmemLayout smem_layout(const MlpShape& s) {
     off += (floats + 3) & ~size_t(3);
     return o;
   };
-  l.ft0 = take(size_t(s.F) * s.M);
-  l.hid = take(size_t(s.M) * s.hid_stride);
+  if (s.alias) {
+    const size_t ft_floats = size_t(s.F) * s.M, hid_floats = size_t(s.M) * s.hid_stride;
+    l.ft0 = take(ft_floats > hid_floats ? ft_floats : hid_floats);
+    l.hid = l.ft0;
+  } else {
+    l.ft0 = take(size_t(s.F) * s.M);
+    l.hid = take(size_t(s.M) * s.hid_stride);
+  }
   l.w1 = take(size_t(s.w1_resident ? s.F : kKC) * s.Hp);
   l.w2 = take(size_t(s.O) * s.w2_stride);
   l.outs = take(size_t(s.M) * s.out_stride);
@@ -199,7 +206,9 @@ __device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __res
   }
 }
 
-template <int HG, int NT>
+// ALIAS: hid overlays ft, so the block synchronises before the hidden rows
+// are stored.
+template <int HG, int NT, bool ALIAS = false>
 __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
                                            const float (&bias)[kTH], const float* ft,
                                            float* w1s, float* hid) {
@@ -247,6 +256,7 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
       }
     }
   }
+  if constexpr (ALIAS) __syncthreads();
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float* row = hid + (rg * 8 + i) * s.hid_stride;
@@ -459,6 +469,145 @@ struct StepParams {
 // channels; beyond kStateRegs of them the rest are read in the epilogue).
 constexpr int kStateRegs = 8;
 
+// One tile of the MLP stage: rows tile * M + [0, M) of the sorted order,
+// features in ft [F][M].  Layer 1, layer 2, then
+// forward_from_features_with_eps + gates + euler_step with TPR threads per
+// row; after_layer2() runs once layer 2 has finished with ft and hid.
+template <int HG, int NT, bool ALIAS, class AfterLayer2>
+__device__ __forceinline__ void mlp_tile(
+    const MlpShape& s, const GridParams& g, const SortedGrid& sg, uint32_t total, uint32_t tile,
+    const float (&bias1)[kTH], const float* __restrict__ w1t, const float* __restrict__ b2,
+    const StepParams& sp, const EulerParams& ep, const float* __restrict__ mask,
+    float4* __restrict__ next_pos, float* __restrict__ next_states, float4* __restrict__ dx_out,
+    float* __restrict__ ds_out, float* __restrict__ features_out, uint32_t step_index, float* ft,
+    float* w1s, float* hid, float* w2s, float* outs, AfterLayer2&& after_layer2) {
+  constexpr int TPR = HG / 8;  // layer-2 / epilogue threads per row (NT / M)
+  const int C = sp.C, D = sp.D;
+  const int r = threadIdx.x / TPR;
+  const int part = threadIdx.x - r * TPR;
+  // Each of a row's TPR threads owns a contiguous run of cpt channels, read
+  // and written as float4 when the rows are 16-byte aligned.
+  const int cpt = (C + TPR - 1) / TPR;
+  const int c0 = part * cpt;
+  const int cend = min(C, c0 + cpt);
+  const bool vec = (C % 4 == 0) && (cpt % 4 == 0) && cpt <= kStateRegs &&
+                   ((reinterpret_cast<uintptr_t>(sp.states) | reinterpret_cast<uintptr_t>(next_states) |
+                     reinterpret_cast<uintptr_t>(ds_out)) & 15u) == 0;
+  // The epilogue's position / mask reads are issued before layer 1 so
+  // their latency is hidden behind it.
+  const uint32_t q = tile * s.M + r;
+  const bool live = q < total;
+  size_t row = 0;
+  float4 pi = make_float4(0.f, 0.f, 0.f, 0.f);
+  float m = 1.0f;
+  if (live) {
+    const uint32_t batch = q / sg.n;
+    const uint32_t local = __ldg(sg.permutation + q);
+    row = size_t(batch) * sg.n + local;
+    pi = __ldg(sg.positions + row);
+    if (sp.lane_seeds)
+      m = stochastic_update_mask(sp.update_prob, local, step_index, __ldg(sp.lane_seeds + batch));
+    else if (mask)
+      m = __ldg(mask + row);
+  }
+  if (features_out && live)
+    for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
+  mlp_layer1<HG, NT, ALIAS>(s, w1t, bias1, ft, w1s, hid);
+  __syncthreads();
+  // own state for the Euler update, hidden behind layer 2
+  float sv[kStateRegs];
+  if (vec) {
+#pragma unroll
+    for (int j4 = 0; j4 < kStateRegs / 4; ++j4) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live && 4 * j4 < cpt) v = __ldg(reinterpret_cast<const float4*>(sp.states + row * C + c0) + j4);
+      sv[4 * j4] = v.x;
+      sv[4 * j4 + 1] = v.y;
+      sv[4 * j4 + 2] = v.z;
+      sv[4 * j4 + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kStateRegs; ++j) {
+      const int ch = c0 + j;
+      sv[j] = (live && ch < cend) ? __ldg(sp.states + row * C + ch) : 0.0f;
+    }
+  }
+  float liveness = 0.0f, sd = 0.0f;
+  if (sp.gates3d && live) {
+    liveness = __ldg(sp.states + row * C + 3);
+    sd = __ldg(sp.states + row * C + 7);
+  }
+  mlp_layer2_any(s, b2, hid, w2s, outs);
+  __syncthreads();
+  after_layer2();
+  // forward_from_features_with_eps + gates + euler_step, TPR threads per row
+  if (live) {
+    const float* u = outs + r * s.out_stride;
+    float norm = 0.0f;
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+      if (a < D) norm = norm + u[a] * u[a];
+    norm = sqrtf(norm);
+    float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+      if (a < D) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
+    float state_gate = 1.0f;
+    if (sp.gates3d) {
+      // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
+      state_gate = clamp_rs((4.0f - liveness) * 2.0f, 0.0f, 1.0f);
+      float motion_gate = 0.0f;
+      if (!(pi.w >= 0.5f)) motion_gate = state_gate * clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) dx[a] = dx[a] * motion_gate;
+    }
+    if (part == 0) {
+      next_pos[row] = euler_position(g, ep, pi, dx, m);
+      if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
+    }
+    float nsv[kStateRegs], dsa[kStateRegs];
+#pragma unroll
+    for (int j = 0; j < kStateRegs; ++j) {
+      const int ch = c0 + j;
+      nsv[j] = 0.0f;
+      dsa[j] = 0.0f;
+      if (ch < cend) {
+        float dsv = u[D + ch];
+        if (sp.gates3d) dsv = dsv * state_gate;
+        nsv[j] = euler_state(ep, C, ch, sv[j], dsv, m);
+        dsa[j] = dsv;
+      }
+    }
+    if (vec) {
+#pragma unroll
+      for (int j4 = 0; j4 < kStateRegs / 4; ++j4)
+        if (4 * j4 < cpt) {
+          reinterpret_cast<float4*>(next_states + row * C + c0)[j4] =
+              make_float4(nsv[4 * j4], nsv[4 * j4 + 1], nsv[4 * j4 + 2], nsv[4 * j4 + 3]);
+          if (ds_out)
+            reinterpret_cast<float4*>(ds_out + row * C + c0)[j4] =
+                make_float4(dsa[4 * j4], dsa[4 * j4 + 1], dsa[4 * j4 + 2], dsa[4 * j4 + 3]);
+        }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kStateRegs; ++j) {
+        const int ch = c0 + j;
+        if (ch < cend) {
+          next_states[row * C + ch] = nsv[j];
+          if (ds_out) ds_out[row * C + ch] = dsa[j];
+        }
+      }
+    }
+    for (int ch = c0 + kStateRegs; ch < cend; ++ch) {
+      float dsv = u[D + ch];
+      if (sp.gates3d) dsv = dsv * state_gate;
+      next_states[row * C + ch] = euler_state(ep, C, ch, __ldg(sp.states + row * C + ch), dsv, m);
+      if (ds_out) ds_out[row * C + ch] = dsv;
+    }
+  }
+}
+
 // The rollout step's MLP stage over feature tiles in sorted order.
 template <int HG, int NT>
 __global__ void __launch_bounds__(NT, 1)
@@ -481,8 +630,6 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   float* w2s = smem + L.w2;
   float* outs = smem + L.outs;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
-  constexpr int TPR = HG / 8;  // layer-2 / epilogue threads per row (NT / M)
-  const int C = sp.C, D = sp.D;
   const uint32_t tiles = tile_end;
   const uint32_t tile_bytes = uint32_t(s.F) * uint32_t(s.M) * 4u;  // a multiple of 16
   auto issue = [&](uint32_t t) {
@@ -496,17 +643,7 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   load_weights(s, w1t, w2, w1s, w2s);
   float bias1[kTH];
   load_bias1<HG>(s, b1, bias1);
-  const int r = threadIdx.x / TPR;
-  const int part = threadIdx.x - r * TPR;
   const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
-  // Each of a row's TPR threads owns a contiguous run of cpt channels, read
-  // and written as float4 when the rows are 16-byte aligned.
-  const int cpt = (C + TPR - 1) / TPR;
-  const int c0 = part * cpt;
-  const int cend = min(C, c0 + cpt);
-  const bool vec = (C % 4 == 0) && (cpt % 4 == 0) && cpt <= kStateRegs &&
-                   ((reinterpret_cast<uintptr_t>(sp.states) | reinterpret_cast<uintptr_t>(next_states) |
-                     reinterpret_cast<uintptr_t>(ds_out)) & 15u) == 0;
   for (; tile < tiles; tile += gridDim.x) {
     const bool arrived = mbar_wait(bar, phase);
     if (__syncthreads_or(!arrived)) {
@@ -520,120 +657,78 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
       return;
     }
     phase ^= 1u;
-    // The epilogue's position / mask reads are issued before layer 1 so
-    // their latency is hidden behind it.
-    const uint32_t q = tile * s.M + r;
-    const bool live = q < total;
-    size_t row = 0;
-    float4 pi = make_float4(0.f, 0.f, 0.f, 0.f);
-    float m = 1.0f;
-    if (live) {
+    mlp_tile<HG, NT, false>(s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
+                            next_states, dx_out, ds_out, features_out, step_index, ft, w1s, hid,
+                            w2s, outs, [&] {
+                              const uint32_t next = tile + gridDim.x;
+                              if (next < tiles) issue(next);
+                            });
+  }
+}
+
+// The fused step: perception and the MLP stage in one kernel, the feature
+// tile never leaving shared memory.  Each block loops over tiles of M sorted
+// slots: its threads first compute the tile's feature rows (one thread per
+// slot and CH-channel chunk, the perception kernels' per-particle code) into
+// ft [F][M], then run mlp_tile on them.  hid overlays ft, which keeps a block
+// under half of the SM's shared memory: two blocks per SM, so one block's
+// neighbour gathers overlap the other's FP32 work.
+constexpr int kFusedThreads = 192;
+
+template <int HG, int DIM, int CH, int OPT>
+__global__ void __launch_bounds__(kFusedThreads, 2)
+fused_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, HitLists hl,
+                  const float* __restrict__ volume, int chunks, uint32_t total,
+                  uint32_t tile_begin, uint32_t tile_end, const float* __restrict__ w1t,
+                  const float* __restrict__ b1, const float* __restrict__ w2,
+                  const float* __restrict__ b2, StepParams sp, EulerParams ep,
+                  const float* __restrict__ mask, float4* __restrict__ next_pos,
+                  float* __restrict__ next_states, float4* __restrict__ dx_out,
+                  float* __restrict__ ds_out, float* __restrict__ features_out) {
+  constexpr int NT = kFusedThreads;
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const SmemLayout L = smem_layout(s);
+  float* ft = smem + L.ft0;
+  float* hid = smem + L.hid;
+  float* w1s = smem + L.w1;
+  float* w2s = smem + L.w2;
+  float* outs = smem + L.outs;
+  load_weights(s, w1t, w2, w1s, w2s);
+  float bias1[kTH];
+  load_bias1<HG>(s, b1, bias1);
+  const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
+  const int C = sp.C;
+  const int items = s.M * chunks;
+  for (uint32_t tile = tile_begin + blockIdx.x; tile < tile_end; tile += gridDim.x) {
+    for (int t = threadIdx.x; t < items; t += NT) {
+      const int rr = t / chunks;
+      const int chunk = t - rr * chunks;
+      const int c0 = chunk * CH;
+      const uint32_t q = tile * s.M + rr;
+      float* col = ft + rr;
+      if (q >= total) {
+        for (int k = chunk; k < s.F; k += chunks) col[k * s.M] = 0.0f;
+        continue;
+      }
       const uint32_t batch = q / sg.n;
-      const uint32_t local = __ldg(sg.permutation + q);
-      row = size_t(batch) * sg.n + local;
-      pi = __ldg(sg.positions + row);
-      if (sp.lane_seeds)
-        m = stochastic_update_mask(sp.update_prob, local, step_index, __ldg(sp.lane_seeds + batch));
-      else if (mask)
-        m = __ldg(mask + row);
+      const size_t row = size_t(batch) * sg.n + sg.permutation[q];
+      const float4 pi = __ldg(sg.positions + row);
+      const int3 c = slot_cell<DIM>(sg, q);
+      float si[CH];
+      load_row<CH>(sp.states, row, C, c0, false, si);
+      PerceptionAcc<DIM, CH> a;
+      perceive_chunk<DIM, CH, OPT>(g, pp, sg, hl, batch, q, pi, c, sp.states, C, c0, volume, si,
+                                   a);
+      emit_features<DIM, CH>(pp, C, c0, chunk == 0, si, a, pi,
+                             [&](int k, float v) { col[k * s.M] = v; });
     }
-    mlp_layer1<HG, NT>(s, w1t, bias1, ft, w1s, hid);
-    if (features_out && live)
-      for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
     __syncthreads();
-    // own state for the Euler update, hidden behind layer 2
-    float sv[kStateRegs];
-    if (vec) {
-#pragma unroll
-      for (int j4 = 0; j4 < kStateRegs / 4; ++j4) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (live && 4 * j4 < cpt) v = __ldg(reinterpret_cast<const float4*>(sp.states + row * C + c0) + j4);
-        sv[4 * j4] = v.x;
-        sv[4 * j4 + 1] = v.y;
-        sv[4 * j4 + 2] = v.z;
-        sv[4 * j4 + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kStateRegs; ++j) {
-        const int ch = c0 + j;
-        sv[j] = (live && ch < cend) ? __ldg(sp.states + row * C + ch) : 0.0f;
-      }
-    }
-    float liveness = 0.0f, sd = 0.0f;
-    if (sp.gates3d && live) {
-      liveness = __ldg(sp.states + row * C + 3);
-      sd = __ldg(sp.states + row * C + 7);
-    }
-    mlp_layer2_any(s, b2, hid, w2s, outs);
-    __syncthreads();
-    const uint32_t next = tile + gridDim.x;
-    if (next < tiles) issue(next);
-    // forward_from_features_with_eps + gates + euler_step, TPR threads per row
-    if (live) {
-      const float* u = outs + r * s.out_stride;
-      float norm = 0.0f;
-#pragma unroll
-      for (int a = 0; a < 3; ++a)
-        if (a < D) norm = norm + u[a] * u[a];
-      norm = sqrtf(norm);
-      float dx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int a = 0; a < 3; ++a)
-        if (a < D) dx[a] = sp.alpha * u[a] * sp.motion_eps / (1.0f + norm);
-      float state_gate = 1.0f;
-      if (sp.gates3d) {
-        // position_conditioned_3d_{maturity,motion}_gate (rollout/mod.rs:67-90)
-        state_gate = clamp_rs((4.0f - liveness) * 2.0f, 0.0f, 1.0f);
-        float motion_gate = 0.0f;
-        if (!(pi.w >= 0.5f)) motion_gate = state_gate * clamp_rs((fabsf(sd) - 0.01f) / 0.02f, 0.0f, 1.0f);
-#pragma unroll
-        for (int a = 0; a < 4; ++a) dx[a] = dx[a] * motion_gate;
-      }
-      if (part == 0) {
-        next_pos[row] = euler_position(g, ep, pi, dx, m);
-        if (dx_out) dx_out[row] = make_float4(dx[0], dx[1], dx[2], dx[3]);
-      }
-      float nsv[kStateRegs], dsa[kStateRegs];
-#pragma unroll
-      for (int j = 0; j < kStateRegs; ++j) {
-        const int ch = c0 + j;
-        nsv[j] = 0.0f;
-        dsa[j] = 0.0f;
-        if (ch < cend) {
-          float dsv = u[D + ch];
-          if (sp.gates3d) dsv = dsv * state_gate;
-          nsv[j] = euler_state(ep, C, ch, sv[j], dsv, m);
-          dsa[j] = dsv;
-        }
-      }
-      if (vec) {
-#pragma unroll
-        for (int j4 = 0; j4 < kStateRegs / 4; ++j4)
-          if (4 * j4 < cpt) {
-            reinterpret_cast<float4*>(next_states + row * C + c0)[j4] =
-                make_float4(nsv[4 * j4], nsv[4 * j4 + 1], nsv[4 * j4 + 2], nsv[4 * j4 + 3]);
-            if (ds_out)
-              reinterpret_cast<float4*>(ds_out + row * C + c0)[j4] =
-                  make_float4(dsa[4 * j4], dsa[4 * j4 + 1], dsa[4 * j4 + 2], dsa[4 * j4 + 3]);
-          }
-      } else {
-#pragma unroll
-        for (int j = 0; j < kStateRegs; ++j) {
-          const int ch = c0 + j;
-          if (ch < cend) {
-            next_states[row * C + ch] = nsv[j];
-            if (ds_out) ds_out[row * C + ch] = dsa[j];
-          }
-        }
-      }
-      for (int ch = c0 + kStateRegs; ch < cend; ++ch) {
-        float dsv = u[D + ch];
-        if (sp.gates3d) dsv = dsv * state_gate;
-        next_states[row * C + ch] = euler_state(ep, C, ch, __ldg(sp.states + row * C + ch), dsv, m);
-        if (ds_out) ds_out[row * C + ch] = dsv;
-      }
-    }
+    // mlp_tile synchronises after layer 2, so the next tile's feature rows
+    // (which overwrite hid) wait for it.
+    mlp_tile<HG, NT, true>(s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
+                           next_states, dx_out, ds_out, features_out, step_index, ft, w1s, hid,
+                           w2s, outs, [] {});
   }
 }
 
@@ -650,6 +745,7 @@ MlpShape shape_with(const DeviceModel& m, int nt) {
   s.hid_stride = s.Hp + 4;
   s.w2_stride = s.Hp + 4;
   s.out_stride = s.O + 1;
+  s.alias = 0;
   s.w1_resident = 1;
   if (smem_layout(s).total * sizeof(float) > kSmemBudget) s.w1_resident = 0;
   // Layer-2 output slots per row: R tpr ceil(O / (R tpr)).  Triples when M
@@ -676,6 +772,18 @@ MlpShape make_shape(const DeviceModel& m, uint64_t rows) {
   const double t_wide = double(waves(wide)) * wide.M;
   const double t_narrow = double(waves(narrow)) * narrow.M * 1.05;
   return t_wide <= t_narrow ? wide : narrow;
+}
+
+// The fused kernel's shape: 192 threads, hid over ft, at most half of an
+// SM's shared memory per block (w1 streamed when its resident copy does not
+// fit).
+constexpr size_t kFusedSmemBudget = 112 * 1024;
+MlpShape fused_shape(const DeviceModel& m) {
+  MlpShape s = shape_with(m, kFusedThreads);
+  s.alias = 1;
+  s.w1_resident = 1;
+  if (smem_layout(s).total * sizeof(float) > kFusedSmemBudget) s.w1_resident = 0;
+  return s;
 }
 
 struct LaunchCfg {
@@ -835,6 +943,23 @@ uint64_t bulk_copy_timeouts() {
   return v;
 }
 
+namespace {
+StepParams step_params(const DeviceModel& m, const GridParams& g, const float* states,
+                       const StochasticMask& sm) {
+  StepParams sp;
+  sp.states = states;
+  sp.update_prob = sm.update_prob;
+  sp.lane_seeds = sm.lane_seeds;
+  sp.step_counter = sm.step_counter;
+  sp.alpha = m.alpha;
+  sp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
+  sp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;
+  sp.C = m.state_dims;
+  sp.D = g.dim;
+  return sp;
+}
+}  // namespace
+
 npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const SortedGrid& sgrid,
                            uint32_t batch, const float* tiles, const float* states, float dt,
                            const float* mask, const StochasticMask& sm,
@@ -848,17 +973,8 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
   if (reinterpret_cast<uintptr_t>(tiles) & 15u)
     return fail(NPA_ERR_INVALID_ARGUMENT, "step workspace must be 16-byte aligned");
   const MlpShape s = make_shape(m, total);
-  StepParams sp;
-  sp.states = states;
-  sp.update_prob = sm.update_prob;
-  sp.lane_seeds = sm.lane_seeds;
-  sp.step_counter = sm.step_counter;
-  sp.alpha = m.alpha;
-  sp.motion_eps = m.equivariance == NPA_EQUIV_PARTICLE_DENSITY_AND_SCALE ? g.eps : m.eps0;
-  sp.gates3d = (g.dim == 3 && m.position_features && m.state_dims > 3) ? 1 : 0;
-  sp.C = m.state_dims;
-  sp.D = g.dim;
-  EulerParams e{dt, g.dim == 3 ? 4 : 2, (g.dim == 3 && m.state_dims > 3) ? 1 : 0};
+  const StepParams sp = step_params(m, g, states, sm);
+  const EulerParams e{dt, g.dim == 3 ? 4 : 2, (g.dim == 3 && m.state_dims > 3) ? 1 : 0};
   const uint32_t ntiles_all = static_cast<uint32_t>((uint64_t(total) + s.M - 1) / s.M);
   tile_end = std::min(tile_end, ntiles_all);
   if (tile_end <= tile_begin) return NPA_OK;
@@ -882,6 +998,53 @@ npa_status launch_mlp_step(const DeviceModel& m, const GridParams& g, const Sort
 #undef NPA_MLP_NT
 #undef NPA_MLP
   return after_launch("mlp_step_kernel");
+}
+
+bool fused_step_supported(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                          uint32_t batch, uint32_t total) {
+  if (g.dim != 2 || m.state_dims <= 4 || !mlp_step_supported(m)) return false;
+  if (m.hidden_padded != 64 && m.hidden_padded != 128) return false;
+  if (p.feature_dims != m.feature_dims) return false;
+  // the dense-cell (warp-cooperative) walk is not part of the fused kernel
+  if (uint64_t(total) >= uint64_t(8) * batch * g.cells) return false;
+  const MlpShape s = fused_shape(m);
+  return (m.update_dims + s.tpr - 1) / s.tpr <= kMaxOut &&
+         smem_layout(s).total * sizeof(float) <= kFusedSmemBudget;
+}
+
+npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                             const SortedGrid& sgrid, const HitLists& hl, uint32_t batch,
+                             const float* states, const float* volume_sorted, float dt,
+                             const float* mask, const StochasticMask& sm, const StepOutputs& out,
+                             cudaStream_t stream) {
+  const uint32_t total = batch * sgrid.n;
+  if (total == 0) return NPA_OK;
+  if (!fused_step_supported(m, g, p, batch, total))
+    return fail(NPA_ERR_UNSUPPORTED, "fused step outside the supported range");
+  PerceptionParams pp = p;
+  pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+  if (p.log_norm_grad || p.log_norm_density_grad) NPA_TRY(device_log1p_table(&pp.l1p, stream));
+  const MlpShape s = fused_shape(m);
+  const StepParams sp = step_params(m, g, states, sm);
+  const EulerParams e{dt, 2, 0};
+  const int chunks = (m.state_dims + 7) / 8;
+  const uint32_t ntiles = static_cast<uint32_t>((uint64_t(total) + s.M - 1) / s.M);
+  const bool fixed_opts = p.state_grad && !p.density_grad && p.hybrid;
+  LaunchCfg lc;
+#define NPA_FUSED(HGV, OPTV)                                                                    \
+  do {                                                                                          \
+    NPA_TRY(plan(fused_step_kernel<HGV, 2, 8, OPTV>, s, ntiles, &lc));                          \
+    fused_step_kernel<HGV, 2, 8, OPTV><<<lc.grid, kFusedThreads, lc.smem, stream>>>(             \
+        s, g, pp, sgrid, hl, volume_sorted, chunks, total, 0, ntiles, m.w1t, m.b1, m.w2, m.b2,   \
+        sp, e, mask, out.next_positions, out.next_states, out.dx, out.ds, out.features);         \
+  } while (0)
+  if (s.Hp == 64) {
+    if (fixed_opts) NPA_FUSED(64 / kTH, 1); else NPA_FUSED(64 / kTH, 0);
+  } else {
+    if (fixed_opts) NPA_FUSED(128 / kTH, 1); else NPA_FUSED(128 / kTH, 0);
+  }
+#undef NPA_FUSED
+  return after_launch("fused_step_kernel");
 }
 
 }  // namespace npa

@@ -332,6 +332,12 @@ class CudaAutomataExecutor:
                                                         ctypes.byref(s)), "state_device")
         return p.value, s.value
 
+    def set_fused_step(self, fused: bool = True) -> None:
+        """Run perception, the MLP and the Euler step as one kernel per step
+        (feature rows kept in shared memory) instead of two; same results."""
+        _lib.check(_lib.lib().npa_executor_set_fused_step(self._handle, int(bool(fused))),
+                   "set_fused_step")
+
     def launches_per_step(self) -> int:
         v = ctypes.c_int64(0)
         _lib.check(_lib.lib().npa_executor_launches_per_step(self._handle, ctypes.byref(v)),

@@ -572,6 +572,15 @@ npa_status npa_executor_state_device(npa_executor* exec, float** d_positions, fl
 /* Kernels launched per rollout step by this executor. */
 npa_status npa_executor_launches_per_step(npa_executor* exec, int64_t* launches);
 
+/* Selects the executor's step kernels: fused = 1 runs perception, the MLP
+ * and the Euler step as one kernel after the density pass (the feature rows
+ * stay in shared memory, the role of the reference's single update pass,
+ * crates/burn_automata/src/gpu_step.wgsl:3656-4484); fused = 0 (the default)
+ * runs perception into feature tiles and the MLP stage as two kernels.  Both
+ * give identical results.  NPA_ERR_UNSUPPORTED outside the fused kernel's
+ * range (2D, C > 4, hidden width <= 128, sparse cells). */
+npa_status npa_executor_set_fused_step(npa_executor* exec, int32_t fused);
+
 #ifdef __cplusplus
 }
 #endif
