@@ -533,12 +533,25 @@ def run_ours(args, rank, world, local_rank):
         phase_ms, total_ms = runner.run_profiled(d_pos, d_st, args.steps, stream=sptr)
         dominant = phase_ms[:, 2]
     else:
-        phase_ms, total_ms = ex.step_state_many_profiled(args.steps, w.dt, use_graph=True,
-                                                         stream=sptr)
-        dominant = phase_ms[:, 3]
+        # the step as a user replays it: whole-step graphs, no events inside
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        ex.step_state_many(args.steps, w.dt, use_graph=True, stream=sptr)
+        ev1.record(stream)
+        ev1.synchronize()
+        total_ms = ev0.elapsed_time(ev1)
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
     launches = lib.npa_kernel_launch_count() - launches0
+    extra_steps = 0
+    if not perception_only:
+        # per-phase times from a separate run with events between the phases
+        # (after the timed region: the events add a few microseconds per phase)
+        extra_steps = min(args.steps, 50)
+        phase_ms, _ = ex.step_state_many_profiled(extra_steps, w.dt, use_graph=True,
+                                                  stream=sptr)
+        dominant = phase_ms[:, 3]
     if world > 1:
         dist.barrier()
     max_ms, dom_ms = multigpu.max_over_ranks([total_ms, float(dominant.mean())], dev)
@@ -562,7 +575,7 @@ def run_ours(args, rank, world, local_rank):
     plans = multigpu.gather_objects((first, per_rank))
     validation = None
     if rank == 0:
-        steps_done = args.warmup + args.steps
+        steps_done = args.warmup + args.steps + extra_steps
         validation = validate_against_one_gpu(args, world, local_rank, plans, gathered,
                                               steps_done, sptr)
 

@@ -1294,6 +1294,11 @@ struct npa_executor {
   size_t ws_bytes = 0;
   PerceiveWorkspace w{};
   cudaGraphExec_t graph[2][kPhases] = {};
+  // Whole steps for the unprofiled replay: step_graph[p] is one step from
+  // ping-pong parity p, pair_graph[p] two steps (back to parity p); one graph
+  // launch instead of one per phase.
+  cudaGraphExec_t step_graph[2] = {};
+  cudaGraphExec_t pair_graph[2] = {};
   float graph_dt = 0.0f;
   cudaStream_t graph_stream = nullptr;
   int64_t launches[kPhases] = {0, 0, 0, 0};
@@ -1351,11 +1356,37 @@ npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cu
 }
 
 void exec_drop_graphs(npa_executor* e) {
+  auto drop = [](cudaGraphExec_t& g) {
+    if (g) cudaGraphExecDestroy(g);
+    g = nullptr;
+  };
   for (auto& row : e->graph)
-    for (auto& g : row) {
-      if (g) cudaGraphExecDestroy(g);
-      g = nullptr;
-    }
+    for (auto& g : row) drop(g);
+  for (auto& g : e->step_graph) drop(g);
+  for (auto& g : e->pair_graph) drop(g);
+}
+
+// Captures the phases of `steps` consecutive steps from parity `from` into one
+// executable graph.
+npa_status exec_capture_steps(npa_executor* e, int from, int steps, float dt, cudaStream_t stream,
+                              cudaGraphExec_t* out) {
+  cudaGraph_t graph = nullptr;
+  NPA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal),
+           "cudaStreamBeginCapture");
+  npa_status st = NPA_OK;
+  for (int k = 0; k < steps && st == NPA_OK; ++k)
+    for (int phase = 0; phase < kPhases && st == NPA_OK; ++phase)
+      st = exec_enqueue_phase(e, (from + k) & 1, phase, dt, stream);
+  cudaError_t ce = cudaStreamEndCapture(stream, &graph);
+  if (st != NPA_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return st;
+  }
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+  ce = cudaGraphInstantiate(out, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+  return NPA_OK;
 }
 
 npa_status exec_capture(npa_executor* e, float dt, cudaStream_t stream) {
@@ -1378,6 +1409,10 @@ npa_status exec_capture(npa_executor* e, float dt, cudaStream_t stream) {
       cudaGraphDestroy(graph);
       if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
     }
+  }
+  for (int from = 0; from < 2; ++from) {
+    NPA_TRY(exec_capture_steps(e, from, 1, dt, stream, &e->step_graph[from]));
+    NPA_TRY(exec_capture_steps(e, from, 2, dt, stream, &e->pair_graph[from]));
   }
   e->graph_dt = dt;
   e->graph_stream = stream;
@@ -1507,7 +1542,24 @@ npa_status npa_executor_step_many(npa_executor* e, int64_t steps, float dt, int3
                                   void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   NPA_TRY(exec_prepare(e, steps, dt, use_graph, s));
-  for (int64_t k = 0; k < steps; ++k) {
+  const int64_t per_step = e->launches[0] + e->launches[1] + e->launches[2] + e->launches[3];
+  int64_t k = 0;
+  if (use_graph) {
+    for (; k + 2 <= steps; k += 2) {
+      NPA_CUDA(cudaGraphLaunch(e->pair_graph[e->cur], s), "cudaGraphLaunch");
+      g_launches.fetch_add(uint64_t(2 * per_step), std::memory_order_relaxed);
+      e->step_index += 2u;
+    }
+    if (k < steps) {
+      NPA_CUDA(cudaGraphLaunch(e->step_graph[e->cur], s), "cudaGraphLaunch");
+      g_launches.fetch_add(uint64_t(per_step), std::memory_order_relaxed);
+      e->cur = 1 - e->cur;
+      e->step_index += 1u;
+      ++k;
+    }
+    return NPA_OK;
+  }
+  for (; k < steps; ++k) {
     for (int phase = 0; phase < kPhases; ++phase) NPA_TRY(exec_run_phase(e, phase, dt, use_graph, s));
     e->cur = 1 - e->cur;
     e->step_index += 1u;
