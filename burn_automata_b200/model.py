@@ -276,6 +276,7 @@ class CudaAutomataExecutor:
         when random01(i, step_index, lane seed) < update_prob; lane seeds are
         fold(seed) ^ (l * particle_count), or fold(lane_seeds[l]) when given."""
         ls = None
+        arr = None
         if lane_seeds is not None:
             arr = np.ascontiguousarray(np.asarray(lane_seeds, dtype=np.uint64))
             if arr.size != self.batch_size:
@@ -285,6 +286,35 @@ class CudaAutomataExecutor:
         _lib.check(_lib.lib().npa_executor_set_update_prob(
             self._handle, float(update_prob), int(seed) & 0xFFFFFFFFFFFFFFFF, ls),
             "set_update_prob")
+        self._mask = (float(update_prob), int(seed) & 0xFFFFFFFFFFFFFFFF,
+                      None if arr is None else arr.copy())
+
+    def save_checkpoint(self, path: str) -> None:
+        """Writes the resident particles, the step index and the mask settings
+        (checkpoint.py); load_checkpoint on an executor of the same shape
+        continues the rollout bit for bit."""
+        from . import checkpoint
+
+        pos, st = self.read_state()
+        prob, seed, lanes = getattr(self, "_mask", (1.0, 0, None))
+        checkpoint.save(path, checkpoint.Checkpoint(
+            pos, st, self.batch_size, self.particle_count, self.model.config.state_dims,
+            self.step_index, prob, seed, lanes))
+
+    def load_checkpoint(self, path: str) -> None:
+        """Restores a checkpoint written by save_checkpoint (same batch, particle
+        count and channel count)."""
+        from . import checkpoint
+
+        ck = checkpoint.load(path)
+        if (ck.batch_size, ck.particle_count, ck.state_dims) != (
+                self.batch_size, self.particle_count, self.model.config.state_dims):
+            raise InvalidArgument(
+                f"checkpoint of {ck.batch_size} x {ck.particle_count} particles with "
+                f"{ck.state_dims} channels does not fit this executor ({self.batch_size} x "
+                f"{self.particle_count}, {self.model.config.state_dims})")
+        self.create_state(ck.positions, ck.states, ck.update_prob, ck.seed, ck.lane_seeds)
+        self.set_step_index(ck.step_index)
 
     @property
     def step_index(self) -> int:
