@@ -504,6 +504,7 @@ def run_ours(args, rank, world, local_rank):
     sptr = stream.cuda_stream
     perception_only = spec["kind"] == "perception"
 
+    step_groups = None
     if perception_only:
         runner = ba.DevicePerception(w.grid, w.options, w.batch, w.n, w.state_dims, local_rank)
         d_pos = torch.from_numpy(w.positions).to(dev)
@@ -518,6 +519,9 @@ def run_ours(args, rank, world, local_rank):
         ex.create_state(w.positions, w.states)
         if args.fused:
             ex.set_fused_step(True)
+        if args.groups:
+            ex.set_step_groups(args.groups)
+        step_groups = ex.step_groups
         ex.step_state_many(args.warmup, w.dt, use_graph=True, stream=sptr)
         features = w.model.perception_dims()
     torch.cuda.synchronize()
@@ -652,6 +656,7 @@ def run_ours(args, rank, world, local_rank):
                        "parallelism": parallelism,
                        "step_kernels": ("fused perception + MLP + Euler" if args.fused
                                         else "perception tiles, then MLP + Euler"),
+                       "step_groups": step_groups,
                        "l2": ("no flush: per-step working set exceeds the 126 MB L2"
                               if particles_rank >= (1 << 20) else
                               "no flush: the shard's per-step working set is below the 126 MB "
@@ -727,6 +732,9 @@ def main():
     ap.add_argument("--fused", action="store_true",
                     help="executor step as one perception + MLP + Euler kernel after the density "
                          "pass (2D, sparse cells)")
+    ap.add_argument("--groups", type=int, default=None,
+                    help="replay the shard's rollouts as this many independent chains (1-4; "
+                         "default: the executor's choice)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

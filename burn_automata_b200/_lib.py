@@ -160,6 +160,8 @@ SIGNATURES = [
     ("npa_executor_state_device", c_i32, [vp, P(vp), P(vp)]),
     ("npa_executor_launches_per_step", c_i32, [vp, P(c_i64)]),
     ("npa_executor_set_fused_step", c_i32, [vp, c_i32]),
+    ("npa_executor_set_step_groups", c_i32, [vp, c_i32]),
+    ("npa_executor_step_groups", c_i32, [vp, P(c_i32)]),
 ]
 
 # Symbols exported beyond the public header (test hooks).

@@ -1280,6 +1280,8 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
 // tiles, (3) MLP + dx/ds + Euler.  Replaying the phases as separate graphs
 // lets a caller bracket each kernel with CUDA events on the launching stream.
 constexpr int kPhases = 4;
+constexpr int kMaxStepGroups = 4;
+constexpr size_t kGroupedMaxParticles = size_t(1) << 18;  // default grouping up to this batch size
 
 struct npa_executor {
   npa_model* model = nullptr;
@@ -1313,46 +1315,87 @@ struct npa_executor {
   // Fused step: phase 2 is empty and phase 3 runs perception + MLP + Euler in
   // one kernel (npa_executor_set_fused_step).
   int fused = 0;
+  // Rollout groups of the whole-step replay (npa_executor_set_step_groups):
+  // the batch split into `groups` runs of consecutive rollouts, each with its
+  // own workspace, step counter and capture stream, whose steps form
+  // independent chains in the step graphs (rollouts never interact), so one
+  // group's latency-bound phases overlap another's.
+  int groups = 1;
+  struct Group {
+    int64_t first = 0, batch = 0;
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    PerceiveWorkspace w{};
+    int tile_rows = 0;
+    uint32_t* d_step = nullptr;
+    cudaStream_t side = nullptr;
+    cudaEvent_t joined = nullptr;
+  };
+  Group grp[kMaxStepGroups];
+  cudaEvent_t fork = nullptr;
+  int64_t step_launches[2] = {0, 0}, pair_launches[2] = {0, 0};
 };
 
 namespace {
 
-npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cudaStream_t s) {
-  const uint32_t B = uint32_t(e->batch), N = uint32_t(e->n);
-  const SortedGrid sv = sorted_view(e->w, N, B, e->pos[from]);
+// The rollouts [first, first + batch) of the executor with their own
+// workspace and step counter: a whole-batch view, or one rollout group.
+struct ExecView {
+  int64_t first, batch;
+  const PerceiveWorkspace* w;
+  int tile_rows;
+  uint32_t* d_step;
+};
+
+ExecView whole_view(const npa_executor* e) {
+  return ExecView{0, e->batch, &e->w, e->tile_rows, e->d_step};
+}
+
+npa_status exec_enqueue_view_phase(npa_executor* e, const ExecView& v, int from, int phase,
+                                   float dt, cudaStream_t s) {
+  const uint32_t B = uint32_t(v.batch), N = uint32_t(e->n);
+  const int C = e->model->dm.state_dims;
+  const size_t row0 = size_t(v.first) * N;
+  float* pos = e->pos[from] + row0 * 4;
+  float* st = e->st[from] + row0 * C;
+  const SortedGrid sv = sorted_view(*v.w, N, B, pos);
   switch (phase) {
     case 0:
-      return launch_hashgrid(e->g, reinterpret_cast<const float4*>(e->pos[from]), B, N, e->w.hg,
-                             e->w.sort_scratch, e->w.sort_scratch_bytes, s);
+      return launch_hashgrid(e->g, reinterpret_cast<const float4*>(pos), B, N, v.w->hg,
+                             v.w->sort_scratch, v.w->sort_scratch_bytes, s);
     case 1:
-      return launch_density(e->g, sv, B, e->w.volume, nullptr, e->w.hits, s);
+      return launch_density(e->g, sv, B, v.w->volume, nullptr, v.w->hits, s);
     case 2:
       if (e->fused) return NPA_OK;
-      return launch_perception_tiles(e->g, e->p, sv, e->w.hits, B, e->st[from], e->model->dm.state_dims,
-                                     e->w.volume, e->tile_rows, e->w.tiles, s);
+      return launch_perception_tiles(e->g, e->p, sv, v.w->hits, B, st, C, v.w->volume,
+                                     v.tile_rows, v.w->tiles, s);
     default: {
       StepOutputs out;
-      out.next_positions = reinterpret_cast<float4*>(e->pos[1 - from]);
-      out.next_states = e->st[1 - from];
+      out.next_positions = reinterpret_cast<float4*>(e->pos[1 - from] + row0 * 4);
+      out.next_states = e->st[1 - from] + row0 * C;
       out.dx = nullptr;
       out.ds = nullptr;
       out.features = nullptr;
       StochasticMask sm;
       if (e->stochastic) {
         sm.update_prob = e->update_prob;
-        sm.lane_seeds = e->d_lane_seeds;
-        sm.step_counter = e->d_step;
+        sm.lane_seeds = e->d_lane_seeds + v.first;
+        sm.step_counter = v.d_step;
       }
       if (e->fused)
-        NPA_TRY(launch_fused_step(e->model->dm, e->g, e->p, sv, e->w.hits, B, e->st[from],
-                                  e->w.volume, dt, nullptr, sm, out, s));
+        NPA_TRY(launch_fused_step(e->model->dm, e->g, e->p, sv, v.w->hits, B, st, v.w->volume,
+                                  dt, nullptr, sm, out, s));
       else
-        NPA_TRY(launch_mlp_step(e->model->dm, e->g, sv, B, e->w.tiles, e->st[from], dt, nullptr,
-                                sm, out, s));
-      if (e->stochastic) NPA_TRY(launch_advance_step(e->d_step, s));
+        NPA_TRY(launch_mlp_step(e->model->dm, e->g, sv, B, v.w->tiles, st, dt, nullptr, sm,
+                                out, s));
+      if (e->stochastic) NPA_TRY(launch_advance_step(v.d_step, s));
       return NPA_OK;
     }
   }
+}
+
+npa_status exec_enqueue_phase(npa_executor* e, int from, int phase, float dt, cudaStream_t s) {
+  return exec_enqueue_view_phase(e, whole_view(e), from, phase, dt, s);
 }
 
 void exec_drop_graphs(npa_executor* e) {
@@ -1369,15 +1412,38 @@ void exec_drop_graphs(npa_executor* e) {
 // Captures the phases of `steps` consecutive steps from parity `from` into one
 // executable graph.
 npa_status exec_capture_steps(npa_executor* e, int from, int steps, float dt, cudaStream_t stream,
-                              cudaGraphExec_t* out) {
+                              cudaGraphExec_t* out, int64_t* launches) {
   cudaGraph_t graph = nullptr;
+  const uint64_t before = npa_kernel_launch_count();
   NPA_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal),
            "cudaStreamBeginCapture");
   npa_status st = NPA_OK;
-  for (int k = 0; k < steps && st == NPA_OK; ++k)
-    for (int phase = 0; phase < kPhases && st == NPA_OK; ++phase)
-      st = exec_enqueue_phase(e, (from + k) & 1, phase, dt, stream);
+  if (e->groups <= 1) {
+    for (int k = 0; k < steps && st == NPA_OK; ++k)
+      for (int phase = 0; phase < kPhases && st == NPA_OK; ++phase)
+        st = exec_enqueue_phase(e, (from + k) & 1, phase, dt, stream);
+  } else {
+    // fork: every group's chain starts after what precedes the graph; join:
+    // the capture stream waits for every chain
+    if (cudaEventRecord(e->fork, stream) != cudaSuccess) st = fail(NPA_ERR_CUDA, "fork record");
+    for (int gi = 0; gi < e->groups && st == NPA_OK; ++gi) {
+      npa_executor::Group& gr = e->grp[gi];
+      const ExecView v{gr.first, gr.batch, &gr.w, gr.tile_rows, gr.d_step};
+      cudaStream_t gs = gi == 0 ? stream : gr.side;
+      if (gi > 0 && cudaStreamWaitEvent(gs, e->fork, 0) != cudaSuccess)
+        st = fail(NPA_ERR_CUDA, "fork wait");
+      for (int k = 0; k < steps && st == NPA_OK; ++k)
+        for (int phase = 0; phase < kPhases && st == NPA_OK; ++phase)
+          st = exec_enqueue_view_phase(e, v, (from + k) & 1, phase, dt, gs);
+      if (st == NPA_OK && gi > 0) {
+        if (cudaEventRecord(gr.joined, gs) != cudaSuccess ||
+            cudaStreamWaitEvent(stream, gr.joined, 0) != cudaSuccess)
+          st = fail(NPA_ERR_CUDA, "join");
+      }
+    }
+  }
   cudaError_t ce = cudaStreamEndCapture(stream, &graph);
+  *launches = int64_t(npa_kernel_launch_count() - before);
   if (st != NPA_OK) {
     if (graph) cudaGraphDestroy(graph);
     return st;
@@ -1411,8 +1477,10 @@ npa_status exec_capture(npa_executor* e, float dt, cudaStream_t stream) {
     }
   }
   for (int from = 0; from < 2; ++from) {
-    NPA_TRY(exec_capture_steps(e, from, 1, dt, stream, &e->step_graph[from]));
-    NPA_TRY(exec_capture_steps(e, from, 2, dt, stream, &e->pair_graph[from]));
+    NPA_TRY(exec_capture_steps(e, from, 1, dt, stream, &e->step_graph[from],
+                               &e->step_launches[from]));
+    NPA_TRY(exec_capture_steps(e, from, 2, dt, stream, &e->pair_graph[from],
+                               &e->pair_launches[from]));
   }
   e->graph_dt = dt;
   e->graph_stream = stream;
@@ -1476,6 +1544,12 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
     st = fail(NPA_ERR_CUDA, "cudaMemset step counter");
   if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w, tf))
     st = fail(NPA_ERR_INVALID_ARGUMENT, "executor workspace layout");
+  // Small batches leave most SMs idle in their latency-bound phases: two
+  // rollout groups overlap them (cfg2 shards of 32 / 64 rollouts: 0.227 vs
+  // 0.243 ms and 0.419 vs 0.441 ms per step); the full 256-rollout batch
+  // fills the GPU and runs best as one chain (1.496 vs 1.536 ms).
+  if (st == NPA_OK && batch >= 2 && total <= kGroupedMaxParticles)
+    st = npa_executor_set_step_groups(e, 2);
   if (st != NPA_OK) {
     npa_executor_destroy(e);
     return st;
@@ -1484,12 +1558,26 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   return NPA_OK;
 }
 
+static void exec_free_groups(npa_executor* e) {
+  for (auto& gr : e->grp) {
+    if (gr.ws) cudaFree(gr.ws);
+    if (gr.d_step) cudaFree(gr.d_step);
+    if (gr.side) cudaStreamDestroy(gr.side);
+    if (gr.joined) cudaEventDestroy(gr.joined);
+    gr = npa_executor::Group{};
+  }
+  if (e->fork) cudaEventDestroy(e->fork);
+  e->fork = nullptr;
+  e->groups = 1;
+}
+
 void npa_executor_destroy(npa_executor* e) {
   if (!e) return;
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(e->model->dm.device);
   exec_drop_graphs(e);
+  exec_free_groups(e);
   for (int i = 0; i < 2; ++i) {
     cudaFree(e->pos[i]);
     cudaFree(e->st[i]);
@@ -1532,9 +1620,13 @@ static npa_status exec_prepare(npa_executor* e, int64_t steps, float dt, int32_t
   if (use_graph && s == nullptr) return fail(NPA_ERR_INVALID_ARGUMENT, "graph replay needs a non-default stream");
   if (use_graph && (!e->graph[0][0] || e->graph_dt != dt || e->graph_stream != s))
     NPA_TRY(exec_capture(e, dt, s));
-  if (e->stochastic && steps > 0)  // the device counter starts from the host's step index
+  if (e->stochastic && steps > 0) {  // the device counters start from the host's step index
     NPA_CUDA(cudaMemcpyAsync(e->d_step, &e->step_index, 4, cudaMemcpyHostToDevice, s),
              "upload step index");
+    for (int gi = 0; gi < e->groups && e->groups > 1; ++gi)
+      NPA_CUDA(cudaMemcpyAsync(e->grp[gi].d_step, &e->step_index, 4, cudaMemcpyHostToDevice, s),
+               "upload step index");
+  }
   return NPA_OK;
 }
 
@@ -1542,17 +1634,16 @@ npa_status npa_executor_step_many(npa_executor* e, int64_t steps, float dt, int3
                                   void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   NPA_TRY(exec_prepare(e, steps, dt, use_graph, s));
-  const int64_t per_step = e->launches[0] + e->launches[1] + e->launches[2] + e->launches[3];
   int64_t k = 0;
   if (use_graph) {
     for (; k + 2 <= steps; k += 2) {
       NPA_CUDA(cudaGraphLaunch(e->pair_graph[e->cur], s), "cudaGraphLaunch");
-      g_launches.fetch_add(uint64_t(2 * per_step), std::memory_order_relaxed);
+      g_launches.fetch_add(uint64_t(e->pair_launches[e->cur]), std::memory_order_relaxed);
       e->step_index += 2u;
     }
     if (k < steps) {
       NPA_CUDA(cudaGraphLaunch(e->step_graph[e->cur], s), "cudaGraphLaunch");
-      g_launches.fetch_add(uint64_t(per_step), std::memory_order_relaxed);
+      g_launches.fetch_add(uint64_t(e->step_launches[e->cur]), std::memory_order_relaxed);
       e->cur = 1 - e->cur;
       e->step_index += 1u;
       ++k;
@@ -1662,6 +1753,58 @@ npa_status npa_executor_state_device(npa_executor* e, float** d_positions, float
   if (!e || !d_positions || !d_states) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
   *d_positions = e->pos[e->cur];
   *d_states = e->st[e->cur];
+  return NPA_OK;
+}
+
+npa_status npa_executor_set_step_groups(npa_executor* e, int32_t groups) {
+  if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  if (groups < 1 || groups > kMaxStepGroups || (e->batch > 0 && groups > e->batch))
+    return fail(NPA_ERR_INVALID_ARGUMENT,
+                "step groups must be between 1 and min(4, batch size), got " +
+                    std::to_string(groups));
+  if (groups == e->groups) return NPA_OK;
+  NPA_TRY(ensure_device(e->model->dm.device));
+  NPA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // no replay still uses them
+  exec_drop_graphs(e);
+  exec_free_groups(e);
+  if (groups == 1) return NPA_OK;
+  const uint32_t N = uint32_t(e->n);
+  const int64_t base = e->batch / groups, extra = e->batch % groups;
+  npa_status st = NPA_OK;
+  if (cudaEventCreateWithFlags(&e->fork, cudaEventDisableTiming) != cudaSuccess)
+    st = fail(NPA_ERR_CUDA, "cudaEventCreate");
+  for (int gi = 0; gi < groups && st == NPA_OK; ++gi) {
+    npa_executor::Group& gr = e->grp[gi];
+    gr.batch = base + (gi < extra ? 1 : 0);
+    gr.first = gi * base + std::min<int64_t>(gi, extra);
+    const uint64_t rows = uint64_t(gr.batch) * N;
+    gr.tile_rows = step_tile_rows(e->model->dm, rows);
+    const size_t tf = tiles_floats(uint32_t(gr.batch), N, e->model->dm.feature_dims, gr.tile_rows);
+    gr.ws_bytes = perceive_workspace_bytes(e->g, uint32_t(gr.batch), N, tf);
+    if (cudaMalloc(&gr.ws, std::max<size_t>(gr.ws_bytes, 256)) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&gr.d_step), 4) != cudaSuccess) {
+      cudaGetLastError();
+      st = fail(NPA_ERR_OUT_OF_MEMORY, "step group workspace");
+      break;
+    }
+    if (cudaMemset(gr.d_step, 0, 4) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&gr.side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&gr.joined, cudaEventDisableTiming) != cudaSuccess)
+      st = fail(NPA_ERR_CUDA, "step group set-up");
+    else if (!carve_perceive(e->g, uint32_t(gr.batch), N, gr.ws, gr.ws_bytes, &gr.w, tf))
+      st = fail(NPA_ERR_INVALID_ARGUMENT, "step group workspace layout");
+  }
+  if (st != NPA_OK) {
+    exec_free_groups(e);
+    return st;
+  }
+  e->groups = groups;
+  return NPA_OK;
+}
+
+npa_status npa_executor_step_groups(npa_executor* e, int32_t* groups) {
+  if (!e || !groups) return fail(NPA_ERR_INVALID_ARGUMENT, "null argument");
+  *groups = e->groups;
   return NPA_OK;
 }
 

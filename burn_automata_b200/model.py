@@ -368,6 +368,19 @@ class CudaAutomataExecutor:
         _lib.check(_lib.lib().npa_executor_set_fused_step(self._handle, int(bool(fused))),
                    "set_fused_step")
 
+    def set_step_groups(self, groups: int) -> None:
+        """Replay the batch as `groups` independent chains of rollouts (1..4),
+        overlapping their latency-bound phases; same results."""
+        _lib.check(_lib.lib().npa_executor_set_step_groups(self._handle, int(groups)),
+                   "set_step_groups")
+
+    @property
+    def step_groups(self) -> int:
+        v = ctypes.c_int32(0)
+        _lib.check(_lib.lib().npa_executor_step_groups(self._handle, ctypes.byref(v)),
+                   "step_groups")
+        return v.value
+
     def launches_per_step(self) -> int:
         v = ctypes.c_int64(0)
         _lib.check(_lib.lib().npa_executor_launches_per_step(self._handle, ctypes.byref(v)),

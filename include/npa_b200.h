@@ -581,6 +581,19 @@ npa_status npa_executor_launches_per_step(npa_executor* exec, int64_t* launches)
  * range (2D, C > 4, hidden width <= 128, sparse cells). */
 npa_status npa_executor_set_fused_step(npa_executor* exec, int32_t fused);
 
+/* Splits the batch into `groups` (1..min(4, batch)) runs of consecutive
+ * rollouts for npa_executor_step_many's graph replay: each run gets its own
+ * workspace and its steps form an independent chain of the step graph, so
+ * the latency-bound phases of one run (the per-rollout sort, the neighbour
+ * walks) overlap the others' work.  Rollouts never interact, so the results
+ * are identical for every grouping.  The profiled replay
+ * (npa_executor_step_many_profiled) and use_graph = 0 step the whole batch
+ * phase by phase. */
+npa_status npa_executor_set_step_groups(npa_executor* exec, int32_t groups);
+/* The executor's rollout groups: 2 after npa_executor_create for batches of
+ * 2 or more rollouts with at most 262,144 particles in all, else 1. */
+npa_status npa_executor_step_groups(npa_executor* exec, int32_t* groups);
+
 #ifdef __cplusplus
 }
 #endif

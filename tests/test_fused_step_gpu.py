@@ -83,3 +83,52 @@ def test_fused_unsupported_outside_its_range():
         ex.set_fused_step(True)
     ex.close()
     m.close()
+
+
+def run_grouped(w, steps, groups, prob=1.0, seed=0):
+    import torch
+
+    import burn_automata_b200 as ba
+
+    m = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
+                                           w.weights.b2))
+    ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
+    ex.create_state(w.positions, w.states, update_prob=prob, seed=seed)
+    ex.set_step_groups(groups)
+    s = torch.cuda.Stream()
+    ex.step_state_many(steps, w.dt, use_graph=True, stream=s.cuda_stream)
+    ex.step_state_many(1, w.dt, use_graph=True, stream=s.cuda_stream)  # odd count: single-step graph
+    out = ex.read_state()
+    idx = ex.step_index
+    ex.close()
+    m.close()
+    return out, idx
+
+
+@pytest.mark.parametrize("groups,prob", [(2, 1.0), (3, 0.5), (4, 1.0)])
+def test_step_groups_equal_one_chain(groups, prob):
+    """Rollout groups replayed as independent graph chains give the batch's
+    results bit for bit (the stochastic mask's per-group step counters
+    included)."""
+    w = workloads.make("cfg2", batch=7, n=4096)
+    (gp, gs), gi = run_grouped(w, 6, groups, prob, 3)
+    (op, os_), oi = run_grouped(w, 6, 1, prob, 3)
+    assert gi == oi == 7
+    np.testing.assert_array_equal(gs, os_)
+    np.testing.assert_array_equal(gp, op)
+
+
+def test_step_groups_range():
+    import burn_automata_b200 as ba
+
+    w = workloads.make("cfg2", batch=2, n=512)
+    m = ba.NpaModel(w.model, ba.NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2,
+                                           w.weights.b2))
+    ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
+    for bad in (0, 3, 5):
+        with pytest.raises(Exception, match="step groups"):
+            ex.set_step_groups(bad)
+    ex.set_step_groups(2)
+    ex.set_step_groups(1)
+    ex.close()
+    m.close()
