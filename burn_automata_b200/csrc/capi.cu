@@ -354,8 +354,10 @@ size_t tiles_floats(uint32_t batch, uint32_t n, int feature_dims, int tile_rows)
   return padded * size_t(feature_dims);
 }
 
+// with_order: room for the processing order of the neighbour walks (the
+// caller passes hashgrid_orders(g, batch, n)).
 size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n,
-                                size_t extra_floats = 0) {
+                                size_t extra_floats = 0, bool with_order = false) {
   const size_t total = size_t(batch) * n;
   Carve c(nullptr, 0);
   c.take<uint32_t>(size_t(batch) * g.cells + 1);
@@ -369,11 +371,12 @@ size_t perceive_workspace_bytes(const GridParams& g, uint32_t batch, uint32_t n,
   const size_t sort = hashgrid_scratch_bytes(g, batch, n);
   c.take<char>(sort);
   c.take<float>(extra_floats);
+  if (with_order) c.take<uint32_t>(total);
   return c.used + 256;
 }
 
 bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, size_t bytes,
-                    PerceiveWorkspace* out, size_t extra_floats = 0) {
+                    PerceiveWorkspace* out, size_t extra_floats = 0, bool with_order = false) {
   const size_t total = size_t(batch) * n;
   Carve c(ws, bytes);
   out->hg.bin_offsets = c.take<uint32_t>(size_t(batch) * g.cells + 1);
@@ -389,6 +392,7 @@ bool carve_perceive(const GridParams& g, uint32_t batch, uint32_t n, void* ws, s
   out->sort_scratch_bytes = hashgrid_scratch_bytes(g, batch, n);
   out->sort_scratch = c.take<char>(out->sort_scratch_bytes);
   out->tiles = extra_floats ? c.take<float>(extra_floats) : nullptr;
+  out->hg.order = with_order ? c.take<uint32_t>(total) : nullptr;
   return c.fits();
 }
 
@@ -400,6 +404,7 @@ SortedGrid sorted_view(const PerceiveWorkspace& w, uint32_t n, uint32_t batch,
   s.srec = w.hg.srec;
   s.scyz = w.hg.scyz;
   s.positions = reinterpret_cast<const float4*>(positions);
+  s.order = w.hg.order;
   s.n = n;
   s.total = n * batch;
   return s;
@@ -645,7 +650,7 @@ npa_status npa_perceive_with_options(const npa_grid_config* cfg, const npa_perce
   float* dst;
   NPA_TRY(s.upload(&dpos, positions, total));
   NPA_TRY(s.upload(&dst, states, size_t(total) * state_dims));
-  const size_t wsb = perceive_workspace_bytes(g, B, N);
+  const size_t wsb = perceive_workspace_bytes(g, B, N, 0, hashgrid_orders(g, B, N));
   char* ws;
   NPA_TRY(s.alloc(&ws, wsb));
   float *dfeat, *ddens = nullptr, *dblur = nullptr, *dsg = nullptr, *ddg = nullptr;
@@ -1092,7 +1097,8 @@ npa_status npa_dev_perceive_workspace_size(const npa_grid_config* cfg, int64_t b
   NPA_TRY(check_bins(cfg, batch));
   if (!bytes || state_dims < 0) return fail(NPA_ERR_INVALID_ARGUMENT, "bad argument");
   const GridParams g = make_grid_params(*cfg);
-  *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n));
+  *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n), 0,
+                                    hashgrid_orders(g, uint32_t(batch), uint32_t(n)));
   return NPA_OK;
 }
 
@@ -1116,7 +1122,7 @@ npa_status perceive_phases(const npa_grid_config* cfg, const npa_perception_opti
   if (total > 0 && (!d_positions || (state_dims > 0 && !d_states) || (p.feature_dims > 0 && !d_features) || !d_workspace))
     return fail(NPA_ERR_INVALID_ARGUMENT, "null buffer");
   PerceiveWorkspace w;
-  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w))
+  if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w, 0, hashgrid_orders(g, B, N)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
   if (ev) NPA_CUDA(cudaEventRecord(ev[0], st), "cudaEventRecord");
   NPA_TRY(launch_hashgrid(g, reinterpret_cast<const float4*>(d_positions), B, N, w.hg,
@@ -1227,7 +1233,8 @@ npa_status npa_dev_step_workspace_size(npa_model* m, const npa_grid_config* grid
   const GridParams g = make_grid_params(*grid);
   *bytes = perceive_workspace_bytes(g, uint32_t(batch), uint32_t(n),
                                     tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims,
-                                                 step_tile_rows(m->dm, uint64_t(batch) * n)));
+                                                 step_tile_rows(m->dm, uint64_t(batch) * n)),
+                                    hashgrid_orders(g, uint32_t(batch), uint32_t(n)));
   return NPA_OK;
 }
 
@@ -1250,7 +1257,7 @@ npa_status npa_dev_model_step(npa_model* m, const npa_grid_config* grid, const f
   PerceiveWorkspace w;
   const int tile_rows = step_tile_rows(m->dm, total);
   if (!carve_perceive(g, B, N, d_workspace, workspace_bytes, &w,
-                      tiles_floats(B, N, m->dm.feature_dims, tile_rows)))
+                      tiles_floats(B, N, m->dm.feature_dims, tile_rows), hashgrid_orders(g, B, N)))
     return fail(NPA_ERR_INVALID_ARGUMENT, "workspace too small");
   const PerceptionParams p = make_perception_params(g, model_options(m->cfg), N, m->dm.state_dims);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1527,7 +1534,8 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   const size_t C = size_t(m->dm.state_dims);
   e->tile_rows = step_tile_rows(m->dm, total);
   const size_t tf = tiles_floats(uint32_t(batch), uint32_t(n), m->dm.feature_dims, e->tile_rows);
-  e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n), tf);
+  const bool ordered = hashgrid_orders(e->g, uint32_t(batch), uint32_t(n));
+  e->ws_bytes = perceive_workspace_bytes(e->g, uint32_t(batch), uint32_t(n), tf, ordered);
   npa_status st = NPA_OK;
   auto alloc = [&](void** p, size_t b) -> npa_status {
     NPA_CUDA(cudaMalloc(p, std::max<size_t>(b, 256)), "cudaMalloc executor");
@@ -1542,7 +1550,8 @@ npa_status npa_executor_create(npa_model* m, const npa_grid_config* grid, int64_
   if (st == NPA_OK) st = alloc(reinterpret_cast<void**>(&e->d_step), 4);
   if (st == NPA_OK && cudaMemset(e->d_step, 0, 4) != cudaSuccess)
     st = fail(NPA_ERR_CUDA, "cudaMemset step counter");
-  if (st == NPA_OK && !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w, tf))
+  if (st == NPA_OK &&
+      !carve_perceive(e->g, uint32_t(batch), uint32_t(n), e->ws, e->ws_bytes, &e->w, tf, ordered))
     st = fail(NPA_ERR_INVALID_ARGUMENT, "executor workspace layout");
   // Small batches leave most SMs idle in their latency-bound phases: two
   // rollout groups overlap them (cfg2 shards of 32 / 64 rollouts: 0.227 vs
@@ -1780,7 +1789,8 @@ npa_status npa_executor_set_step_groups(npa_executor* e, int32_t groups) {
     const uint64_t rows = uint64_t(gr.batch) * N;
     gr.tile_rows = step_tile_rows(e->model->dm, rows);
     const size_t tf = tiles_floats(uint32_t(gr.batch), N, e->model->dm.feature_dims, gr.tile_rows);
-    gr.ws_bytes = perceive_workspace_bytes(e->g, uint32_t(gr.batch), N, tf);
+    const bool ordered = hashgrid_orders(e->g, uint32_t(gr.batch), N);
+    gr.ws_bytes = perceive_workspace_bytes(e->g, uint32_t(gr.batch), N, tf, ordered);
     if (cudaMalloc(&gr.ws, std::max<size_t>(gr.ws_bytes, 256)) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&gr.d_step), 4) != cudaSuccess) {
       cudaGetLastError();
@@ -1791,7 +1801,7 @@ npa_status npa_executor_set_step_groups(npa_executor* e, int32_t groups) {
         cudaStreamCreateWithFlags(&gr.side, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&gr.joined, cudaEventDisableTiming) != cudaSuccess)
       st = fail(NPA_ERR_CUDA, "step group set-up");
-    else if (!carve_perceive(e->g, uint32_t(gr.batch), N, gr.ws, gr.ws_bytes, &gr.w, tf))
+    else if (!carve_perceive(e->g, uint32_t(gr.batch), N, gr.ws, gr.ws_bytes, &gr.w, tf, ordered))
       st = fail(NPA_ERR_INVALID_ARGUMENT, "step group workspace layout");
   }
   if (st != NPA_OK) {

@@ -34,6 +34,7 @@ constexpr int kItemsPerLane = 16;
 constexpr int kWarpItems = 32 * kItemsPerLane;             // 512
 constexpr int kTile = kSortWarps * kWarpItems;              // 4096
 constexpr int kDigits = 256;
+constexpr uint32_t kOrderCodes = 4096;  // 12-bit Morton codes of the processing order
 constexpr int kScanThreads = 1024;
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -213,6 +214,52 @@ __global__ void finalize_kernel(GridParams g, const float4* __restrict__ pos,
   for (uint32_t bin = first; bin <= key; ++bin) bin_offsets[bin] = q;
   if (q == total - 1)
     for (uint32_t bin = key + 1; bin <= total_bins; ++bin) bin_offsets[bin] = total;
+}
+
+// Processing order of the device-wide path: sorted slots keyed by batch and
+// the Morton code of their cell block (cell coordinates >> shift, the low
+// `bits` bits per axis), so consecutive threads of the neighbour walks handle
+// spatially adjacent particles whose neighbours are shared in cache (hash
+// order scatters them).  Digit 0 of the keys is histogrammed per tile as in
+// keys_hist_kernel; the stable radix passes then sort (key, slot).
+__global__ void __launch_bounds__(kSortThreads)
+order_keys_kernel(GridParams g, const float4* __restrict__ srec, const int2* __restrict__ scyz,
+                  uint32_t total, uint32_t n, int shift, uint32_t* __restrict__ keys,
+                  uint32_t* __restrict__ vals, uint32_t* __restrict__ hist, uint32_t tiles) {
+  __shared__ uint32_t h[kDigits];
+  for (int i = threadIdx.x; i < kDigits; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t seg = blockIdx.x * kTile + warp * kWarpItems;
+#pragma unroll 4
+  for (int r = 0; r < kItemsPerLane; ++r) {
+    const uint32_t i = seg + r * 32 + lane;
+    if (i < total) {
+      const float4 rec = srec[i];
+      uint32_t code = 0;
+      if (g.dim == 2) {
+        const uint32_t x = uint32_t(__float_as_int(rec.z) >> shift);
+        const uint32_t y = uint32_t(__float_as_int(rec.w) >> shift);
+#pragma unroll
+        for (int b = 0; b < 6; ++b)
+          code |= (((x >> b) & 1u) << (2 * b)) | (((y >> b) & 1u) << (2 * b + 1));
+      } else {
+        const int2 yz = scyz[i];
+        const uint32_t x = uint32_t(__float_as_int(rec.w) >> shift);
+        const uint32_t y = uint32_t(yz.x >> shift), z = uint32_t(yz.y >> shift);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          code |= (((x >> b) & 1u) << (3 * b)) | (((y >> b) & 1u) << (3 * b + 1)) |
+                  (((z >> b) & 1u) << (3 * b + 2));
+      }
+      const uint32_t key = (i / n) * kOrderCodes + code;
+      keys[i] = key;
+      vals[i] = i;
+      atomicAdd(&h[key & 0xffu], 1u);
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < kDigits; d += blockDim.x) hist[d * tiles + blockIdx.x] = h[d];
 }
 
 // ---------------------------------------------------------------------------
@@ -430,7 +477,47 @@ npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_
   finalize_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
       g, positions, ka, va, total, n, bins, out.bin_offsets, out.permutation, out.inverse,
       out.srec, out.scyz);
-  return after_launch("finalize_kernel");
+  NPA_TRY(after_launch("finalize_kernel"));
+  if (!out.order) return NPA_OK;
+  // The processing order: the sorted slots sorted again by (batch, cell-block
+  // Morton code), in the same scratch.  The block edge 2^shift cells is chosen
+  // from the grid's extent so that 64 blocks span a Particle-mode table's side
+  // (or 16 in 3D): cfg1's 512 x 512 table -> blocks of 8 x 8 cells.
+  const int axis_bits = g.dim == 2 ? 6 : 4;
+  int shift = 0;
+  while (shift < 16 && (uint64_t(1) << (axis_bits + shift)) < uint64_t(g.grid_size[0])) ++shift;
+  const uint32_t obits = key_bits(uint64_t(batch) * kOrderCodes);
+  const uint32_t opasses = (obits + 7) / 8;
+  order_keys_kernel<<<tiles, kSortThreads, 0, stream>>>(g, out.srec, out.scyz, total, n, shift, ka,
+                                                         va, hist, tiles);
+  NPA_TRY(after_launch("order_keys_kernel"));
+  for (uint32_t pass = 0; pass < opasses; ++pass) {
+    const uint32_t sh = pass * 8;
+    if (pass > 0) {
+      hist_kernel<<<tiles, kSortThreads, 0, stream>>>(ka, total, sh, hist, tiles);
+      NPA_TRY(after_launch("hist_kernel"));
+    }
+    scan_kernel<<<1, kScanThreads, 0, stream>>>(hist, tiles * kDigits);
+    NPA_TRY(after_launch("scan_kernel"));
+    scatter_kernel<<<tiles, kSortThreads, 0, stream>>>(ka, va, kb, vb, total, sh, hist, tiles);
+    NPA_TRY(after_launch("scatter_kernel"));
+    std::swap(ka, kb);
+    std::swap(va, vb);
+  }
+  NPA_CUDA(cudaMemcpyAsync(out.order, va, size_t(total) * sizeof(uint32_t),
+                           cudaMemcpyDeviceToDevice, stream),
+           "cudaMemcpyAsync order");
+  return NPA_OK;
+}
+
+// Only dense cells (mean bin occupancy >= 8, the warp-cooperative walks) gain
+// more than the extra sort costs: cfg4 (4,194,304 clustered particles)
+// perception 3.32 vs 3.70 s per step; cfg1 (1,048,576 uniform, ~4 per bin)
+// 1.184 vs 1.262 ms but the order's sort adds 0.081 ms; cfg3 (16,384 on a
+// torus) loses 0.02 ms.
+bool hashgrid_orders(const GridParams& g, uint32_t batch, uint32_t n) {
+  const uint64_t total = uint64_t(batch) * n;
+  return total > 0 && !rollout_sort_fits(g, batch, n) && total >= uint64_t(8) * batch * g.cells;
 }
 
 // ---------------------------------------------------------------------------

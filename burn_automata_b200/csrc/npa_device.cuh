@@ -326,6 +326,10 @@ struct SortedGrid {
   const float4* srec;           // [B*N] 2D {x, y, cx, cy}; 3D {x, y, z, cx} (cells as int bits)
   const int2* scyz;             // [B*N] 3D only: {cy, cz}
   const float4* positions;      // [B*N] caller-order positions (own position, w included)
+  // [B*N] or null: the processing order of the kernels that walk neighbours
+  // (thread / tile row t handles sorted slot order[t]; null = the sorted order
+  // itself).  Hit lists and feature tiles are indexed by t.
+  const uint32_t* order;
   uint32_t n;                   // particles per batch
   uint32_t total;               // B*N: sorted slots are < total
 };
@@ -569,6 +573,11 @@ struct HitLists {
   int cap;
   uint32_t stride;   // >= B*N
 };
+
+// Sorted slot handled by processing index t.
+__device__ __forceinline__ uint32_t slot_of(const SortedGrid& s, uint32_t t) {
+  return s.order ? __ldg(s.order + t) : t;
+}
 
 // Cell coordinates of sorted slot q (from its record).
 template <int DIM>

@@ -59,7 +59,15 @@ struct HashgridBuffers {
   uint32_t* inverse;       // [B*N]
   float4* srec;            // [B*N] sorted neighbour records (position + cell)
   int2* scyz;              // [B*N] 3D cell y, z (unused in 2D)
+  // [B*N] optional: a processing order for the neighbour walks, a permutation
+  // of the sorted slots that groups spatially adjacent particles (written by
+  // the device-wide sort only; see hashgrid_orders).
+  uint32_t* order = nullptr;
 };
+// Whether launch_hashgrid writes a processing order for this shape (the
+// device-wide sort path: large rollouts, whose hash order scatters the
+// neighbour gathers over DRAM); the per-rollout path's data stays in L2.
+bool hashgrid_orders(const GridParams& g, uint32_t batch, uint32_t n);
 // Bytes of scratch the sort needs beyond HashgridBuffers.
 size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n);
 // Size of the sorted views (srec + scyz).

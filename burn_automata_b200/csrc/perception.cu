@@ -37,17 +37,19 @@ __global__ void __launch_bounds__(256)
 density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ volume,
                float* __restrict__ density_out, HitLists hl) {
   __shared__ WarpWindow windows[COOP ? 256 / 32 : 1];
-  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  // processing index t (hit lists are indexed by it), sorted slot q
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
   // Whole warp in range (warp-uniform), so warp collectives below are safe.
-  const bool full_warp = (q | 31u) < total;
-  if (q >= total) return;
+  const bool full_warp = (t | 31u) < total;
+  if (t >= total) return;
+  const uint32_t q = slot_of(s, t);
   const uint32_t batch = q / s.n;
   float4 pi;
   int3 c;
   load_record<DIM>(s, q, pi, c);
   float rho = 0.0f;
   uint32_t hits = 0;
-  uint32_t* list = hl.slots ? hl.slots + q : nullptr;
+  uint32_t* list = hl.slots ? hl.slots + t : nullptr;
   auto visit = [&](uint32_t qj, float r2) {
     rho = rho + poly6(g, r2);
     if (list && hits < uint32_t(hl.cap)) list[size_t(hits) * hl.stride] = qj;
@@ -63,7 +65,7 @@ density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ v
     for_each_neighbor<DIM, KB>(g, s, batch, pi, c,
                               [&](uint32_t qj, float4, float r2) { visit(qj, r2); });
   }
-  if (list) hl.count[q] = min(hits, uint32_t(hl.cap + 1));
+  if (list) hl.count[t] = min(hits, uint32_t(hl.cap + 1));
   volume[q] = recip_finite(rho);
   if (density_out) density_out[size_t(batch) * s.n + s.permutation[q]] = rho;
 }
@@ -86,9 +88,10 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
   const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const bool full_warp = (t | 31u) < uint64_t(total) * chunks;  // warp-uniform
   if (t >= uint64_t(total) * chunks) return;
-  const uint32_t q = static_cast<uint32_t>(t / chunks);
-  const int chunk = static_cast<int>(t - uint64_t(q) * chunks);
+  const uint32_t pt = static_cast<uint32_t>(t / chunks);  // processing index
+  const int chunk = static_cast<int>(t - uint64_t(pt) * chunks);
   const int c0 = chunk * CH;
+  const uint32_t q = slot_of(s, pt);
   const uint32_t batch = q / s.n;
   const size_t row = size_t(batch) * s.n + s.permutation[q];
   const float4 pi = __ldg(s.positions + row);
@@ -102,7 +105,7 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
+  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a, win,
                           peers);
   const size_t F = p.feature_dims;
   float* f = features + row * F;
@@ -135,15 +138,17 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists
   const bool full_warp = (t | 31u) < uint64_t(q_end - q_begin) * chunks &&
                          q_begin + static_cast<uint32_t>((t | 31u) / chunks) < total;
   if (t >= uint64_t(q_end - q_begin) * chunks) return;
-  const uint32_t q = q_begin + static_cast<uint32_t>(t / chunks);
-  const int chunk = static_cast<int>(t - uint64_t(q - q_begin) * chunks);
+  // processing index pt: tile row pt, sorted slot q
+  const uint32_t pt = q_begin + static_cast<uint32_t>(t / chunks);
+  const int chunk = static_cast<int>(t - uint64_t(pt - q_begin) * chunks);
   const int c0 = chunk * CH;
   const size_t F = p.feature_dims;
-  float* tile = tiles + size_t(q / tile_rows) * F * tile_rows + (q % tile_rows);
-  if (q >= total) {
+  float* tile = tiles + size_t(pt / tile_rows) * F * tile_rows + (pt % tile_rows);
+  if (pt >= total) {
     for (int k = chunk; k < int(F); k += chunks) tile[size_t(k) * tile_rows] = 0.0f;
     return;
   }
+  const uint32_t q = slot_of(s, pt);
   const uint32_t batch = q / s.n;
   const size_t row = size_t(batch) * s.n + s.permutation[q];
   const float4 pi = __ldg(s.positions + row);
@@ -157,8 +162,8 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH, OPT>(g, p, s, hl, batch, q, pi, c, states, C, c0, volume, si, a, win,
-                          peers);
+  perceive_chunk<DIM, CH, OPT>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a,
+                               win, peers);
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
                          [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
 }

@@ -199,14 +199,16 @@ __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkSta
 // caller-order state matrix [B*N][C]; `volume` is recip_finite(density) per
 // sorted slot; `si` holds the particle's own channels.  Channels >= C stay 0.
 // The neighbours come from the density pass's hit list when it holds them all,
-// otherwise from a fresh hashgrid walk; both give the walk order.  `win` is
-// set (warp-uniformly) when the warp's lanes fall into few (batch, cell)
-// groups (`peers`: this lane's group): then a walk, if any lane needs one, is
-// the warp-cooperative walk of each group.
+// otherwise from a fresh hashgrid walk; both give the walk order.  `hit_row`
+// is the processing index under which the density pass wrote the particle's
+// hit list.  `win` is set (warp-uniformly) when the warp's lanes fall into few
+// (batch, cell) groups (`peers`: this lane's group): then a walk, if any lane
+// needs one, is the warp-cooperative walk of each group.
 template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void perceive_chunk(const GridParams& g, const PerceptionParams& p,
                                                const SortedGrid& s, const HitLists& hl,
-                                               uint32_t batch, uint32_t q, float4 pi,
+                                               uint32_t batch, uint32_t q, uint32_t hit_row,
+                                               float4 pi,
                                                int3 center, const float* __restrict__ states,
                                                int C, int c0, const float* __restrict__ volume,
                                                const float (&si)[CH],
@@ -217,7 +219,7 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
                     (c0 + CH <= C);
   ChunkState<DIM, CH> st;
   chunk_init(st);
-  const uint32_t nh = hl.slots ? __ldg(hl.count + q) : uint32_t(hl.cap + 1);
+  const uint32_t nh = hl.slots ? __ldg(hl.count + hit_row) : uint32_t(hl.cap + 1);
   if (win && __any_sync(0xffffffffu, nh > uint32_t(hl.cap))) {
     for_each_neighbor_warp<DIM>(
         g, s, batch, pi, center, peers, *win,
@@ -231,7 +233,7 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
           chunk_add<DIM, CH, OPT>(g, p, qn == q, d, r2, win->vol[j], sjv, si, st);
         });
   } else if (nh <= uint32_t(hl.cap)) {
-    const uint32_t* list = hl.slots + q;
+    const uint32_t* list = hl.slots + hit_row;
     for (uint32_t e0 = 0; e0 < nh; e0 += 2) {
       uint32_t qj[2];
       float4 pj[2];

@@ -494,13 +494,14 @@ __device__ __forceinline__ void mlp_tile(
                    ((reinterpret_cast<uintptr_t>(sp.states) | reinterpret_cast<uintptr_t>(next_states) |
                      reinterpret_cast<uintptr_t>(ds_out)) & 15u) == 0;
   // The epilogue's position / mask reads are issued before layer 1 so
-  // their latency is hidden behind it.
-  const uint32_t q = tile * s.M + r;
-  const bool live = q < total;
+  // their latency is hidden behind it.  Tile row r is processing index t.
+  const uint32_t t = tile * s.M + r;
+  const bool live = t < total;
   size_t row = 0;
   float4 pi = make_float4(0.f, 0.f, 0.f, 0.f);
   float m = 1.0f;
   if (live) {
+    const uint32_t q = slot_of(sg, t);
     const uint32_t batch = q / sg.n;
     const uint32_t local = __ldg(sg.permutation + q);
     row = size_t(batch) * sg.n + local;
@@ -701,16 +702,17 @@ fused_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, 
   const int C = sp.C;
   const int items = s.M * chunks;
   for (uint32_t tile = tile_begin + blockIdx.x; tile < tile_end; tile += gridDim.x) {
-    for (int t = threadIdx.x; t < items; t += NT) {
-      const int rr = t / chunks;
-      const int chunk = t - rr * chunks;
+    for (int it = threadIdx.x; it < items; it += NT) {
+      const int rr = it / chunks;
+      const int chunk = it - rr * chunks;
       const int c0 = chunk * CH;
-      const uint32_t q = tile * s.M + rr;
+      const uint32_t t = tile * s.M + rr;  // processing index
       float* col = ft + rr;
-      if (q >= total) {
+      if (t >= total) {
         for (int k = chunk; k < s.F; k += chunks) col[k * s.M] = 0.0f;
         continue;
       }
+      const uint32_t q = slot_of(sg, t);
       const uint32_t batch = q / sg.n;
       const size_t row = size_t(batch) * sg.n + sg.permutation[q];
       const float4 pi = __ldg(sg.positions + row);
@@ -718,8 +720,8 @@ fused_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, 
       float si[CH];
       load_row<CH>(sp.states, row, C, c0, false, si);
       PerceptionAcc<DIM, CH> a;
-      perceive_chunk<DIM, CH, OPT>(g, pp, sg, hl, batch, q, pi, c, sp.states, C, c0, volume, si,
-                                   a);
+      perceive_chunk<DIM, CH, OPT>(g, pp, sg, hl, batch, q, t, pi, c, sp.states, C, c0, volume,
+                                   si, a);
       emit_features<DIM, CH>(pp, C, c0, chunk == 0, si, a, pi,
                              [&](int k, float v) { col[k * s.M] = v; });
     }
