@@ -498,7 +498,9 @@ def run_ours(args, rank, world, local_rank):
     lib = ba.load_library()
     spec = WORKLOADS[args.workload]
     first, per_rank, scaling = shard_plan(args, world, rank)
-    w = workloads.make(args.workload, batch=per_rank, first=first)
+    w = workloads.make(args.workload, batch=per_rank, first=first,
+                       **({"n": args.particles} if args.particles else {}),
+                       **({"components": args.components} if args.components else {}))
     particles_rank = w.batch * w.n
     stream = torch.cuda.Stream(dev)
     sptr = stream.cuda_stream
@@ -648,7 +650,11 @@ def run_ours(args, rank, world, local_rank):
             "ms_per_step": max_ms / args.steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "data": DATA,
-            "config": {"workload": args.workload, "rollouts_per_gpu": per_rank,
+            "config": {"workload": (args.workload if not (args.particles or args.components)
+                                    else f"{args.workload} reduced: {w.n} particles per rollout"
+                                         + (f", {args.components} components"
+                                            if args.components else "")),
+                       "rollouts_per_gpu": per_rank,
                        "rollouts_total": sum(c for _, c in plans),
                        "particles_per_rollout": w.n, "particles_per_gpu": particles_rank,
                        "state_dims": w.state_dims, "features": features,
@@ -735,6 +741,12 @@ def main():
     ap.add_argument("--groups", type=int, default=None,
                     help="replay the shard's rollouts as this many independent chains (1-4; "
                          "default: the executor's choice)")
+    ap.add_argument("--particles", type=int, default=None,
+                    help="particles per rollout instead of the workload's (reduced cases for "
+                         "profiling; the bench line then names a reduced workload)")
+    ap.add_argument("--components", type=int, default=None,
+                    help="cfg4: mixture components (1 with --particles 65536 is one component at "
+                         "the full draw's density)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
