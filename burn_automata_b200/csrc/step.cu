@@ -268,6 +268,10 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
   }
 }
 
+__device__ __forceinline__ float lane_of(const float4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
 // Layer 2: outs[r][o] = b2[o] + sum_h w2[o][h] * hid[r][h], sequential in h.
 // R rows per thread: R * tpr threads per row group, thread j owning outputs
 // o = j + R tpr u (u in [u0, u0 + NOUT)) of the group's R rows; each weight
@@ -303,24 +307,17 @@ __device__ __forceinline__ void mlp_layer2_rows(const MlpShape& s, const float* 
     float4 hv[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) hv[i] = *reinterpret_cast<const float4*>(hid + hoff[i] + h);
-    float p[R][NOUT][4];
+    float4 wv[NOUT];
 #pragma unroll
-    for (int u = 0; u < NOUT; ++u) {
-      const float4 w = *reinterpret_cast<const float4*>(w2s + woff[u] + h);
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        p[i][u][0] = w.x * hv[i].x;
-        p[i][u][1] = w.y * hv[i].y;
-        p[i][u][2] = w.z * hv[i].z;
-        p[i][u][3] = w.w * hv[i].w;
-      }
-    }
+    for (int u = 0; u < NOUT; ++u) wv[u] = *reinterpret_cast<const float4*>(w2s + woff[u] + h);
+    // each product is added as soon as it is formed: batching the products
+    // first, as layer 1 does, is slower here (cfg2 MLP 0.922 vs 0.897 ms)
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
       for (int u = 0; u < NOUT; ++u)
 #pragma unroll
-        for (int i = 0; i < R; ++i) acc[i][u] = acc[i][u] + p[i][u][k];
+        for (int i = 0; i < R; ++i) acc[i][u] = acc[i][u] + lane_of(wv[u], k) * lane_of(hv[i], k);
   }
   for (int h = H4; h < s.H; ++h) {
 #pragma unroll
