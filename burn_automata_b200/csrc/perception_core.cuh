@@ -225,7 +225,8 @@ __device__ __forceinline__ void perceive_chunk(const GridParams& g, const Percep
         g, s, batch, pi, center, peers, *win,
         [&](uint32_t lane, uint32_t qn) {
           win->vol[lane] = __ldg(volume + qn);
-          win->row[lane] = batch_base + __ldg(s.permutation + qn);
+          // qn is in the walked group's rollout, which need not be this lane's
+          win->row[lane] = qn / s.n * s.n + __ldg(s.permutation + qn);
         },
         [&](uint32_t j, uint32_t qn, float4 d, float r2) {
           float sjv[CH];

@@ -490,6 +490,27 @@ def test_dense_cluster_perception_full_options(oracle_mod):
         np.testing.assert_allclose(gpu.features, ref["features"], rtol=RTOL, atol=ATOL)
 
 
+def test_dense_cluster_batches_with_warps_across_rollouts(oracle_mod):
+    """Dense cells in a batch of rollouts whose size is not a multiple of 32:
+    some warps hold particles of two rollouts, and the cooperative walk of
+    one rollout's cell group is staged by lanes of the other (their state
+    rows must come from the walked rollout)."""
+    b, n = 3, 2011
+    w = workloads.make("cfg4", batch=b, n=n, components=1, steps=1)
+    w.grid = w.grid.with_(grid_size=(8, 8, 1))  # ~31 particles per bin: cooperative kernels
+    w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False)
+    opt = w.model.perception_options()
+    gpu = ba.perceive_with_options(w.positions, w.states, b, n, w.state_dims, w.grid, opt)
+    ref = oracle_mod.perceive_with_options(w.positions, w.states, b, n, w.state_dims, w.grid, opt)
+    np.testing.assert_array_equal(gpu.density, ref["density"])
+    np.testing.assert_array_equal(gpu.features, ref["features"])
+    m = make_model(w)
+    got = m.step(w.positions, w.states, b, n, w.grid, w.dt)
+    want = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, b, n, w.dt)
+    for key in ("features", "next_states", "next_positions"):
+        np.testing.assert_array_equal(getattr(got, key), want[key], err_msg=key)
+
+
 def test_mlp_feature_tile_bulk_copies_complete():
     """The MLP step kernel's bulk (TMA) copies of feature tiles all complete
     within their bounded waits: the device timeout counter stays 0 over
