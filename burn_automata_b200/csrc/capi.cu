@@ -446,6 +446,7 @@ struct HostArena {
   void* base = nullptr;
   size_t cap = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t stream2 = nullptr;  // second compute stream of the chunk pipeline
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   std::vector<cudaEvent_t> events;
 };
@@ -828,11 +829,11 @@ void npa_model_destroy(npa_model* m) {
   cudaFree(m->dm.w2);
   cudaFree(m->dm.b2);
   HostArena& a = m->arena;
-  for (cudaStream_t s : {a.stream, a.copy_in, a.copy_out})
+  for (cudaStream_t s : {a.stream, a.stream2, a.copy_in, a.copy_out})
     if (s) cudaStreamSynchronize(s);
   cudaFree(a.base);
   for (cudaEvent_t e : a.events) cudaEventDestroy(e);
-  for (cudaStream_t s : {a.stream, a.copy_in, a.copy_out})
+  for (cudaStream_t s : {a.stream, a.stream2, a.copy_in, a.copy_out})
     if (s) cudaStreamDestroy(s);
   cudaSetDevice(prev);
   delete m;
@@ -887,6 +888,7 @@ npa_status arena_reserve(npa_model* m, size_t bytes) {
   const uint64_t cap = g_alloc_cap.load();
   if (cap && bytes > cap) return fail(NPA_ERR_OUT_OF_MEMORY, "allocation cap reached");
   NPA_CUDA(cudaStreamSynchronize(a.stream), "cudaStreamSynchronize");
+  if (a.stream2) NPA_CUDA(cudaStreamSynchronize(a.stream2), "cudaStreamSynchronize");
   cudaFree(a.base);
   a.base = nullptr;
   a.cap = 0;
@@ -921,7 +923,7 @@ static uint32_t host_step_chunks(uint32_t B, uint32_t N, bool pinned) {
 }
 
 static npa_status arena_pipeline(HostArena& a, uint32_t chunks) {
-  for (cudaStream_t* s : {&a.copy_in, &a.copy_out})
+  for (cudaStream_t* s : {&a.copy_in, &a.copy_out, &a.stream2})
     if (!*s) NPA_CUDA(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "cudaStreamCreate");
   while (a.events.size() < 2 * size_t(chunks)) {
     cudaEvent_t e;
@@ -969,6 +971,7 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
     float4 *pos, *np, *dx;
     float *st, *mask, *ns, *ds, *feat, *dens;
     char* ws;
+    char* ws2;  // the second compute stream's workspace (chunked steps)
   } b{};
   const size_t F = size_t(m->dm.feature_dims);
   auto layout = [&](void* base) {
@@ -983,16 +986,18 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
     b.feat = features ? c.take<float>(size_t(total) * F) : nullptr;
     b.dens = density ? c.take<float>(total) : nullptr;
     b.ws = c.take<char>(wsb);
+    b.ws2 = chunks > 1 ? c.take<char>(wsb) : nullptr;
     return c.used + 256;
   };
   NPA_TRY(arena_reserve(m, layout(nullptr)));
   layout(m->arena.base);
   HostArena& a = m->arena;
-  cudaStream_t st = a.stream, in = st, out = st;
+  cudaStream_t st = a.stream, st2 = st, in = st, out = st;
   if (chunks > 1) {
     NPA_TRY(arena_pipeline(a, chunks));
     in = a.copy_in;
     out = a.copy_out;
+    st2 = a.stream2;
   }
   auto h2d = [&](void* d, const void* h, size_t bytes) -> npa_status {
     if (bytes) NPA_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, in), "cudaMemcpyAsync H2D");
@@ -1017,19 +1022,23 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
       if (update_mask) NPA_TRY(h2d(b.mask + p0, update_mask + p0, (p1 - p0) * 4));
       if (chunks > 1) NPA_CUDA(cudaEventRecord(a.events[2 * c], in), "cudaEventRecord");
     }
+    // Consecutive chunks alternate between two compute streams (each with
+    // its own workspace), so one chunk's latency-bound phases overlap the
+    // next chunk's kernels, as in the executor's rollout groups.
     for (uint32_t c = 0; c < chunks; ++c) {
       size_t p0, p1;
       span(c, &p0, &p1);
       const int64_t rollouts = int64_t((p1 - p0) / std::max<uint32_t>(N, 1));
-      if (chunks > 1) NPA_CUDA(cudaStreamWaitEvent(st, a.events[2 * c], 0), "cudaStreamWaitEvent");
+      cudaStream_t cs = (c & 1) ? st2 : st;
+      if (chunks > 1) NPA_CUDA(cudaStreamWaitEvent(cs, a.events[2 * c], 0), "cudaStreamWaitEvent");
       NPA_TRY(npa_dev_model_step(m, grid, reinterpret_cast<float*>(b.pos + p0), b.st + p0 * C,
                                  chunks > 1 ? rollouts : batch, n, dt,
                                  b.mask ? b.mask + p0 : nullptr, reinterpret_cast<float*>(b.np + p0),
                                  b.ns + p0 * C, b.dx ? reinterpret_cast<float*>(b.dx + p0) : nullptr,
                                  b.ds ? b.ds + p0 * C : nullptr, b.feat ? b.feat + p0 * F : nullptr,
-                                 b.dens ? b.dens + p0 : nullptr, b.ws, wsb, st));
+                                 b.dens ? b.dens + p0 : nullptr, (c & 1) ? b.ws2 : b.ws, wsb, cs));
       if (chunks > 1) {
-        NPA_CUDA(cudaEventRecord(a.events[2 * c + 1], st), "cudaEventRecord");
+        NPA_CUDA(cudaEventRecord(a.events[2 * c + 1], cs), "cudaEventRecord");
         NPA_CUDA(cudaStreamWaitEvent(out, a.events[2 * c + 1], 0), "cudaStreamWaitEvent");
       }
       NPA_TRY(d2h(next_positions + 4 * p0, b.np + p0, (p1 - p0) * 16));
@@ -1045,8 +1054,9 @@ npa_status npa_model_step(npa_model* m, const npa_grid_config* grid, const float
   const cudaError_t e_out = cudaStreamSynchronize(out);
   const cudaError_t e_in = in != out ? cudaStreamSynchronize(in) : cudaSuccess;
   const cudaError_t e_st = st != out ? cudaStreamSynchronize(st) : cudaSuccess;
+  const cudaError_t e_st2 = st2 != st ? cudaStreamSynchronize(st2) : cudaSuccess;
   if (status != NPA_OK) return status;
-  for (cudaError_t e : {e_out, e_in, e_st})
+  for (cudaError_t e : {e_out, e_in, e_st, e_st2})
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
   return check_bulk_copies();
 }
