@@ -437,8 +437,9 @@ npa_status launch_hashgrid(const GridParams& g, const float4* positions, uint32_
   if (rollout_sort_fits(g, batch, n)) {
     const size_t smem = rollout_sort_smem(g, n);
     auto launch = [&](auto kernel) -> npa_status {
-      NPA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-               "cudaFuncSetAttribute");
+      int per_sm = 0, sms = 0;
+      NPA_TRY(kernel_occupancy(reinterpret_cast<const void*>(kernel), kRolloutThreads, smem,
+                               &per_sm, &sms));
       kernel<<<batch, kRolloutThreads, smem, stream>>>(g, positions, n, batch, out.bin_offsets,
                                                         out.permutation, out.inverse, out.srec,
                                                         out.scyz);
@@ -592,6 +593,70 @@ npa_status static_scratch_address(void** out) {
 }
 
 }  // namespace
+
+// Launch plans: the dynamic shared memory limit is set and the occupancy
+// queried once per (device, context, kernel, block size, shared memory); a
+// host step makes tens of launches, and these runtime calls cost as much host
+// time as the launches themselves.
+namespace {
+struct PlanKey {
+  int device;
+  CUcontext ctx;
+  const void* kernel;
+  int threads;
+  size_t smem;
+  int per_sm;
+  int sms;
+};
+std::mutex g_plan_mu;
+std::vector<PlanKey> g_plans;
+}  // namespace
+
+npa_status kernel_occupancy(const void* kernel, int threads, size_t smem, int* per_sm, int* sms) {
+  int dev = 0;
+  NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  CUcontext ctx = nullptr;
+  NPA_TRY(current_context(&ctx));
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mu);
+    if (ctx)
+      for (const PlanKey& k : g_plans)
+        if (k.device == dev && k.ctx == ctx && k.kernel == kernel && k.threads == threads &&
+            k.smem == smem) {
+          *per_sm = k.per_sm;
+          *sms = k.sms;
+          return NPA_OK;
+        }
+  }
+  int max_optin = 0, count = 0, blocks = 0;
+  NPA_CUDA(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
+           "cudaDeviceGetAttribute");
+  NPA_CUDA(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev),
+           "cudaDeviceGetAttribute");
+  if (smem > size_t(max_optin))
+    return fail(NPA_ERR_UNSUPPORTED, "kernel needs more shared memory than a block has");
+  // The limit only ever rises: launches planned earlier with more shared
+  // memory keep theirs.
+  size_t limit = smem;
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mu);
+    for (const PlanKey& k : g_plans)
+      if (k.device == dev && k.ctx == ctx && k.kernel == kernel) limit = std::max(limit, k.smem);
+  }
+  NPA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(limit)),
+           "cudaFuncSetAttribute");
+  NPA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem),
+           "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  NPA_TRY(current_context(&ctx));
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mu);
+    g_plans.push_back(PlanKey{dev, ctx, kernel, threads, smem, blocks, count});
+  }
+  *per_sm = blocks;
+  *sms = count;
+  return NPA_OK;
+}
+
 }  // namespace npa
 
 extern "C" npa_status npa_dev_build_hashgrid_noalloc(const npa_grid_config* cfg,

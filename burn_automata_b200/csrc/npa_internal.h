@@ -68,6 +68,10 @@ struct HashgridBuffers {
 // device-wide sort path: large rollouts, whose hash order scatters the
 // neighbour gathers over DRAM); the per-rollout path's data stays in L2.
 bool hashgrid_orders(const GridParams& g, uint32_t batch, uint32_t n);
+// Blocks of `kernel` resident per SM at `threads` threads and `smem` bytes of
+// dynamic shared memory, and the SM count; sets the kernel's dynamic shared
+// memory limit first.  Cached per (device, context, kernel, threads, smem).
+npa_status kernel_occupancy(const void* kernel, int threads, size_t smem, int* per_sm, int* sms);
 // Bytes of scratch the sort needs beyond HashgridBuffers.
 size_t hashgrid_scratch_bytes(const GridParams& g, uint32_t batch, uint32_t n);
 // Size of the sorted views (srec + scyz).

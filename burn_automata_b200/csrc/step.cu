@@ -793,20 +793,8 @@ struct LaunchCfg {
 template <class K>
 npa_status plan(K kernel, const MlpShape& s, uint64_t tiles, LaunchCfg* out) {
   const size_t smem = smem_layout(s).total * sizeof(float);
-  int dev = 0;
-  NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  int max_optin = 0, sms = 0;
-  NPA_CUDA(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
-           "cudaDeviceGetAttribute");
-  NPA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
-           "cudaDeviceGetAttribute");
-  if (smem > size_t(max_optin))
-    return fail(NPA_ERR_UNSUPPORTED, "MLP shape needs more shared memory than a block has");
-  NPA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-           "cudaFuncSetAttribute");
-  int per_sm = 0;
-  NPA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, s.NT, smem),
-           "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int per_sm = 0, sms = 0;
+  NPA_TRY(kernel_occupancy(reinterpret_cast<const void*>(kernel), s.NT, smem, &per_sm, &sms));
   if (per_sm < 1) return fail(NPA_ERR_UNSUPPORTED, "MLP kernel cannot be resident");
   const uint64_t slots = uint64_t(per_sm) * sms;
   out->grid = static_cast<unsigned>(std::max<uint64_t>(1, std::min<uint64_t>(tiles, slots)));
