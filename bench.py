@@ -719,6 +719,33 @@ def run_ours(args, rank, world, local_rank):
     multigpu.finish()
 
 
+def fp32_ceiling():
+    """The MLP's layer-1 register tile alone (npa_debug_fp32_tile_rate): 64
+    products and 64 sums per k step from shared memory, nothing else.  Its
+    rate against 148 SMs x 128 lanes x the sampled clock is the practical FP32
+    ceiling of exact-order multiply-add (a rounded multiply, then a rounded
+    add)."""
+    import ctypes
+
+    import burn_automata_b200 as ba
+    import torch
+
+    lib = ba.load_library()
+    torch.cuda.init()
+    sampler = ClockSampler([0])
+    sampler.start()
+    rate, ms = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    status = lib.npa_debug_fp32_tile_rate(4000, ctypes.byref(rate), ctypes.byref(ms))
+    clocks = sampler.stop()
+    if status != 0:
+        raise SystemExit(f"probe failed: {lib.npa_last_error_message().decode()}")
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    peak = 148 * 128 * mhz * 1e6
+    print(json.dumps({"probe": "exact-order FP32 register tile (MLP layer 1 inner loop)",
+                      "ops_per_s": rate.value, "kernel_ms": ms.value, "peak_ops_per_s": peak,
+                      "frac": rate.value / peak, "clocks": clocks}))
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -747,6 +774,9 @@ def main():
     ap.add_argument("--components", type=int, default=None,
                     help="cfg4: mixture components (1 with --particles 65536 is one component at "
                          "the full draw's density)")
+    ap.add_argument("--fp32-ceiling", action="store_true",
+                    help="print the FP32 pipe rate of the MLP's exact-order register tile alone "
+                         "(the ceiling the MLP kernel can approach) and exit")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -759,6 +789,9 @@ def main():
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
     local_rank = env_int("LOCAL_RANK", 0)
+    if args.fp32_ceiling:
+        fp32_ceiling()
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -167,6 +167,7 @@ SIGNATURES = [
 # Symbols exported beyond the public header (test hooks).
 EXTRA_SIGNATURES = [
     ("npa_debug_set_allocation_cap", None, [c_u64]),
+    ("npa_debug_fp32_tile_rate", c_i32, [c_i32, P(ctypes.c_double), P(ctypes.c_double)]),
 ]
 
 
