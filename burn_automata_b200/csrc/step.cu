@@ -470,8 +470,12 @@ constexpr int kStateRegs = 8;
 // features in ft [F][M].  Layer 1, layer 2, then
 // forward_from_features_with_eps + gates + euler_step with TPR threads per
 // row; after_layer2() runs once layer 2 has finished with ft and hid.
+// `arrived`: this thread saw the tile's copy complete.  The block decides at
+// the barrier after layer 1 (so a thread may start layer 1 while others
+// finish the previous tile's epilogue); false for any thread -> the tile is
+// abandoned and mlp_tile returns false.
 template <int HG, int NT, bool ALIAS, class AfterLayer2>
-__device__ __forceinline__ void mlp_tile(
+__device__ __forceinline__ bool mlp_tile(bool arrived,
     const MlpShape& s, const GridParams& g, const SortedGrid& sg, uint32_t total, uint32_t tile,
     const float (&bias1)[kTH], const float* __restrict__ w1t, const float* __restrict__ b2,
     const StepParams& sp, const EulerParams& ep, const float* __restrict__ mask,
@@ -511,7 +515,7 @@ __device__ __forceinline__ void mlp_tile(
   if (features_out && live)
     for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
   mlp_layer1<HG, NT, ALIAS>(s, w1t, bias1, ft, w1s, hid);
-  __syncthreads();
+  if (__syncthreads_or(!arrived)) return false;
   // own state for the Euler update, hidden behind layer 2
   float sv[kStateRegs];
   if (vec) {
@@ -604,6 +608,7 @@ __device__ __forceinline__ void mlp_tile(
       if (ds_out) ds_out[row * C + ch] = dsv;
     }
   }
+  return true;
 }
 
 // The rollout step's MLP stage over feature tiles in sorted order.
@@ -642,9 +647,20 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   float bias1[kTH];
   load_bias1<HG>(s, b1, bias1);
   const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
+  // No barrier at the top of a tile: a thread waits for the tile's copy on
+  // the mbarrier itself and goes on into layer 1 while slower threads finish
+  // the previous tile's epilogue (which reads neither ft nor hid); the block's
+  // decision on a copy that did not complete comes at the barrier after
+  // layer 1.
   for (; tile < tiles; tile += gridDim.x) {
     const bool arrived = mbar_wait(bar, phase);
-    if (__syncthreads_or(!arrived)) {
+    const bool done = mlp_tile<HG, NT, false>(
+        arrived, s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos, next_states,
+        dx_out, ds_out, features_out, step_index, ft, w1s, hid, w2s, outs, [&] {
+          const uint32_t next = tile + gridDim.x;
+          if (next < tiles) issue(next);
+        });
+    if (!done) {
       // The copy did not complete in time (for some thread): the whole block
       // counts it, gives the copy a last bounded wait so nothing lands in its
       // shared memory after it exits, and leaves the remaining tiles undone.
@@ -655,12 +671,6 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
       return;
     }
     phase ^= 1u;
-    mlp_tile<HG, NT, false>(s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
-                            next_states, dx_out, ds_out, features_out, step_index, ft, w1s, hid,
-                            w2s, outs, [&] {
-                              const uint32_t next = tile + gridDim.x;
-                              if (next < tiles) issue(next);
-                            });
   }
 }
 
@@ -725,7 +735,7 @@ fused_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, 
     __syncthreads();
     // mlp_tile synchronises after layer 2, so the next tile's feature rows
     // (which overwrite hid) wait for it.
-    mlp_tile<HG, NT, true>(s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
+    mlp_tile<HG, NT, true>(true, s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
                            next_states, dx_out, ds_out, features_out, step_index, ft, w1s, hid,
                            w2s, outs, [] {});
   }
