@@ -111,6 +111,13 @@ def mlp_kernel_bytes(model) -> int:
     return 4 * model.perception_dims() + 32 + 8 * model.state_dims + 4
 
 
+def fused_kernel_bytes(model) -> int:
+    """The fused step kernel per particle: the MLP stage's bytes without the
+    feature row, plus the perception's own reads: hit list and count (~40),
+    own state (4C), volume (4) and record (16)."""
+    return 32 + 8 * model.state_dims + 4 + 40 + 4 * model.state_dims + 4 + 16
+
+
 def step_bytes(w) -> float:
     """Whole rollout step per particle-step: position read + write (32),
     state read + write (8C), density write + read (8), hashgrid key /
@@ -632,7 +639,10 @@ def run_ours(args, rank, world, local_rank):
             sbytes = perception_step_bytes(w, features)
             names = ["hashgrid", "density", "perception"]
         else:
-            kernel, kbytes = "mlp_step_kernel", mlp_kernel_bytes(w.model)
+            if args.fused:
+                kernel, kbytes = "fused_step_kernel", fused_kernel_bytes(w.model)
+            else:
+                kernel, kbytes = "mlp_step_kernel", mlp_kernel_bytes(w.model)
             sbytes = step_bytes(w)
             names = ["hashgrid", "density", "perception", "mlp_step"]
         achieved = kbytes * particles_rank / (dom_ms / 1000.0) / 1e9
