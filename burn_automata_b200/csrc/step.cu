@@ -30,6 +30,7 @@
 // (crates/burn_automata_kernels/src/reference/step.rs:4-55), writing the next
 // position / state in the caller's particle order.
 #include <algorithm>
+#include <type_traits>
 
 #include "perception_core.cuh"
 
@@ -131,11 +132,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// The threads that run an MLP tile: the whole block, or a block's consumer
+// warps in the warp-specialised step (their own index and named barrier).
+struct BlockGroup {
+  static __device__ __forceinline__ int tid() { return threadIdx.x; }
+  static __device__ __forceinline__ int size() { return blockDim.x; }
+  static __device__ __forceinline__ void sync() { __syncthreads(); }
+  static __device__ __forceinline__ bool sync_or(bool p) { return __syncthreads_or(p); }
+};
+
 // Weights into shared memory: w2 [O][H] -> rows of w2_stride; w1^T when resident.
+template <class G = BlockGroup>
 __device__ __forceinline__ void load_weights(const MlpShape& s, const float* __restrict__ w1t,
                                              const float* __restrict__ w2, float* w1s,
                                              float* w2s) {
-  for (int e = threadIdx.x; e < s.O * s.H; e += blockDim.x) {
+  for (int e = G::tid(); e < s.O * s.H; e += G::size()) {
     const int o = e / s.H, h = e - o * s.H;
     w2s[o * s.w2_stride + h] = __ldg(w2 + e);
   }
@@ -143,7 +154,7 @@ __device__ __forceinline__ void load_weights(const MlpShape& s, const float* __r
     const float4* src = reinterpret_cast<const float4*>(w1t);
     float4* dst = reinterpret_cast<float4*>(w1s);
     const int n4 = s.F * s.Hp / 4;
-    for (int e = threadIdx.x; e < n4; e += blockDim.x) dst[e] = __ldg(src + e);
+    for (int e = G::tid(); e < n4; e += G::size()) dst[e] = __ldg(src + e);
   }
 }
 
@@ -181,24 +192,24 @@ __device__ __forceinline__ void micro_tile(float (&acc)[8][kTH], float4 a0, floa
 // hg owns units (j4 HG + hg) 4 + e, j4 in {0, 1}, e in [0, 4), so each
 // 16-byte weight load of a warp reads 128 contiguous bytes and each feature
 // load four 32-byte-spaced rows: one shared-memory wavefront apiece.
-template <int HG>
+template <int HG, class G = BlockGroup>
 __device__ __forceinline__ int layer1_hidden_group() {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = G::tid() & 31, warp = G::tid() >> 5;
   return (warp % (HG / 8)) * 8 + (lane & 7);
 }
-template <int HG>
+template <int HG, class G = BlockGroup>
 __device__ __forceinline__ int layer1_row_group() {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = G::tid() & 31, warp = G::tid() >> 5;
   return (warp / (HG / 8)) * 4 + (lane >> 3);
 }
 static_assert(kTH == 8, "layer1_unit assumes two float4 groups per thread");
 __host__ __device__ constexpr int layer1_unit(int HG, int hg, int j4) { return (j4 * HG + hg) * 4; }
 
 // The layer-1 biases of this thread's hidden units (constant over tiles).
-template <int HG>
+template <int HG, class G = BlockGroup>
 __device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __restrict__ b1,
                                            float (&bias)[kTH]) {
-  const int hg = layer1_hidden_group<HG>();
+  const int hg = layer1_hidden_group<HG, G>();
 #pragma unroll
   for (int j = 0; j < kTH; ++j) {
     const int h = layer1_unit(HG, hg, j / 4) + (j & 3);
@@ -208,16 +219,16 @@ __device__ __forceinline__ void load_bias1(const MlpShape& s, const float* __res
 
 // ALIAS: hid overlays ft, so the block synchronises before the hidden rows
 // are stored.
-template <int HG, int NT, bool ALIAS = false>
+template <int HG, int NT, bool ALIAS = false, class G = BlockGroup>
 __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __restrict__ w1t,
                                            const float (&bias)[kTH], const float* ft,
                                            float* w1s, float* hid) {
   static_assert(HG % 8 == 0 && (NT / 32) % (HG / 8) == 0, "layer-1 thread layout");
   constexpr int RG = NT / HG;
   constexpr int M = RG * 8;
-  const int t = threadIdx.x;
-  const int rg = layer1_row_group<HG>();
-  const int hg = layer1_hidden_group<HG>();
+  const int t = G::tid();
+  const int rg = layer1_row_group<HG, G>();
+  const int hg = layer1_hidden_group<HG, G>();
   float acc[8][kTH];
 #pragma unroll
   for (int j = 0; j < kTH; ++j)
@@ -239,11 +250,11 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
     const int hp4 = s.Hp >> 2;
     for (int kc = 0; kc < s.F; kc += kKC) {
       const int kn = min(kKC, s.F - kc);
-      __syncthreads();  // previous slice consumed
+      G::sync();  // previous slice consumed
       const float4* src = reinterpret_cast<const float4*>(w1t + size_t(kc) * s.Hp);
       float4* dst = reinterpret_cast<float4*>(w1s);
       for (int e = t; e < kn * hp4; e += NT) dst[e] = __ldg(src + e);
-      __syncthreads();
+      G::sync();
       for (int kk = 0; kk < kn; ++kk) {
         const int k = kc + kk;
         const float4 a0 = *reinterpret_cast<const float4*>(arow + k * M);
@@ -256,7 +267,7 @@ __device__ __forceinline__ void mlp_layer1(const MlpShape& s, const float* __res
       }
     }
   }
-  if constexpr (ALIAS) __syncthreads();
+  if constexpr (ALIAS) G::sync();
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float* row = hid + (rg * 8 + i) * s.hid_stride;
@@ -278,12 +289,12 @@ __device__ __forceinline__ float lane_of(const float4& v, int k) {
 // load serves R rows.  Group g holds rows g + i M / R (i < R), so the rows a
 // warp reads at one h fall in distinct shared-memory banks.  Outputs past O
 // are computed on a valid row, not stored.
-template <int R, int NOUT>
+template <int R, int NOUT, class G = BlockGroup>
 __device__ __forceinline__ void mlp_layer2_rows(const MlpShape& s, const float* __restrict__ b2,
                                                 const float* hid, const float* w2s, float* outs,
                                                 int u0) {
   const int tpg = R * s.tpr;
-  const int t = threadIdx.x;
+  const int t = G::tid();
   const int rg = t / tpg;
   const int j = t - rg * tpg;
   const int ngroups = s.M / R;
@@ -339,7 +350,7 @@ __device__ __forceinline__ void mlp_layer2_rows(const MlpShape& s, const float* 
 
 // Outputs per thread per pass over the hidden rows (bounds the products'
 // registers: R * NOUT * 4 of them).
-template <int R>
+template <int R, class G = BlockGroup>
 __device__ __forceinline__ void mlp_layer2_r(const MlpShape& s, const float* __restrict__ b2,
                                              const float* hid, const float* w2s, float* outs) {
   constexpr int kChunk = R == 2 ? 8 : 4;
@@ -348,7 +359,7 @@ __device__ __forceinline__ void mlp_layer2_r(const MlpShape& s, const float* __r
     switch (min(kChunk, per_thread - u0)) {
 #define NPA_L2(N)                                                  \
   case N:                                                          \
-    if constexpr (N <= kChunk) mlp_layer2_rows<R, N>(s, b2, hid, w2s, outs, u0); \
+    if constexpr (N <= kChunk) mlp_layer2_rows<R, N, G>(s, b2, hid, w2s, outs, u0); \
     break;
       NPA_L2(1) NPA_L2(2) NPA_L2(3) NPA_L2(4) NPA_L2(5) NPA_L2(6) NPA_L2(7) NPA_L2(8)
 #undef NPA_L2
@@ -358,12 +369,13 @@ __device__ __forceinline__ void mlp_layer2_r(const MlpShape& s, const float* __r
   }
 }
 
+template <class G = BlockGroup>
 __device__ __forceinline__ void mlp_layer2_any(const MlpShape& s, const float* __restrict__ b2,
                                                const float* hid, const float* w2s, float* outs) {
   if (s.l2_rows == 3)
-    mlp_layer2_r<3>(s, b2, hid, w2s, outs);
+    mlp_layer2_r<3, G>(s, b2, hid, w2s, outs);
   else
-    mlp_layer2_r<2>(s, b2, hid, w2s, outs);
+    mlp_layer2_r<2, G>(s, b2, hid, w2s, outs);
 }
 
 // API MLP: rows of the caller's row-major feature matrix.
@@ -474,18 +486,20 @@ constexpr int kStateRegs = 8;
 // the barrier after layer 1 (so a thread may start layer 1 while others
 // finish the previous tile's epilogue); false for any thread -> the tile is
 // abandoned and mlp_tile returns false.
-template <int HG, int NT, bool ALIAS, class AfterLayer2>
+template <int HG, int NT, bool ALIAS, class AfterLayer2, class G = BlockGroup,
+          class AfterLayer1 = void (*)()>
 __device__ __forceinline__ bool mlp_tile(bool arrived,
     const MlpShape& s, const GridParams& g, const SortedGrid& sg, uint32_t total, uint32_t tile,
     const float (&bias1)[kTH], const float* __restrict__ w1t, const float* __restrict__ b2,
     const StepParams& sp, const EulerParams& ep, const float* __restrict__ mask,
     float4* __restrict__ next_pos, float* __restrict__ next_states, float4* __restrict__ dx_out,
     float* __restrict__ ds_out, float* __restrict__ features_out, uint32_t step_index, float* ft,
-    float* w1s, float* hid, float* w2s, float* outs, AfterLayer2&& after_layer2) {
+    float* w1s, float* hid, float* w2s, float* outs, AfterLayer2&& after_layer2,
+    AfterLayer1 after_layer1 = nullptr) {
   constexpr int TPR = HG / 8;  // layer-2 / epilogue threads per row (NT / M)
   const int C = sp.C, D = sp.D;
-  const int r = threadIdx.x / TPR;
-  const int part = threadIdx.x - r * TPR;
+  const int r = G::tid() / TPR;
+  const int part = G::tid() - r * TPR;
   // Each of a row's TPR threads owns a contiguous run of cpt channels, read
   // and written as float4 when the rows are 16-byte aligned.
   const int cpt = (C + TPR - 1) / TPR;
@@ -514,8 +528,9 @@ __device__ __forceinline__ bool mlp_tile(bool arrived,
   }
   if (features_out && live)
     for (int f = part; f < s.F; f += TPR) features_out[row * s.F + f] = ft[f * s.M + r];
-  mlp_layer1<HG, NT, ALIAS>(s, w1t, bias1, ft, w1s, hid);
-  if (__syncthreads_or(!arrived)) return false;
+  mlp_layer1<HG, NT, ALIAS, G>(s, w1t, bias1, ft, w1s, hid);
+  if (G::sync_or(!arrived)) return false;
+  if constexpr (!std::is_pointer<AfterLayer1>::value) after_layer1();
   // own state for the Euler update, hidden behind layer 2
   float sv[kStateRegs];
   if (vec) {
@@ -540,8 +555,8 @@ __device__ __forceinline__ bool mlp_tile(bool arrived,
     liveness = __ldg(sp.states + row * C + 3);
     sd = __ldg(sp.states + row * C + 7);
   }
-  mlp_layer2_any(s, b2, hid, w2s, outs);
-  __syncthreads();
+  mlp_layer2_any<G>(s, b2, hid, w2s, outs);
+  G::sync();
   after_layer2();
   // forward_from_features_with_eps + gates + euler_step, TPR threads per row
   if (live) {
@@ -647,6 +662,7 @@ mlp_step_kernel(MlpShape s, GridParams g, SortedGrid sg, uint32_t total, uint32_
   float bias1[kTH];
   load_bias1<HG>(s, b1, bias1);
   const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
+  __syncthreads();  // the weights in shared memory are complete before any layer 1
   // No barrier at the top of a tile: a thread waits for the tile's copy on
   // the mbarrier itself and goes on into layer 1 while slower threads finish
   // the previous tile's epilogue (which reads neither ft nor hid); the block's
