@@ -526,8 +526,8 @@ def run_ours(args, rank, world, local_rank):
                                                    w.weights.b2), device=local_rank)
         ex = ba.CudaAutomataExecutor(model, w.grid, w.batch, w.n)
         ex.create_state(w.positions, w.states)
-        if args.fused:
-            ex.set_fused_step(True)
+        if args.fused or args.ws:
+            ex.set_fused_step(2 if args.ws else True)
         if args.groups:
             ex.set_step_groups(args.groups)
         step_groups = ex.step_groups
@@ -639,8 +639,9 @@ def run_ours(args, rank, world, local_rank):
             sbytes = perception_step_bytes(w, features)
             names = ["hashgrid", "density", "perception"]
         else:
-            if args.fused:
-                kernel, kbytes = "fused_step_kernel", fused_kernel_bytes(w.model)
+            if args.fused or args.ws:
+                kernel = "ws_step_kernel" if args.ws else "fused_step_kernel"
+                kbytes = fused_kernel_bytes(w.model)
             else:
                 kernel, kbytes = "mlp_step_kernel", mlp_kernel_bytes(w.model)
             sbytes = step_bytes(w)
@@ -670,7 +671,9 @@ def run_ours(args, rank, world, local_rank):
                        "state_dims": w.state_dims, "features": features,
                        "eps": w.grid.eps, "grid": list(w.grid.grid_size[:w.grid.dim]),
                        "parallelism": parallelism,
-                       "step_kernels": ("fused perception + MLP + Euler" if args.fused
+                       "step_kernels": ("warp-specialised fused perception + MLP + Euler"
+                                        if args.ws else
+                                        "fused perception + MLP + Euler" if args.fused
                                         else "perception tiles, then MLP + Euler"),
                        "step_groups": step_groups,
                        "l2": ("no flush: per-step working set exceeds the 126 MB L2"
@@ -775,6 +778,9 @@ def main():
     ap.add_argument("--fused", action="store_true",
                     help="executor step as one perception + MLP + Euler kernel after the density "
                          "pass (2D, sparse cells)")
+    ap.add_argument("--ws", action="store_true",
+                    help="executor step as the warp-specialised fused kernel (perception and MLP "
+                         "warps in one block per SM)")
     ap.add_argument("--groups", type=int, default=None,
                     help="replay the shard's rollouts as this many independent chains (1-4; "
                          "default: the executor's choice)")

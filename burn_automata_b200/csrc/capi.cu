@@ -531,7 +531,7 @@ npa_status npa_last_error_detail(npa_error_detail* out) {
 
 uint64_t npa_kernel_launch_count(void) { return g_launches.load(); }
 
-uint64_t npa_bulk_copy_timeouts(void) { return bulk_copy_timeouts(); }
+uint64_t npa_bulk_copy_timeouts(void) { return bulk_copy_timeouts() + ws_step_timeouts(); }
 
 npa_status npa_prepare_host_tables(int64_t* ln_1p_exceptions) {
   NPA_TRY(prepare_host_log1p());
@@ -871,12 +871,14 @@ static std::vector<uint64_t> g_bulk_timeouts_seen;
 static npa_status check_bulk_copies() {
   int dev = 0;
   NPA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  const uint64_t now = bulk_copy_timeouts();
+  const uint64_t now = bulk_copy_timeouts() + ws_step_timeouts();
   std::lock_guard<std::mutex> lock(g_bulk_mu);
   if (dev >= int(g_bulk_timeouts_seen.size())) g_bulk_timeouts_seen.resize(dev + 1, 0);
   if (now <= g_bulk_timeouts_seen[dev]) return NPA_OK;
   g_bulk_timeouts_seen[dev] = now;
-  return fail(NPA_ERR_TIMEOUT, "an MLP feature-tile copy did not complete within its bounded wait");
+  return fail(NPA_ERR_TIMEOUT,
+              "a bounded wait of the step kernels (an MLP feature-tile copy or a feature-tile "
+              "hand-over) gave up");
 }
 
 // Reserves `bytes` of the model's host-call arena (caller holds m->mu).
@@ -1399,7 +1401,10 @@ npa_status exec_enqueue_view_phase(npa_executor* e, const ExecView& v, int from,
         sm.lane_seeds = e->d_lane_seeds + v.first;
         sm.step_counter = v.d_step;
       }
-      if (e->fused)
+      if (e->fused == 2)
+        NPA_TRY(launch_ws_step(e->model->dm, e->g, e->p, sv, v.w->hits, B, st, v.w->volume, dt,
+                               nullptr, sm, out, s));
+      else if (e->fused)
         NPA_TRY(launch_fused_step(e->model->dm, e->g, e->p, sv, v.w->hits, B, st, v.w->volume,
                                   dt, nullptr, sm, out, s));
       else
@@ -1830,17 +1835,22 @@ npa_status npa_executor_step_groups(npa_executor* e, int32_t* groups) {
 
 npa_status npa_executor_set_fused_step(npa_executor* e, int32_t fused) {
   if (!e) return fail(NPA_ERR_INVALID_ARGUMENT, "null executor");
+  if (fused < 0 || fused > 2) return fail(NPA_ERR_INVALID_ARGUMENT, "fused must be 0, 1 or 2");
   const uint32_t B = uint32_t(e->batch), N = uint32_t(e->n);
-  if (fused && !fused_step_supported(e->model->dm, e->g, e->p, B, B * N))
+  if (fused == 1 && !fused_step_supported(e->model->dm, e->g, e->p, B, B * N))
     return fail(NPA_ERR_UNSUPPORTED,
                 "the fused step covers 2D models with more than 4 channels, hidden width up to "
                 "128 and sparse cells");
-  if ((fused != 0) != (e->fused != 0)) {
+  if (fused == 2 && !ws_step_supported(e->model->dm, e->g, e->p, B, B * N))
+    return fail(NPA_ERR_UNSUPPORTED,
+                "the warp-specialised fused step covers 2D models with at most 16 channels, "
+                "hidden width 128 and sparse cells");
+  if (fused != e->fused) {
     NPA_TRY(ensure_device(e->model->dm.device));
     exec_drop_graphs(e);
     for (auto& l : e->launches) l = 0;
   }
-  e->fused = fused != 0;
+  e->fused = fused;
   return NPA_OK;
 }
 

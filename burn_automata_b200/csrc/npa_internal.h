@@ -189,6 +189,20 @@ npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const Pe
                              const float* mask, const StochasticMask& sm, const StepOutputs& out,
                              cudaStream_t stream);
 
+// The warp-specialised step (perception producer warps and MLP consumer warps
+// in one 512-thread block per SM, feature tiles handed over in shared
+// memory): 2D models with at most 16 channels, hidden width 128, sparse
+// cells; the same results as the split kernels.
+bool ws_step_supported(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                       uint32_t batch, uint32_t total);
+npa_status launch_ws_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                          const SortedGrid& s, const HitLists& hl, uint32_t batch,
+                          const float* states, const float* volume_sorted, float dt,
+                          const float* mask, const StochasticMask& sm, const StepOutputs& out,
+                          cudaStream_t stream);
+// Bounded waits of the warp-specialised step that gave up (device counter).
+uint64_t ws_step_timeouts();
+
 // ---- training rollout backward (train.cu) ----
 // out[r][O] = adjoint of row r's raw update (target2d.rs:3566-3604): the masked
 // position adjoint through raw_motion_adjoint, the displacement regularizer

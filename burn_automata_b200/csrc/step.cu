@@ -757,6 +757,186 @@ fused_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, 
   }
 }
 
+// ---- the warp-specialised step ----
+// One 512-thread block per SM: warps 0-7 (producers, 80 registers) compute
+// the perception of a tile of 128 sorted slots (one thread per slot and
+// 8-channel chunk) into one of two shared feature buffers; warps 8-15
+// (consumers, 176 registers) run the MLP tile on the other buffer.  The
+// buffers hand over on mbarriers (full: 256 producer arrivals; empty: one
+// consumer arrival once layer 1 has read the buffer), so the producers'
+// neighbour gathers overlap the consumers' FP32 work on the same SM, and
+// each role has the register budget its code needs (setmaxnreg: 256 x 80 +
+// 256 x 176 = the block's 512 x 128).  Every wait is bounded; a wait that
+// gives up sets the block's abort flag, which every other wait also checks,
+// and counts in g_ws_timeouts.
+constexpr int kWsThreads = 512;
+constexpr int kWsProducers = 256;
+constexpr int kWsConsumers = 256;
+__device__ unsigned long long g_ws_timeouts = 0;
+
+struct ConsumerGroup {
+  static __device__ __forceinline__ int tid() { return int(threadIdx.x) - kWsProducers; }
+  static __device__ __forceinline__ int size() { return kWsConsumers; }
+  static __device__ __forceinline__ void sync() {
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kWsConsumers) : "memory");
+  }
+  static __device__ __forceinline__ bool sync_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, 1, %2, a;\n"
+        " selp.u32 %0, 1, 0, b;\n}\n"
+        : "=r"(r)
+        : "r"(uint32_t(p)), "n"(kWsConsumers)
+        : "memory");
+    return r != 0;
+  }
+};
+
+__device__ __forceinline__ void mbar_init_count(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// Waits for phase `parity` for at most about two seconds, giving up early
+// when the block's abort flag is set; false (flag set) when it gave up.
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (*abort_flag) return false;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    if (t - t0 > 2000000000ull) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+struct WsLayout {
+  size_t ft, hid, w1, w2, outs, bar, total;  // offsets in floats
+};
+__host__ __device__ inline WsLayout ws_layout(const MlpShape& s) {
+  WsLayout l;
+  size_t off = 0;
+  auto take = [&](size_t floats) {
+    size_t o = off;
+    off += (floats + 3) & ~size_t(3);
+    return o;
+  };
+  l.ft = take(2 * size_t(s.F) * s.M);
+  l.hid = take(size_t(s.M) * s.hid_stride);
+  l.w1 = take(size_t(s.F) * s.Hp);
+  l.w2 = take(size_t(s.O) * s.w2_stride);
+  l.outs = take(size_t(s.M) * s.out_stride);
+  l.bar = take(12);  // full[2], empty[2] (8 bytes each), the abort flag
+  l.total = off;
+  return l;
+}
+
+template <int HG, int CH, int OPT>
+__global__ void __launch_bounds__(kWsThreads, 1)
+ws_step_kernel(MlpShape s, GridParams g, PerceptionParams pp, SortedGrid sg, HitLists hl,
+               const float* __restrict__ volume, int chunks, uint32_t total, uint32_t ntiles,
+               const float* __restrict__ w1t, const float* __restrict__ b1,
+               const float* __restrict__ w2, const float* __restrict__ b2, StepParams sp,
+               EulerParams ep, const float* __restrict__ mask, float4* __restrict__ next_pos,
+               float* __restrict__ next_states) {
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  const WsLayout L = ws_layout(s);
+  float* ft0 = smem + L.ft;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar);
+  uint64_t* empty = full + 2;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 4);
+  if (threadIdx.x == 0) {
+    mbar_init_count(&full[0], kWsProducers);
+    mbar_init_count(&full[1], kWsProducers);
+    mbar_init_count(&empty[0], 1);
+    mbar_init_count(&empty[1], 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  const size_t FM = size_t(s.F) * s.M;
+  if (threadIdx.x < kWsProducers) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 80;\n" ::: "memory");
+    const int C = sp.C;
+    const int rr = int(threadIdx.x) / chunks;  // this thread's row of every tile
+    const int chunk = int(threadIdx.x) - rr * chunks;
+    const int c0 = chunk * CH;
+    uint32_t k = 0;
+    for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+      const uint32_t b = k & 1u, use = k >> 1;
+      if (use > 0 && !ws_wait(&empty[b], (use - 1u) & 1u, abort_flag)) break;
+      float* col = ft0 + b * FM + rr;
+      const uint32_t t = tile * s.M + rr;  // processing index
+      if (rr >= s.M) {
+        // no row (one chunk per particle: threads past the tile's rows)
+      } else if (t >= total) {
+        for (int f = chunk; f < s.F; f += chunks) col[size_t(f) * s.M] = 0.0f;
+      } else {
+        const uint32_t q = slot_of(sg, t);
+        const uint32_t batch = q / sg.n;
+        const size_t row = size_t(batch) * sg.n + sg.permutation[q];
+        const float4 pi = __ldg(sg.positions + row);
+        const int3 c = slot_cell<2>(sg, q);
+        float si[CH];
+        load_row<CH>(sp.states, row, C, c0, false, si);
+        PerceptionAcc<2, CH> a;
+        perceive_chunk<2, CH, OPT>(g, pp, sg, hl, batch, q, t, pi, c, sp.states, C, c0, volume,
+                                   si, a);
+        emit_features<2, CH>(pp, C, c0, chunk == 0, si, a, pi,
+                             [&](int f, float v) { col[size_t(f) * s.M] = v; });
+      }
+      mbar_arrive(&full[b]);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 176;\n" ::: "memory");
+    float* hid = smem + L.hid;
+    float* w1s = smem + L.w1;
+    float* w2s = smem + L.w2;
+    float* outs = smem + L.outs;
+    load_weights<ConsumerGroup>(s, w1t, w2, w1s, w2s);
+    float bias1[kTH];
+    load_bias1<HG, ConsumerGroup>(s, b1, bias1);
+    const uint32_t step_index = sp.lane_seeds ? __ldg(sp.step_counter) : 0u;
+    ConsumerGroup::sync();  // the weights are complete before any layer 1
+    uint32_t k = 0;
+    for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+      const uint32_t b = k & 1u, use = k >> 1;
+      const bool arrived = ws_wait(&full[b], use & 1u, abort_flag);
+      auto nothing = [] {};
+      auto release = [&] {
+        // layer 1 is done with the buffer: the producers may refill it
+        if (ConsumerGroup::tid() == 0) mbar_arrive(&empty[b]);
+      };
+      const bool ok =
+          mlp_tile<HG, kWsConsumers, false, decltype(nothing)&, ConsumerGroup, decltype(release)>(
+              arrived, s, g, sg, total, tile, bias1, w1t, b2, sp, ep, mask, next_pos,
+              next_states, nullptr, nullptr, nullptr, step_index, ft0 + b * FM, w1s, hid, w2s,
+              outs, nothing, release);
+      if (!ok) {
+        if (ConsumerGroup::tid() == 0) {
+          *abort_flag = 1;
+          atomicAdd(&g_ws_timeouts, 1ull);
+        }
+        break;
+      }
+    }
+  }
+}
+
 MlpShape shape_with(const DeviceModel& m, int nt) {
   MlpShape s;
   s.NT = nt;
@@ -1058,6 +1238,66 @@ npa_status launch_fused_step(const DeviceModel& m, const GridParams& g, const Pe
   }
 #undef NPA_FUSED
   return after_launch("fused_step_kernel");
+}
+
+bool ws_step_supported(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                       uint32_t batch, uint32_t total) {
+  if (g.dim != 2 || m.state_dims < 1 || m.state_dims > 16 || !mlp_step_supported(m)) return false;
+  if (m.hidden_padded != 128 || p.feature_dims != m.feature_dims) return false;
+  if (uint64_t(total) >= uint64_t(8) * batch * g.cells) return false;  // dense cells
+  const MlpShape s = shape_with(m, kWsConsumers);
+  return s.M == 128 && (m.update_dims + s.tpr - 1) / s.tpr <= kMaxOut &&
+         ws_layout(s).total * sizeof(float) <= kSmemBudget;
+}
+
+npa_status launch_ws_step(const DeviceModel& m, const GridParams& g, const PerceptionParams& p,
+                          const SortedGrid& sgrid, const HitLists& hl, uint32_t batch,
+                          const float* states, const float* volume_sorted, float dt,
+                          const float* mask, const StochasticMask& sm, const StepOutputs& out,
+                          cudaStream_t stream) {
+  const uint32_t total = batch * sgrid.n;
+  if (total == 0) return NPA_OK;
+  if (!ws_step_supported(m, g, p, batch, total))
+    return fail(NPA_ERR_UNSUPPORTED, "warp-specialised step outside the supported range");
+  PerceptionParams pp = p;
+  pp.vec_states = (reinterpret_cast<uintptr_t>(states) % 16) == 0;
+  if (p.log_norm_grad || p.log_norm_density_grad) NPA_TRY(device_log1p_table(&pp.l1p, stream));
+  MlpShape s = shape_with(m, kWsConsumers);
+  s.w1_resident = 1;
+  const StepParams sp = step_params(m, g, states, sm);
+  const EulerParams e{dt, 2, 0};
+  const int ch = m.state_dims <= 4 ? 4 : 8;
+  const int chunks = (m.state_dims + ch - 1) / ch;
+  const uint32_t ntiles = static_cast<uint32_t>((uint64_t(total) + s.M - 1) / s.M);
+  const bool fixed_opts = p.state_grad && !p.density_grad && p.hybrid;
+  const size_t smem = ws_layout(s).total * sizeof(float);
+  int per_sm = 0, sms = 0;
+#define NPA_WS(CHV, OPTV)                                                                      \
+  do {                                                                                         \
+    NPA_TRY(kernel_occupancy(reinterpret_cast<const void*>(ws_step_kernel<16, CHV, OPTV>),     \
+                             kWsThreads, smem, &per_sm, &sms));                                \
+    if (per_sm < 1) return fail(NPA_ERR_UNSUPPORTED, "warp-specialised step cannot be resident"); \
+    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>(ntiles, uint64_t(sms))); \
+    ws_step_kernel<16, CHV, OPTV><<<grid, kWsThreads, smem, stream>>>(                         \
+        s, g, pp, sgrid, hl, volume_sorted, chunks, total, ntiles, m.w1t, m.b1, m.w2, m.b2,     \
+        sp, e, mask, out.next_positions, out.next_states);                                     \
+  } while (0)
+  if (ch == 4) {
+    if (fixed_opts) NPA_WS(4, 1); else NPA_WS(4, 0);
+  } else {
+    if (fixed_opts) NPA_WS(8, 1); else NPA_WS(8, 0);
+  }
+#undef NPA_WS
+  return after_launch("ws_step_kernel");
+}
+
+uint64_t ws_step_timeouts() {
+  unsigned long long v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_ws_timeouts, sizeof(v)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return v;
 }
 
 }  // namespace npa

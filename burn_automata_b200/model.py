@@ -362,11 +362,13 @@ class CudaAutomataExecutor:
                                                         ctypes.byref(s)), "state_device")
         return p.value, s.value
 
-    def set_fused_step(self, fused: bool = True) -> None:
+    def set_fused_step(self, fused=True) -> None:
         """Run perception, the MLP and the Euler step as one kernel per step
-        (feature rows kept in shared memory) instead of two; same results."""
-        _lib.check(_lib.lib().npa_executor_set_fused_step(self._handle, int(bool(fused))),
-                   "set_fused_step")
+        (feature rows kept in shared memory) instead of two; same results.
+        fused = 2 selects the warp-specialised form (perception warps and
+        MLP warps in one block per SM)."""
+        mode = 2 if fused == 2 else int(bool(fused))
+        _lib.check(_lib.lib().npa_executor_set_fused_step(self._handle, mode), "set_fused_step")
 
     def set_step_groups(self, groups: int) -> None:
         """Replay the batch as `groups` independent chains of rollouts (1..4),

@@ -155,9 +155,10 @@ const char* npa_last_error_message(void);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t npa_kernel_launch_count(void);
 
-/* Diagnostic: feature-tile bulk copies of the MLP step kernel that did not
- * complete within their bounded wait on the current device (0 in a healthy
- * run; a block that gives up leaves its remaining tiles undone).  The
+/* Diagnostic: feature-tile bulk copies of the MLP step kernel, and feature-tile
+ * hand-overs of the warp-specialised step, that did not complete within their
+ * bounded wait on the current device (0 in a healthy run; a block that gives
+ * up leaves its remaining tiles undone).  The
  * synchronising host calls (npa_model_step, npa_model_run_rollout*,
  * npa_executor_read_state) return NPA_ERR_TIMEOUT when this device's count
  * has grown since the last such check on the device. */
@@ -575,10 +576,14 @@ npa_status npa_executor_launches_per_step(npa_executor* exec, int64_t* launches)
 /* Selects the executor's step kernels: fused = 1 runs perception, the MLP
  * and the Euler step as one kernel after the density pass (the feature rows
  * stay in shared memory, the role of the reference's single update pass,
- * crates/burn_automata/src/gpu_step.wgsl:3656-4484); fused = 0 (the default)
- * runs perception into feature tiles and the MLP stage as two kernels.  Both
- * give identical results.  NPA_ERR_UNSUPPORTED outside the fused kernel's
- * range (2D, C > 4, hidden width <= 128, sparse cells). */
+ * crates/burn_automata/src/gpu_step.wgsl:3656-4484), two blocks per SM each
+ * alternating perception and MLP; fused = 2 is the warp-specialised form
+ * (perception warps and MLP warps of one block per SM handing feature tiles
+ * over in shared memory); fused = 0 (the default) runs perception into
+ * feature tiles and the MLP stage as two kernels.  All give identical
+ * results.  NPA_ERR_UNSUPPORTED outside a fused kernel's range (2D, sparse
+ * cells; fused = 1: C > 4, hidden width <= 128; fused = 2: C <= 16, hidden
+ * width 128). */
 npa_status npa_executor_set_fused_step(npa_executor* exec, int32_t fused);
 
 /* Splits the batch into `groups` (1..min(4, batch)) runs of consecutive

@@ -28,7 +28,7 @@ def run(w, steps, fused, prob=1.0, seed=0):
     ex = ba.CudaAutomataExecutor(m, w.grid, w.batch, w.n)
     ex.create_state(w.positions, w.states, update_prob=prob, seed=seed)
     if fused:
-        ex.set_fused_step(True)
+        ex.set_fused_step(fused)
     s = torch.cuda.Stream()
     ex.step_state_many(steps, w.dt, use_graph=True, stream=s.cuda_stream)
     out = ex.read_state()
@@ -132,3 +132,25 @@ def test_step_groups_range():
     ex.set_step_groups(1)
     ex.close()
     m.close()
+
+
+WS_CASES = [("cfg2", 8, 4096, 1.0, 12), ("cfg0", 1, 4096, 0.5, 8), ("cfg0", 1, 3001, 1.0, 6)]
+
+
+@pytest.mark.parametrize("name,batch,n,prob,steps", WS_CASES,
+                         ids=[f"{c[0]}x{c[1]}_n{c[2]}_p{c[3]}" for c in WS_CASES])
+def test_warp_specialised_step_equals_split(name, batch, n, prob, steps):
+    """The warp-specialised fused step (perception warps and MLP warps of one
+    block handing feature tiles over in shared memory) gives the split
+    kernels' bits, and its bounded waits all complete."""
+    import burn_automata_b200 as ba
+
+    lib = ba.load_library()
+    before = lib.npa_bulk_copy_timeouts()
+    w = workloads.make(name, batch=batch, n=n)
+    (fp, fs), lf = run(w, steps, 2, prob, 7)
+    (sp, ss), ls = run(w, steps, False, prob, 7)
+    np.testing.assert_array_equal(fs, ss)
+    np.testing.assert_array_equal(fp, sp)
+    assert lf == ls - 1
+    assert lib.npa_bulk_copy_timeouts() == before
