@@ -75,7 +75,7 @@ WORKLOADS = {
 #   profiles/mlp_step_kernel_cfg2.txt: 356.9 MB + 68.6 MB for 1,048,576 rows;
 #   profiles/perception_kernel_cfg1.txt: 1306.5 MB + 620.9 MB for 1,048,576 particles.
 NCU_TRAFFIC_PER_PARTICLE = {
-    ("cfg2", "mlp_step_kernel"): (356.706560e6 + 68.559104e6) / 1048576,
+    ("cfg2", "mlp_step_kernel"): (356.652288e6 + 71.074048e6) / 1048576,
     ("cfg1", "perception_kernel"): (1306.484736e6 + 620.867840e6) / 1048576,
 }
 NCU_TRAFFIC_SOURCE = {
