@@ -230,8 +230,8 @@ def make_model(w):
     return NpaModel(w.model, NpaWeights(w.weights.w1, w.weights.b1, w.weights.w2, w.weights.b2))
 
 
-# cfg2 x 72 (294,912 rows: 11 waves of 192-row tiles beat 16 of 128-row ones)
-# runs the 384-thread MLP tiles, the others the 256-thread ones.
+# cfg0 / cfg2 (hidden width 128) run the step's MLP as two 192-thread blocks
+# per SM (96-row tiles); cfg3 (hidden width 256) keeps one block per SM.
 @pytest.mark.parametrize("name,batch,n", [("cfg0", 1, 4096), ("cfg2", 4, 4096), ("cfg2", 72, 4096),
                                           ("cfg3", 1, 4096)])
 def test_step_parity(oracle_mod, name, batch, n):
@@ -258,6 +258,25 @@ def test_step_bit_exact_without_log_norm(oracle_mod, batch):
     gpu = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt, mask)
     ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, w.dt,
                           mask)
+    for key in ("features", "ds", "dx", "next_states", "next_positions", "density"):
+        np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
+
+
+@pytest.mark.parametrize("hidden", [3, 64, 100])
+def test_step_mlp_shapes_bit_exact(oracle_mod, hidden):
+    """The step's MLP stage at other hidden widths: 64 (a 192-row tile, one
+    layer-2 / epilogue thread per row), 3 (the same shape, most hidden units
+    padding) and 100 (padded to 128); three 1,000-particle rollouts, so the
+    last tile is partly empty."""
+    w = workloads.make("cfg2", batch=3, n=1000, steps=1)
+    w.model = w.model.with_(log_norm_grad=False, log_norm_density_grad=False, hidden_dims=hidden)
+    kw = workloads.kaiming_weights(w.model, hidden)
+    rng = np.random.default_rng(hidden)
+    w.weights = type(kw)(kw.w1, (rng.standard_normal(hidden) * 0.1).astype(np.float32), kw.w2,
+                         (rng.standard_normal(w.model.update_dims()) * 0.01).astype(np.float32))
+    m = make_model(w)
+    gpu = m.step(w.positions, w.states, w.batch, w.n, w.grid, w.dt)
+    ref = oracle_mod.step(w.model, w.weights, w.grid, w.positions, w.states, w.batch, w.n, w.dt)
     for key in ("features", "ds", "dx", "next_states", "next_positions", "density"):
         np.testing.assert_array_equal(getattr(gpu, key), ref[key], err_msg=key)
 
