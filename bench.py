@@ -72,7 +72,7 @@ WORKLOADS = {
 
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu captures, per particle of that launch:
-#   profiles/mlp_step_kernel_cfg2.txt: 356.9 MB + 68.6 MB for 1,048,576 rows;
+#   profiles/mlp_step_kernel_cfg2.txt: 356.7 MB + 71.1 MB for 1,048,576 rows;
 #   profiles/perception_kernel_cfg1.txt: 1306.5 MB + 620.9 MB for 1,048,576 particles.
 NCU_TRAFFIC_PER_PARTICLE = {
     ("cfg2", "mlp_step_kernel"): (356.652288e6 + 71.074048e6) / 1048576,
