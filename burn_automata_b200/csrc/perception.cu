@@ -162,7 +162,7 @@ perception_tiles_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH, OPT>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a,
+  perceive_chunk<DIM, CH, OPT, true>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a,
                                win, peers);
   emit_features<DIM, CH>(p, C, c0, chunk == 0, si, a, pi,
                          [&](int k, float v) { tile[size_t(k) * tile_rows] = v; });
