@@ -77,7 +77,7 @@ __device__ __forceinline__ void load_own(const float* __restrict__ states, size_
   for (int c = 0; c < CH; ++c) si[c] = (c0 + c < C) ? __ldg(states + row * C + c0 + c) : 0.0f;
 }
 
-template <int DIM, int CH, bool COOP>
+template <int DIM, int CH, bool COOP, int OPT = 0>
 __global__ void __launch_bounds__(128, PerceptionBlocks<DIM>::value)
 perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, uint32_t total,
                   const float* __restrict__ states, int C, int chunks,
@@ -105,7 +105,7 @@ perception_kernel(GridParams g, PerceptionParams p, SortedGrid s, HitLists hl, u
   float si[CH];
   load_own<CH>(states, row, C, c0, si);
   PerceptionAcc<DIM, CH> a;
-  perceive_chunk<DIM, CH>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a, win,
+  perceive_chunk<DIM, CH, OPT>(g, p, s, hl, batch, q, pt, pi, c, states, C, c0, volume, si, a, win,
                           peers);
   const size_t F = p.feature_dims;
   float* f = features + row * F;
@@ -261,10 +261,19 @@ npa_status launch_perception(const GridParams& g, const PerceptionParams& p, con
   const int ch = chunk_channels(state_dims);
   const int chunks = state_dims > 0 ? (state_dims + ch - 1) / ch : 1;
   const unsigned blocks = grid_for(uint64_t(total) * chunks, 128);
+  // the full growing_2d option set compiled in (2D): cfg1's perception
+  const bool full_opts = p.state_grad && p.density_grad && p.hybrid;
 #define NPA_PERC(D, CHV, CO)                                                                  \
-  perception_kernel<D, CHV, CO><<<blocks, 128, 0, stream>>>(                                  \
-      g, pp, s, hl, total, states, state_dims, chunks, volume_sorted, features, blurred,      \
-      state_gradient, density_gradient)
+  do {                                                                                        \
+    if (D == 2 && full_opts)                                                                  \
+      perception_kernel<D, CHV, CO, (D == 2 ? 2 : 0)><<<blocks, 128, 0, stream>>>(            \
+          g, pp, s, hl, total, states, state_dims, chunks, volume_sorted, features, blurred,  \
+          state_gradient, density_gradient);                                                  \
+    else                                                                                      \
+      perception_kernel<D, CHV, CO><<<blocks, 128, 0, stream>>>(                              \
+          g, pp, s, hl, total, states, state_dims, chunks, volume_sorted, features, blurred,  \
+          state_gradient, density_gradient);                                                  \
+  } while (0)
 #define NPA_PERC_CH(D, CO)                                   \
   do {                                                       \
     if (ch == 4) NPA_PERC(D, 4, CO); else NPA_PERC(D, 8, CO); \

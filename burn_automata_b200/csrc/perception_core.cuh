@@ -102,14 +102,16 @@ __device__ __forceinline__ void load_row(const float* __restrict__ states, size_
 // One neighbour's terms (second_pass_particle, forward.rs:249-295, or the
 // separate passes of the other branch), added in the reference's order.
 // OPT = 1 fixes the rollout models' options at compile time (state gradient
-// and hybrid moment on, density gradient off; p must hold the same), which
+// and hybrid moment on, density gradient off; p must hold the same), OPT = 2
+// the full growing_2d set (state and density gradients, hybrid moment), which
 // drops the per-pair option branches; OPT = 0 reads them from p.
 template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionParams& p,
                                           bool self, float4 d, float r2, float vol,
                                           const float (&sjv)[CH], const float (&si)[CH],
                                           ChunkState<DIM, CH>& st) {
-  const bool sg = OPT ? true : p.state_grad, dg = OPT ? false : p.density_grad;
+  const bool sg = OPT ? true : p.state_grad;
+  const bool dg = OPT == 2 ? true : (OPT ? false : p.density_grad);
   const bool hy = OPT ? true : p.hybrid;
   const float smooth = poly6(g, r2);
   if (sg && dg) {
@@ -151,7 +153,8 @@ __device__ __forceinline__ void chunk_add(const GridParams& g, const PerceptionP
 // Moment correction (normalize.rs:93-118) and gradient normalisation (:5-58).
 template <int DIM, int CH, int OPT = 0>
 __device__ __forceinline__ void chunk_finish(const PerceptionParams& p, ChunkState<DIM, CH>& st) {
-  const bool sg = OPT ? true : p.state_grad, dg = OPT ? false : p.density_grad;
+  const bool sg = OPT ? true : p.state_grad;
+  const bool dg = OPT == 2 ? true : (OPT ? false : p.density_grad);
   const bool hy = OPT ? true : p.hybrid;
   if (sg) {
     if (hy) {
