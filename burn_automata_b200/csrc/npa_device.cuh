@@ -437,6 +437,60 @@ __device__ __forceinline__ void for_each_neighbor(const GridParams& g, const Sor
   }
 }
 
+// for_each_neighbor with one candidate in flight and the per-bin starts and
+// running counts in shared memory (`tab` is this thread's column of a
+// [2 NB][stride] table): a bin change reads two words instead of selecting
+// from register arrays, and the walk keeps 18 fewer registers live (2D
+// density: 28 instead of 40, eight 256-thread blocks per SM instead of six;
+// cfg2 density 0.134 vs 0.180 ms, cfg1 0.236 vs 0.293 ms).
+template <int DIM, class Visit>
+__device__ __forceinline__ void for_each_neighbor_tab(const GridParams& g, const SortedGrid& s,
+                                                      uint32_t batch, float4 pi, int3 center,
+                                                      uint32_t* tab, uint32_t stride,
+                                                      Visit&& visit) {
+  constexpr int NB = DIM == 3 ? 27 : 9;
+  const uint32_t bin_base = batch * g.cells;
+  uint32_t ncand = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int3 nc = add_wrapping(center, bin_delta<DIM>(b));
+    const long long cell = cell_index<DIM>(g, nc.x, nc.y, nc.z);
+    uint32_t lo = 0, cnt = 0;
+    if (cell >= 0) {
+      const uint32_t bin = bin_base + static_cast<uint32_t>(cell);
+      lo = __ldg(s.bin_offsets + bin);
+      const uint32_t hi = min(__ldg(s.bin_offsets + bin + 1), s.total);
+      cnt = hi > lo ? hi - lo : 0u;
+    }
+    tab[b * stride] = lo;
+    ncand += cnt;
+    tab[(NB + b) * stride] = ncand;
+  }
+  int b = 0;
+  uint32_t cur_beg = tab[0], cur_lo = 0, cur_hi = tab[NB * stride];
+  for (uint32_t v = 0; v < ncand; ++v) {
+    while (v >= cur_hi) {
+      ++b;
+      cur_lo = cur_hi;
+      cur_beg = tab[b * stride];
+      cur_hi = tab[(NB + b) * stride];
+    }
+    const uint32_t q = cur_beg + (v - cur_lo);
+    float4 pj;
+    int3 cj;
+    load_record<DIM>(s, q, pj, cj);
+    if (g.mode == kModeParticle) {
+      const int3 want = add_wrapping(center, bin_delta<DIM>(b));
+      if (cj.x != want.x || cj.y != want.y || cj.z != want.z) continue;
+    }
+    const float4 d = neighbor_delta<DIM>(g, pi, pj);
+    float r2 = d.x * d.x;
+    r2 = r2 + d.y * d.y;
+    if (DIM == 3) r2 = r2 + d.z * d.z;
+    if (r2 < g.eps2) visit(q, d, r2);
+  }
+}
+
 // Per-warp staging of the cooperative walk: one 32-candidate window.
 struct WarpWindow {
   float4 rec[32];     // candidate position; w = 1 when its cell is the visited cell

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(256)
 density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ volume,
                float* __restrict__ density_out, HitLists hl) {
   __shared__ WarpWindow windows[COOP ? 256 / 32 : 1];
+  // 2D, one candidate in flight: the walk's bin table, one column per thread
+  __shared__ uint32_t tab[(DIM == 2 && KB == 1) ? 18 * 256 : 1];
   // processing index t (hit lists are indexed by it), sorted slot q
   const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
   // Whole warp in range (warp-uniform), so warp collectives below are safe.
@@ -62,8 +64,12 @@ density_kernel(GridParams g, SortedGrid s, uint32_t total, float* __restrict__ v
                                 [](uint32_t, uint32_t) {},
                                 [&](uint32_t, uint32_t qj, float4, float r2) { visit(qj, r2); });
   } else {
-    for_each_neighbor<DIM, KB>(g, s, batch, pi, c,
-                              [&](uint32_t qj, float4, float r2) { visit(qj, r2); });
+    if constexpr (DIM == 2 && KB == 1)
+      for_each_neighbor_tab<DIM>(g, s, batch, pi, c, tab + threadIdx.x, 256u,
+                                 [&](uint32_t qj, float4, float r2) { visit(qj, r2); });
+    else
+      for_each_neighbor<DIM, KB>(g, s, batch, pi, c,
+                                [&](uint32_t qj, float4, float r2) { visit(qj, r2); });
   }
   if (list) hl.count[t] = min(hits, uint32_t(hl.cap + 1));
   volume[q] = recip_finite(rho);
