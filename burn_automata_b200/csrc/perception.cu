@@ -242,8 +242,11 @@ npa_status launch_density(const GridParams& g, const SortedGrid& s, uint32_t bat
     else NPA_DENS(D, CO, 4);                    \
   } while (0)
   const bool coop = dense_cells(g, batch, total);
-  // at least two waves of resident 256-thread blocks (four per SM)
-  const bool wide = total >= 2u * 148u * 4u * 256u;
+  // One candidate in flight: in 2D (bin table in shared memory) from 65,536
+  // particles (measured: 32 rollouts of 4,096 density 0.035 vs 0.039 ms, 64
+  // rollouts 0.046 vs 0.062 ms; one rollout 0.029 vs 0.026 ms the other way),
+  // in 3D from two waves of resident 256-thread blocks (four per SM).
+  const bool wide = g.dim == 2 ? total >= 65536u : total >= 2u * 148u * 4u * 256u;
   if (g.dim == 2) {
     if (coop) NPA_DENS_KB(2, true); else NPA_DENS_KB(2, false);
   } else {
