@@ -1028,7 +1028,7 @@ int hidden_padded_for(int hidden) { return hidden <= 64 ? 64 : (hidden <= 128 ? 
 // block's FP32 work.  Measured against one 384-thread block per SM (cfg2
 // MLP stage 0.884 vs 0.896 ms; 32 rollouts 0.132 vs 0.139 ms; cfg0 0.0248 vs
 // 0.0267 ms).  Hidden width 256 keeps the one-block shapes (its layer-1
-// thread grid needs 8-warp multiples).
+// thread grid needs a multiple of four warps per block; 192 threads have six).
 MlpShape make_step_shape(const DeviceModel& m, uint64_t rows) {
   if (rows > 0 && m.hidden_padded <= 128) {
     MlpShape s = shape_with(m, kTwoBlockThreads);
